@@ -1,0 +1,511 @@
+// MoE decode path: top-k router with residency bias, token/expert alignment, grouped gate|up and down GEMVs
+// (gemv.cuh), and the fixed-order combine.
+//
+// Workspace layout of exl3_moe_align / exl3_moe_decode (int32 words unless noted; P = valid pairs + shared rows):
+//   [0] n_items  [1] n_pairs_valid  [2..7] reserved
+//   item_expert[max_items] item_start[max_items] item_cnt[max_items]
+//   pair_tok[P_max] pair_of[npairs] pair_w[P_max] (fp32)
+//   then (decode only, 256-byte aligned) abuf fp16 [P_max][I], ybuf fp32 [P_max][H]
+#include "gemv.cuh"
+
+namespace exl3 {
+
+constexpr int kItemRows = 8;     // rows per GEMV work item (the MMA's N)
+
+struct WsLayout {
+    size_t item_expert, item_start, item_cnt, pair_tok, pair_of, pair_w, abuf, ybuf, total;
+    int max_items, p_max;
+};
+
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+inline WsLayout ws_layout(int M, int topk, int E, int H, int I, int shared, int chunk) {
+    WsLayout L;
+    const int npairs = M * topk;
+    const int active = npairs < E ? npairs : E;
+    L.max_items = active + (npairs + chunk - 1) / chunk + (shared ? (M + chunk - 1) / chunk : 0);
+    L.p_max = npairs + (shared ? M : 0);
+    size_t o = 8 * 4;
+    L.item_expert = o; o += (size_t)L.max_items * 4;
+    L.item_start = o; o += (size_t)L.max_items * 4;
+    L.item_cnt = o; o += (size_t)L.max_items * 4;
+    L.pair_tok = o; o += (size_t)L.p_max * 4;
+    L.pair_of = o; o += (size_t)npairs * 4;
+    L.pair_w = o; o += (size_t)L.p_max * 4;
+    o = align_up(o, 256);
+    L.abuf = o; o += align_up((size_t)L.p_max * I * 2, 256);
+    L.ybuf = o; o += (size_t)L.p_max * H * 4;
+    L.total = o;
+    return L;
+}
+
+// ------------------------------------------------------------------------------------------------ router
+
+__device__ __forceinline__ uint32_t ordered_bits(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+// Max-reduction key: higher score first, then lower expert index.
+__device__ __forceinline__ uint64_t pack_key(float key, int e) {
+    if (isnan(key)) key = -INFINITY;
+    return ((uint64_t)ordered_bits(key) << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)e);
+}
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) {
+        uint64_t o = __shfl_xor_sync(0xFFFFFFFFu, v, m);
+        v = o > v ? o : v;
+    }
+    return v;
+}
+
+constexpr int kRouteThreads = 256;
+constexpr int kRouteMaxE = 1024;
+constexpr int kRoutePer = kRouteMaxE / kRouteThreads;   // experts per thread
+constexpr int kRouteMaxK = 32;
+
+// One CTA per row. score in fp64 rounded once to fp32; selection by k argmax passes (ties -> lowest index).
+__global__ void __launch_bounds__(kRouteThreads) k_route(const float* __restrict__ logits, int ld, int E, int kind,
+                                                         int k, const float* bias, const float* res,
+                                                         const float* mul, float scale, int renorm, void* ids,
+                                                         int ids64, float* w, void* want) {
+    __shared__ float s_score[kRouteMaxE];
+    __shared__ uint64_t s_red[kRouteThreads / 32];
+    __shared__ int s_pick[kRouteMaxK];
+    __shared__ double s_dred[kRouteThreads / 32];
+    const int row = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const float* l = logits + (size_t)row * ld;
+
+    // scores
+    float lmax = -INFINITY;
+    for (int j = 0; j < kRoutePer; ++j) {
+        const int e = t + j * kRouteThreads;
+        if (e >= E) break;
+        const float v = l[e];
+        float s;
+        if (kind == EXL3_ROUTE_SIGMOID) {
+            s = (float)(1.0 / (1.0 + exp(-(double)v)));
+        } else if (kind == EXL3_ROUTE_SQRT_SOFTPLUS) {
+            const double d = (double)v;
+            s = (float)sqrt(d > 20.0 ? d : log1p(exp(d)));
+        } else {
+            s = v;
+            lmax = fmaxf(lmax, v);
+        }
+        s_score[e] = s;
+    }
+    // softmax denominator (fp64), only for the weights
+    double denom = 1.0, dmax = 0.0;
+    if (kind == EXL3_ROUTE_SOFTMAX) {
+        float m = lmax;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+        if (lane == 0) s_dred[warp] = m;
+        __syncthreads();
+        double mm = -INFINITY;
+        for (int i = 0; i < kRouteThreads / 32; ++i) mm = fmax(mm, s_dred[i]);
+        dmax = mm;
+        __syncthreads();
+        double part = 0.0;
+        for (int j = 0; j < kRoutePer; ++j) {
+            const int e = t + j * kRouteThreads;
+            if (e >= E) break;
+            part += exp((double)l[e] - dmax);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, o);
+        if (lane == 0) s_dred[warp] = part;
+        __syncthreads();
+        denom = 0.0;
+        for (int i = 0; i < kRouteThreads / 32; ++i) denom += s_dred[i];
+    }
+    __syncthreads();
+
+    for (int pass = 0; pass < 2; ++pass) {
+        if (pass == 1 && !want) break;
+        uint64_t key[kRoutePer];
+#pragma unroll
+        for (int j = 0; j < kRoutePer; ++j) {
+            const int e = t + j * kRouteThreads;
+            key[j] = 0;
+            if (e < E) {
+                float kv = s_score[e];
+                if (pass == 0 && mul) kv = kv * mul[e];
+                if (bias) kv = kv + bias[e];
+                if (pass == 0 && res) kv = kv + res[e];
+                key[j] = pack_key(kv, e);
+            }
+        }
+        for (int j = 0; j < k; ++j) {
+            uint64_t best = 0;
+#pragma unroll
+            for (int i = 0; i < kRoutePer; ++i) best = key[i] > best ? key[i] : best;
+            best = warp_max_u64(best);
+            if (lane == 0) s_red[warp] = best;
+            __syncthreads();
+            uint64_t all = 0;
+#pragma unroll
+            for (int i = 0; i < kRouteThreads / 32; ++i) all = s_red[i] > all ? s_red[i] : all;
+            const int e = (int)(0xFFFFFFFFu - (uint32_t)(all & 0xFFFFFFFFu));
+#pragma unroll
+            for (int i = 0; i < kRoutePer; ++i)
+                if (key[i] == all) key[i] = 0;
+            if (t == 0) s_pick[j] = e;
+            __syncthreads();
+        }
+        if (t == 0) {
+            if (pass == 0) {
+                // weights from the unbiased score, summed over the picks in slot order
+                float wv[kRouteMaxK];
+                float tot = 0.f;
+                for (int j = 0; j < k; ++j) {
+                    const int e = s_pick[j];
+                    wv[j] = kind == EXL3_ROUTE_SOFTMAX ? (float)(exp((double)l[e] - dmax) / denom) : s_score[e];
+                    tot += wv[j];
+                }
+                for (int j = 0; j < k; ++j) {
+                    float o;
+                    if (kind == EXL3_ROUTE_SOFTMAX) o = renorm ? wv[j] / (tot + 1e-20f) : wv[j];
+                    else o = wv[j] * scale / (tot + 1e-20f);
+                    w[(size_t)row * k + j] = o;
+                    if (ids64) static_cast<int64_t*>(ids)[(size_t)row * k + j] = s_pick[j];
+                    else static_cast<int32_t*>(ids)[(size_t)row * k + j] = s_pick[j];
+                }
+            } else {
+                for (int j = 0; j < k; ++j) {
+                    if (ids64) static_cast<int64_t*>(want)[(size_t)row * k + j] = s_pick[j];
+                    else static_cast<int32_t*>(want)[(size_t)row * k + j] = s_pick[j];
+                }
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ align
+
+constexpr int kAlignThreads = 1024;
+constexpr int kAlignWarps = kAlignThreads / 32;
+
+// Exclusive prefix sum over the CTA (one value per thread); *total receives the sum of all values.
+__device__ __forceinline__ int block_excl_scan(int v, int* scan, int* total) {
+    const int t = threadIdx.x;
+    scan[t] = v;
+    __syncthreads();
+    for (int o = 1; o < kAlignThreads; o <<= 1) {
+        const int add = t >= o ? scan[t - o] : 0;
+        __syncthreads();
+        scan[t] += add;
+        __syncthreads();
+    }
+    const int incl = scan[t];
+    *total = scan[kAlignThreads - 1];
+    __syncthreads();
+    return incl - v;
+}
+
+// One CTA. Pairs are split into 32 contiguous warp segments; per-(warp, expert) counts give every pair a stable
+// position (experts ascending, pair index ascending within an expert): deterministic, unlike an atomic fill
+// (glm/xpu/csrc/exl3_moe.n128.sycl:693-734 fills positions in atomic order). Items: ceil(count / chunk) per active
+// expert in expert order, then the shared expert's rows (expert id E, weight 1) at positions n_valid + m.
+__global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restrict__ ids, const float* __restrict__ w,
+                                                         int npairs, int topk, int E, int M, int shared, int chunk,
+                                                         int* ws_i, int* item_expert, int* item_start, int* item_cnt,
+                                                         int* pair_tok, int* pair_of, float* pair_w) {
+    extern __shared__ int sm[];
+    int* cnt = sm;                             // [kAlignWarps][E]
+    int* scan = sm + kAlignWarps * E;          // [kAlignThreads]
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    for (int i = t; i < kAlignWarps * E; i += kAlignThreads) cnt[i] = 0;
+    __syncthreads();
+    const int seg = (npairs + kAlignWarps - 1) / kAlignWarps;
+    const int a0 = min(npairs, warp * seg), a1 = min(npairs, a0 + seg);
+    for (int i = a0 + lane; i < a1; i += 32) {
+        const int e = ids[i];
+        if (e >= 0 && e < E) atomicAdd(&cnt[warp * E + e], 1);
+    }
+    __syncthreads();
+    int total = 0;
+    if (t < E)
+        for (int ww = 0; ww < kAlignWarps; ++ww) total += cnt[ww * E + t];
+    const int nch = (total + chunk - 1) / chunk;
+    int n_valid = 0, n_routed_items = 0;
+    const int start = block_excl_scan(total, scan, &n_valid);
+    if (t < E) {
+        int run = start;
+        for (int ww = 0; ww < kAlignWarps; ++ww) {
+            const int c = cnt[ww * E + t];
+            cnt[ww * E + t] = run;
+            run += c;
+        }
+    }
+    const int ibase = block_excl_scan(nch, scan, &n_routed_items);
+    const int shared_items = shared ? (M + chunk - 1) / chunk : 0;
+    if (t == 0) {
+        ws_i[0] = n_routed_items + shared_items;
+        ws_i[1] = n_valid;
+    }
+    __syncthreads();
+    // stable placement: each warp walks its segment in order, 32 pairs at a time
+    for (int base = a0; base < a1; base += 32) {
+        const int i = base + lane;
+        const bool act = i < a1;
+        const unsigned amask = __ballot_sync(0xFFFFFFFFu, act);
+        if (act) {
+            const int e = ids[i];
+            const bool valid = e >= 0 && e < E;
+            const unsigned peers = __match_any_sync(amask, valid ? e : -1);
+            const unsigned before = peers & ((1u << lane) - 1u);
+            if (valid) {
+                const int pos = cnt[warp * E + e] + __popc(before);
+                pair_tok[pos] = i / topk;
+                pair_w[pos] = w[i];
+                pair_of[i] = pos;
+            } else {
+                pair_of[i] = -1;
+            }
+            __syncwarp(amask);
+            if (valid && before == 0) cnt[warp * E + e] += __popc(peers);
+            __syncwarp(amask);
+        }
+    }
+    if (t < E)
+        for (int c = 0; c < nch; ++c) {
+            item_expert[ibase + c] = t;
+            item_start[ibase + c] = start + c * chunk;
+            item_cnt[ibase + c] = min(chunk, total - c * chunk);
+        }
+    if (shared) {
+        for (int m = t; m < M; m += kAlignThreads) {
+            pair_tok[n_valid + m] = m;
+            pair_w[n_valid + m] = 1.0f;
+        }
+        for (int c = t; c < shared_items; c += kAlignThreads) {
+            item_expert[n_routed_items + c] = E;
+            item_start[n_routed_items + c] = n_valid + c * chunk;
+            item_cnt[n_routed_items + c] = min(chunk, M - c * chunk);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ combine
+
+// out[m][h] = sum_j ybuf[pair_of[m*topk + j]][h] (+ ybuf[n_valid + m][h] for the shared expert), slot order.
+template <typename TOut>
+__global__ void k_combine(const float* __restrict__ ybuf, const int* __restrict__ pair_of, const int* ws_i, int M,
+                          int H, int topk, int shared, TOut* out) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;     // one float4 of one row
+    const int per_row = H / 4;
+    if (idx >= M * per_row) return;
+    const int m = idx / per_row, c = (idx % per_row) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < topk; ++j) {
+        const int pos = pair_of[m * topk + j];
+        if (pos < 0) continue;
+        const float4 v = *reinterpret_cast<const float4*>(ybuf + (size_t)pos * H + c);
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    if (shared) {
+        const float4 v = *reinterpret_cast<const float4*>(ybuf + (size_t)(ws_i[1] + m) * H + c);
+        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    if constexpr (sizeof(TOut) == 4) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)m * H + c) = acc;
+    } else {
+        __half* o = reinterpret_cast<__half*>(out) + (size_t)m * H + c;
+        o[0] = __float2half_rn(acc.x); o[1] = __float2half_rn(acc.y);
+        o[2] = __float2half_rn(acc.z); o[3] = __float2half_rn(acc.w);
+    }
+}
+
+static int launch_align(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
+                        uint8_t* ws, const WsLayout& L, cudaStream_t st) {
+    const size_t smem = (size_t)(kAlignWarps * E + kAlignThreads) * 4;
+    EXL3_REQUIRE(smem <= 227 * 1024, EXL3_ERR_UNSUPPORTED, "moe align: E=%d too large", E);
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(k_align, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
+            set_error("moe align: cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError()));
+            return EXL3_ERR_CUDA;
+        }
+        configured[dev] = 1;
+    }
+    int* wi = reinterpret_cast<int*>(ws);
+    k_align<<<1, kAlignThreads, smem, st>>>(ids, w, M * topk, topk, E, M, shared, chunk, wi,
+                                            reinterpret_cast<int*>(ws + L.item_expert),
+                                            reinterpret_cast<int*>(ws + L.item_start),
+                                            reinterpret_cast<int*>(ws + L.item_cnt),
+                                            reinterpret_cast<int*>(ws + L.pair_tok),
+                                            reinterpret_cast<int*>(ws + L.pair_of),
+                                            reinterpret_cast<float*>(ws + L.pair_w));
+    EXL3_LAUNCH_CHECK("moe align");
+    return EXL3_OK;
+}
+
+}  // namespace exl3
+
+using namespace exl3;
+
+extern "C" {
+
+int exl3_route(const float* logits, int ld, int R, int E, int kind, int k, const float* bias, const float* res,
+               const float* mul, float scale, int renorm, void* ids, int ids64, float* w, void* want,
+               void* stream) {
+    EXL3_REQUIRE(logits && ids && w && R >= 0 && E > 0 && ld >= E, EXL3_ERR_ARG, "exl3_route: bad arguments");
+    EXL3_REQUIRE(E <= kRouteMaxE, EXL3_ERR_UNSUPPORTED, "exl3_route: E=%d > %d", E, kRouteMaxE);
+    EXL3_REQUIRE(k >= 1 && k <= kRouteMaxK && k <= E, EXL3_ERR_ARG, "exl3_route: k=%d", k);
+    EXL3_REQUIRE(kind >= 0 && kind <= 2, EXL3_ERR_ARG, "exl3_route: kind=%d", kind);
+    if (R == 0) return EXL3_OK;
+    k_route<<<R, kRouteThreads, 0, static_cast<cudaStream_t>(stream)>>>(logits, ld, E, kind, k, bias, res, mul, scale,
+                                                                        renorm, ids, ids64, w, want);
+    EXL3_LAUNCH_CHECK("exl3_route");
+    return EXL3_OK;
+}
+
+size_t exl3_moe_workspace_size(int M, int topk, int E, int H, int I, int shared) {
+    if (M <= 0 || topk <= 0 || E <= 0) return 0;
+    return ws_layout(M, topk, E, H, I, shared, kItemRows).total;
+}
+
+int exl3_moe_align(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
+                   void* workspace, size_t ws_bytes, void* stream) {
+    EXL3_REQUIRE(ids && w && M > 0 && topk > 0 && E > 0 && chunk > 0, EXL3_ERR_ARG, "exl3_moe_align: bad arguments");
+    EXL3_REQUIRE(E <= 1024, EXL3_ERR_UNSUPPORTED, "exl3_moe_align: E=%d > 1024", E);
+    const WsLayout L = ws_layout(M, topk, E, 128, 128, shared, chunk);
+    EXL3_REQUIRE(workspace && ws_bytes >= L.abuf, EXL3_ERR_WORKSPACE, "exl3_moe_align: workspace %zu < %zu",
+                 ws_bytes, L.abuf);
+    return launch_align(ids, w, M, topk, E, shared, chunk, static_cast<uint8_t*>(workspace), L,
+                        static_cast<cudaStream_t>(stream));
+}
+
+static int moe_check(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
+                     int H, int I, int split_k, const char* what) {
+    EXL3_REQUIRE(experts && M >= 0 && topk > 0 && E > 0, EXL3_ERR_ARG, "%s: bad arguments", what);
+    EXL3_REQUIRE(E <= 1024, EXL3_ERR_UNSUPPORTED, "%s: E=%d > 1024", what, E);
+    EXL3_REQUIRE(H % 128 == 0 && I % 128 == 0 && H > 0 && I > 0, EXL3_ERR_ARG,
+                 "%s: H=%d, I=%d must be multiples of 128", what, H, I);
+    if (x) {
+        EXL3_REQUIRE(x_dtype == EXL3_F16 || x_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "%s: x dtype", what);
+        EXL3_REQUIRE(ldx >= H && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 7) == 0, EXL3_ERR_ARG,
+                     "%s: x rows must be 8-byte aligned (ldx=%d)", what, ldx);
+    }
+    EXL3_REQUIRE(split_k >= 0 && split_k <= kMaxCluster, EXL3_ERR_ARG, "%s: split_k=%d", what, split_k);
+    return EXL3_OK;
+}
+
+static GemvArgs moe_args(const void* x, int x_dtype, int ldx, const exl3_expert* experts, float act_limit,
+                         uint8_t* ws, const WsLayout& L) {
+    GemvArgs a = {};
+    a.x = x;
+    a.ldx = ldx;
+    a.x_bf16 = x_dtype == EXL3_BF16;
+    a.experts = reinterpret_cast<const ExpertDesc*>(experts);
+    a.items.n_items = reinterpret_cast<const int*>(ws);
+    a.items.item_expert = reinterpret_cast<const int*>(ws + L.item_expert);
+    a.items.item_start = reinterpret_cast<const int*>(ws + L.item_start);
+    a.items.item_cnt = reinterpret_cast<const int*>(ws + L.item_cnt);
+    a.items.pair_tok = reinterpret_cast<const int*>(ws + L.pair_tok);
+    a.items.pair_w = reinterpret_cast<const float*>(ws + L.pair_w);
+    a.abuf = reinterpret_cast<__half*>(ws + L.abuf);
+    a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
+    a.act_limit = act_limit;
+    a.status = device_status_ptr();
+    return a;
+}
+
+static int run_gateup(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
+                      int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes, int split_k,
+                      cudaStream_t st) {
+    int rc = moe_check(x, x_dtype, ldx, M, topk, experts, E, H, I, split_k, "exl3_moe_gateup");
+    if (rc || M == 0) return rc;
+    EXL3_REQUIRE(x, EXL3_ERR_ARG, "exl3_moe_gateup: null x");
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, kItemRows);
+    EXL3_REQUIRE(workspace && ws_bytes >= L.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
+                 "exl3_moe_gateup: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, L.total);
+    GemvArgs a = moe_args(x, x_dtype, ldx, experts, act_limit, static_cast<uint8_t*>(workspace), L);
+    a.k = H;
+    a.n = I;
+    const int units = L.max_items * (I / 128);
+    a.split = choose_split(units, H, 2, split_k);
+    return launch_gemv<EPI_GATEUP, __half>(a, units, st, "exl3_moe_gateup");
+}
+
+static int run_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
+                    size_t ws_bytes, int split_k, cudaStream_t st) {
+    int rc = moe_check(nullptr, 0, 0, M, topk, experts, E, H, I, split_k, "exl3_moe_down");
+    if (rc || M == 0) return rc;
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, kItemRows);
+    EXL3_REQUIRE(workspace && ws_bytes >= L.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
+                 "exl3_moe_down: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, L.total);
+    GemvArgs a = moe_args(nullptr, 0, 0, experts, 0.f, static_cast<uint8_t*>(workspace), L);
+    a.k = I;
+    a.n = H;
+    const int units = L.max_items * (H / 128);
+    a.split = choose_split(units, I, 1, split_k);
+    return launch_gemv<EPI_DOWN, __half>(a, units, st, "exl3_moe_down");
+}
+
+static int run_combine(int M, int topk, int E, int shared, int H, int I, void* out, int out_dtype, void* workspace,
+                       size_t ws_bytes, cudaStream_t st) {
+    EXL3_REQUIRE(out && M >= 0 && topk > 0 && H % 128 == 0, EXL3_ERR_ARG, "exl3_moe_combine: bad arguments");
+    EXL3_REQUIRE(out_dtype == EXL3_F16 || out_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED, "exl3_moe_combine: out dtype");
+    if (M == 0) return EXL3_OK;
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, kItemRows);
+    EXL3_REQUIRE(workspace && ws_bytes >= L.total, EXL3_ERR_WORKSPACE, "exl3_moe_combine: workspace too small");
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const float* ybuf = reinterpret_cast<const float*>(ws + L.ybuf);
+    const int* pair_of = reinterpret_cast<const int*>(ws + L.pair_of);
+    const int n4 = M * (H / 4);
+    if (out_dtype == EXL3_F32)
+        k_combine<float><<<(n4 + 255) / 256, 256, 0, st>>>(ybuf, pair_of, reinterpret_cast<const int*>(ws), M, H,
+                                                           topk, shared, static_cast<float*>(out));
+    else
+        k_combine<__half><<<(n4 + 255) / 256, 256, 0, st>>>(ybuf, pair_of, reinterpret_cast<const int*>(ws), M, H,
+                                                            topk, shared, static_cast<__half*>(out));
+    EXL3_LAUNCH_CHECK("exl3_moe_combine");
+    return EXL3_OK;
+}
+
+int exl3_moe_gateup(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
+                    int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes, int split_k,
+                    void* stream) {
+    return run_gateup(x, x_dtype, ldx, M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, split_k,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int exl3_moe_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
+                  size_t ws_bytes, int split_k, void* stream) {
+    return run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, split_k,
+                    static_cast<cudaStream_t>(stream));
+}
+
+int exl3_moe_combine(int M, int topk, int E, int shared, int H, int I, void* out, int out_dtype, void* workspace,
+                     size_t ws_bytes, void* stream) {
+    return run_combine(M, topk, E, shared, H, I, out, out_dtype, workspace, ws_bytes,
+                       static_cast<cudaStream_t>(stream));
+}
+
+int exl3_moe_decode(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w, int topk,
+                    const exl3_expert* experts, int E, int shared, int H, int I, float act_limit, void* out,
+                    int out_dtype, void* workspace, size_t ws_bytes, int split_k, void* stream) {
+    int rc = moe_check(x, x_dtype, ldx, M, topk, experts, E, H, I, split_k, "exl3_moe_decode");
+    if (rc) return rc;
+    EXL3_REQUIRE(x && ids && w && out, EXL3_ERR_ARG, "exl3_moe_decode: null pointer");
+    EXL3_REQUIRE(out_dtype == EXL3_F16 || out_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED, "exl3_moe_decode: out dtype");
+    if (M == 0) return EXL3_OK;
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, kItemRows);
+    EXL3_REQUIRE(workspace && ws_bytes >= L.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
+                 "exl3_moe_decode: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, L.total);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    rc = launch_align(ids, w, M, topk, E, shared, kItemRows, static_cast<uint8_t*>(workspace), L, st);
+    if (rc) return rc;
+    rc = run_gateup(x, x_dtype, ldx, M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, split_k, st);
+    if (rc) return rc;
+    rc = run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, split_k, st);
+    if (rc) return rc;
+    return run_combine(M, topk, E, shared, H, I, out, out_dtype, workspace, ws_bytes, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,69 @@
+// Library plumbing: per-thread error text, SM count, and the device status word that bounded device waits write.
+#include <stdarg.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace exl3 {
+
+static thread_local char t_err[512] = {0};
+
+void set_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(t_err, sizeof(t_err), fmt, ap);
+    va_end(ap);
+}
+
+int num_sms() {
+    static int cache[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev] = n > 0 ? n : 148;
+    }
+    return cache[dev];
+}
+
+// Sticky device-side status (first failure wins); kernels receive its address as an argument.
+static __device__ int g_device_status;
+
+int* device_status_ptr() {
+    static int* cache[64] = {nullptr};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cache[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+        cache[dev] = static_cast<int*>(p);
+    }
+    return cache[dev];
+}
+
+}  // namespace exl3
+
+extern "C" {
+
+int exl3_version(void) { return 100; }
+
+const char* exl3_last_error(void) { return exl3::t_err; }
+
+int exl3_device_status(int reset) {
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, exl3::g_device_status, sizeof(int)) != cudaSuccess) {
+        exl3::set_error("exl3_device_status: %s", cudaGetErrorString(cudaGetLastError()));
+        return EXL3_ERR_CUDA;
+    }
+    if (reset) {
+        int z = 0;
+        cudaMemcpyToSymbol(exl3::g_device_status, &z, sizeof(int));
+    }
+    return v;
+}
+
+}  // extern "C"

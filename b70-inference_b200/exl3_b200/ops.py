@@ -1,0 +1,243 @@
+"""exllamav3_ext ops of the EXL3 linear path on B200, with the reference's names, arguments and in-place semantics.
+
+Mirrors glm/xpu/glm_xpu/ops.py of horvay/b70-inference (the XPU stand-in for exllamav3's extension): callers hand in
+preallocated outputs and read them back, as the CUDA ops do. Every op runs on this package's CUDA library through
+its C ABI; none has a CPU path.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _lib as L
+
+SMALL_M_MAX = int(os.environ.get("EXL3_SMALL_M_MAX", "32"))        # rows up to this: fused decode GEMV (8-row calls)
+RECON_SLICE_N = int(os.environ.get("EXL3_RECON_SLICE_N", "16384"))  # prefill: dequantised column slice width
+
+
+def _f16(t: torch.Tensor) -> torch.Tensor:
+    t = t if t.dtype in (torch.float16, torch.bfloat16) else t.half()
+    return t if t.is_contiguous() else t.contiguous()
+
+
+# ----------------------------------------------------------------------------------------------- EXL3 linear
+
+def exl3_gemv(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
+              y: torch.Tensor, split_k: int = 0) -> None:
+    """y[M, n] = Had(Had(x * suh) @ W_hat) * svh for M <= 8 rows; y fp16/bf16/fp32 preallocated (C ABI exl3_gemv)."""
+    L.require_cuda(x, trellis, y)
+    M, k = x.shape
+    n = svh.shape[0]
+    rc = L.lib().exl3_gemv(x.data_ptr(), L.dtype_code(x.dtype), x.stride(0), M, trellis.data_ptr(),
+                           L.ptr(suh), svh.data_ptr(), k, n, int(K), 2, y.data_ptr(), L.dtype_code(y.dtype),
+                           y.stride(0), int(split_k), L.stream_of(x))
+    L.check(rc, "exl3_gemv")
+
+
+def exl3_reconstruct(trellis: torch.Tensor, w: torch.Tensor, n0: int, K: int, cb: int = 2) -> None:
+    """w[k, n_slice] (fp16, written) = W_hat[:, n0 : n0 + n_slice] (glm/xpu/csrc/exl3_ops.sycl:539-555)."""
+    L.require_cuda(trellis, w)
+    k, n = trellis.shape[0] * 16, trellis.shape[1] * 16
+    rc = L.lib().exl3_dequant(trellis.data_ptr(), k, n, int(K), int(cb), int(n0), w.shape[1], w.data_ptr(),
+                              w.stride(0), L.stream_of(w))
+    L.check(rc, "exl3_dequant")
+
+
+def reconstruct(unpacked: torch.Tensor, packed: torch.Tensor, K, mcg: bool = False, mul1: bool = True) -> None:
+    """exllamav3 reconstruct(unpacked, packed, K, mcg, mul1) (glm/docs/ext-op-inventory.md:597-612)."""
+    if mcg or not mul1:
+        raise L.Exl3Error("reconstruct: only the mul1 codebook is supported")
+    exl3_reconstruct(packed, unpacked, 0, int(K))
+
+
+def reconstruct_slice(unpacked: torch.Tensor, packed: torch.Tensor, K, mcg: bool, mul1: bool, n_offset: int) -> None:
+    if mcg or not mul1:
+        raise L.Exl3Error("reconstruct_slice: only the mul1 codebook is supported")
+    exl3_reconstruct(packed, unpacked, int(n_offset), int(K))
+
+
+def had_r_128(input: torch.Tensor, output: torch.Tensor, pre_scale, post_scale, scale: float) -> None:
+    """Blockwise 128-point Hadamard * scale/sqrt(128); pre_scale wins over post_scale (glm/xpu/glm_xpu/ops.py:
+    132-142). fp16 in/out (products rounded to fp16) or fp32 in/out. In place allowed."""
+    L.require_cuda(input, output)
+    if input.dtype != output.dtype or input.dtype not in (torch.float16, torch.float32):
+        raise L.Exl3Error("had_r_128: input/output must both be fp16 or both fp32")
+    x = input if input.is_contiguous() else input.contiguous()
+    out = output if output.is_contiguous() else torch.empty_like(output)
+    cols = x.shape[-1]
+    rows = x.numel() // cols
+    pre = pre_scale.half().contiguous() if pre_scale is not None else None
+    post = post_scale.half().contiguous() if post_scale is not None else None
+    rc = L.lib().exl3_had_r_128(x.data_ptr(), out.data_ptr(), L.dtype_code(x.dtype), rows, cols, L.ptr(pre),
+                                L.ptr(post), float(scale), L.stream_of(x))
+    L.check(rc, "had_r_128")
+    if out is not output:
+        output.copy_(out)
+
+
+class BC_LinearEXL3:
+    """EXL3 linear y = Had(Had(x * suh) @ W_hat) * svh (glm/xpu/glm_xpu/ops.py:34-88; exllamav3 contract
+    glm/docs/ext-op-inventory.md:471-496). Other modules read trellis/suh/svh/K/mcg/mul1 by name.
+
+    run(x, y): x fp16/bf16 [..., k] -> y (fp16/bf16/fp32, preallocated) [..., n].
+      rows <= SMALL_M_MAX: the fused decode GEMV, 8 rows per launch (weights streamed once per launch);
+      larger: rotate x, dequantise W_hat in RECON_SLICE_N-column slices, library GEMM, rotate back
+      (the reference's prefill path, glm/xpu/csrc/exl3_ops.sycl:651-757)."""
+
+    def __init__(self, trellis, suh, svh, K, bias, mcg, mul1, xh):
+        if mcg or not mul1:
+            raise L.Exl3Error("BC_LinearEXL3: only the mul1 codebook is supported")
+        if float(K) != int(K) or not 1 <= int(K) <= 8:
+            raise L.Exl3Error(f"BC_LinearEXL3: K={K} (integer 1..8 supported)")
+        self.trellis = trellis
+        self.suh = suh
+        self.svh = svh
+        self.K = K
+        self.bias = bias
+        self.mcg = mcg
+        self.mul1 = mul1
+        self.xh = xh
+        self.Ki = int(K)
+        self.in_features = trellis.shape[0] * 16
+        self.out_features = trellis.shape[1] * 16
+        if trellis.shape[2] != 16 * self.Ki:
+            raise L.Exl3Error(f"BC_LinearEXL3: trellis {tuple(trellis.shape)} does not match K={K}")
+
+    def run(self, x: torch.Tensor, y: torch.Tensor) -> None:
+        x2 = _f16(x.reshape(-1, self.in_features))
+        y2 = y.view(-1, self.out_features)
+        M = x2.shape[0]
+        if M == 0:
+            return
+        if M <= SMALL_M_MAX:
+            for m0 in range(0, M, 8):
+                exl3_gemv(x2[m0:m0 + 8], self.trellis, self.suh, self.svh, self.Ki, y2[m0:m0 + 8])
+        else:
+            self._run_recon(x2, y2)
+        if self.bias is not None:
+            y2.add_(self.bias)
+
+    def _run_recon(self, x2: torch.Tensor, y2: torch.Tensor) -> None:
+        M, k, n = x2.shape[0], self.in_features, self.out_features
+        xh = torch.empty((M, k), dtype=torch.float16, device=x2.device)
+        had_r_128(x2.half(), xh, self.suh, None, 1.0)
+        acc = torch.empty((M, n), dtype=torch.float16 if y2.dtype != torch.float32 else torch.float32,
+                          device=x2.device)
+        w = torch.empty((k, min(RECON_SLICE_N, n)), dtype=torch.float16, device=x2.device)
+        for n0 in range(0, n, RECON_SLICE_N):
+            n1 = min(n0 + RECON_SLICE_N, n)
+            ws = w[:, :n1 - n0]
+            exl3_reconstruct(self.trellis, ws, n0, self.Ki)
+            if acc.dtype == torch.float32:
+                acc[:, n0:n1] = torch.matmul(xh.float(), ws.float())
+            else:
+                torch.matmul(xh, ws, out=acc[:, n0:n1])
+        if y2.dtype == torch.float32:
+            had_r_128(acc, acc, None, self.svh.float(), 1.0)
+            y2.copy_(acc)
+        else:
+            had_r_128(acc, acc, None, self.svh, 1.0)
+            y2.copy_(acc)
+
+    def run_alloc(self, x: torch.Tensor, out_features: int, output_fp32: bool) -> torch.Tensor:
+        y = torch.empty(x.shape[:-1] + (out_features,), dtype=torch.float if output_fp32 else torch.half,
+                        device=x.device)
+        if out_features == 0:
+            return y
+        self.run(x.reshape(-1, x.shape[-1]), y.view(-1, out_features))
+        return y
+
+
+def exl3_gemm(A, B, C, suh, A_had, svh, force_shape_idx=-1, mcg=False, mul1=True, force_num_sms=0) -> int:
+    """exllamav3 exl3_gemm(A, B, C, suh, A_had, svh, ...) (glm/docs/ext-op-inventory.md:498-557): C = lin(A)."""
+    K = B.shape[2] // 16
+    BC_LinearEXL3(B, suh, svh, K, None, mcg, mul1, A_had).run(A, C)
+    return 0
+
+
+# ----------------------------------------------------------------------------------------------- activation / MLP
+
+def silu_mul(x: torch.Tensor, y: torch.Tensor, z: torch.Tensor, act_limit: float) -> None:
+    """z = min(silu(x), L) * clamp(y, -L, L) (L = act_limit, 0 disables), fp32 math, stored to z (fp16)
+    (glm/xpu/glm_xpu/ops.py:147-154)."""
+    L.require_cuda(x, y, z)
+    g = x.half().contiguous()
+    u = y.half().contiguous()
+    zz = z if (z.dtype == torch.float16 and z.is_contiguous()) else torch.empty_like(g)
+    rc = L.lib().exl3_silu_mul(g.data_ptr(), u.data_ptr(), zz.data_ptr(), g.numel(), float(act_limit or 0.0),
+                               L.stream_of(g))
+    L.check(rc, "silu_mul")
+    if zz is not z:
+        z.copy_(zz.view(z.shape))
+
+
+class BC_GatedMLP:
+    """Dense / shared-expert gated MLP for rows <= 8: g, u = gate(x), up(x); a = silu_mul(g, u); d = down(a)
+    (glm/xpu/glm_xpu/ops.py:157-172)."""
+
+    def __init__(self, guh, gu, a, down_xh, gu_ptrs_trellis, gu_ptrs_suh, gu_ptrs_svh, gu_K, gu_mcg, gu_mul1,
+                 act_silu, act_gelu, act_relu2, gate, up, down, act_limit):
+        if gate is None or up is None:
+            raise L.Exl3Error("BC_GatedMLP: fused gate/up pointer tables are not supported; pass gate and up")
+        if not act_silu:
+            raise L.Exl3Error("BC_GatedMLP: only SiLU gated MLPs")
+        self.gate, self.up, self.down = gate, up, down
+        self.act_limit = act_limit
+
+    def run_bszN(self, x: torch.Tensor, d: torch.Tensor) -> None:
+        x2 = x.reshape(-1, x.shape[-1])
+        g = self.gate.run_alloc(x2, self.gate.out_features, False)
+        u = self.up.run_alloc(x2, self.up.out_features, False)
+        silu_mul(g, u, u, self.act_limit)
+        self.down.run(u, d.view(-1, d.shape[-1]))
+
+
+# ----------------------------------------------------------------------------------------------- routing
+
+def route(logits: torch.Tensor, kind: int, k: int, bias=None, res=None, mul=None, scale: float = 1.0,
+          renorm: bool = True, want: bool = False, ids_dtype=torch.int32):
+    """Top-k routing with residency bias on fp32 logits [R, E] -> (ids [R, k], w fp32 [R, k], want or None).
+    See exl3_route in include/exl3_b200.h for the exact math."""
+    L.require_cuda(logits)
+    lg = logits.float().contiguous()
+    R, E = lg.shape
+    dev = lg.device
+    ids = torch.empty((R, k), dtype=ids_dtype, device=dev)
+    w = torch.empty((R, k), dtype=torch.float32, device=dev)
+    wt = torch.empty((R, k), dtype=ids_dtype, device=dev) if want else None
+    b = bias.float().contiguous() if bias is not None else None
+    r = res.float().contiguous() if res is not None else None
+    m = mul.float().contiguous() if mul is not None else None
+    rc = L.lib().exl3_route(lg.data_ptr(), lg.stride(0), R, E, int(kind), int(k), L.ptr(b), L.ptr(r), L.ptr(m),
+                            float(scale), int(bool(renorm)), ids.data_ptr(), int(ids_dtype == torch.int64),
+                            w.data_ptr(), L.ptr(wt), L.stream_of(lg))
+    L.check(rc, "exl3_route")
+    return ids, w, wt
+
+
+def routing_ds3_nogroup(hidden, gate, scores, bias, topk_indices, topk_weights, scaling_factor, gate_t, act_fn,
+                        gate_i8, gate_sb, res=None):
+    """Sigmoid / noaux_tc top-k routing (glm/xpu/glm_xpu/ops.py:177-193): logits = hidden @ gate rounded to fp16
+    (written to scores); selection by sigmoid + bias (+ residency bias `res`, glm/xpu/glm_xpu/block_graphs.py:
+    164-167); weights from the unbiased sigmoid, normalised over the picks and scaled. Writes scores, topk_indices,
+    topk_weights in place."""
+    if act_fn != 0:
+        raise L.Exl3Error("routing_ds3_nogroup: sigmoid routing only (act_fn 0)")
+    E = scores.shape[-1]
+    k = topk_indices.shape[-1]
+    if hidden.dtype == gate.dtype == torch.half:
+        logits = torch.matmul(hidden, gate[:, :E])
+    else:
+        logits = torch.matmul(hidden.float(), gate[:, :E].float()).half()
+    scores.copy_(logits)
+    ids, w, _ = route(logits.float(), L.ROUTE_SIGMOID, k, bias=bias, res=res, scale=scaling_factor,
+                      ids_dtype=torch.int64 if topk_indices.dtype == torch.int64 else torch.int32)
+    topk_indices.copy_(ids)
+    topk_weights.copy_(w)
+
+
+def det_quant_weight(w, w_i8, w_s) -> None:
+    """No-op: only feeds exllamav3's deterministic routing GEMM, which this path does not use
+    (glm/xpu/glm_xpu/ops.py:196-197)."""
+    return None

@@ -1,0 +1,148 @@
+/* C ABI of the B200 EXL3 trellis library (libexl3_b200.so).
+ *
+ * Plain device pointers, sizes and a CUDA stream (passed as void*, a cudaStream_t; NULL = legacy default stream).
+ * Every entry point returns EXL3_OK or an error code and never throws; exl3_last_error() gives the text of the
+ * calling thread's last failure. No entry point allocates device memory except where stated; scratch comes from
+ * the caller as (workspace, ws_bytes) sized by the matching *_workspace_size function. All launches go on the
+ * given stream, so calls are CUDA-graph capturable when the caller's buffers are fixed.
+ *
+ * Layouts (exllamav3 EXL3, unchanged): trellis = int16 [k/16][n/16][16*K] (a 16x16 tile of K-bit weights is
+ * 8*K little-endian uint32 words); suh = fp16 [k]; svh = fp16 [n]; activations row-major [rows][k].
+ * Reference interfaces are cited as paths inside horvay/b70-inference.
+ */
+#ifndef EXL3_B200_H
+#define EXL3_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define EXL3_API __attribute__((visibility("default")))
+#else
+#define EXL3_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define EXL3_OK 0
+#define EXL3_ERR_ARG 1          /* invalid argument (shape, pointer, alignment) */
+#define EXL3_ERR_UNSUPPORTED 2  /* valid but not supported (codebook, K, size) */
+#define EXL3_ERR_WORKSPACE 3    /* workspace missing or too small */
+#define EXL3_ERR_CUDA 4         /* CUDA runtime error (launch, attribute) */
+#define EXL3_ERR_TIMEOUT 5      /* a device-side wait gave up (recorded in the device status word) */
+
+/* element types */
+#define EXL3_F16 0
+#define EXL3_BF16 1
+#define EXL3_F32 2
+
+/* router kinds */
+#define EXL3_ROUTE_SIGMOID 0       /* noaux_tc sigmoid: glm/xpu/glm_xpu/ops.py:177-193 */
+#define EXL3_ROUTE_SOFTMAX 1       /* Qwen-Next softmax: trellis-serve.patch:394-441 */
+#define EXL3_ROUTE_SQRT_SOFTPLUS 2 /* DeepSeek-V4 sqrt(softplus): dsv41/xpu/csrc/dsv_moe_glue.sycl:155-193 */
+
+/* One expert's three EXL3 matrices (device addresses). The shared expert is an ordinary entry.
+ * Replaces the int64 pointer tables of exllamav3's BC_BlockSparseMLP / exl3_mgemm
+ * (glm/docs/ext-op-inventory.md:1018-1024,1104-1120) and the per-expert blob of
+ * glm/xpu/csrc/exl3_moe.n128.sycl:3-13 (K may differ per matrix, as the DSV piece tables allow,
+ * dsv41/xpu/csrc/dsv_moe.sycl:24-143). */
+typedef struct exl3_expert {
+    const void* trellis[3]; /* gate, up, down: int16 [k/16][n/16][16K]; gate/up k = hidden, n = interm */
+    const void* suh[3];     /* fp16 [k] */
+    const void* svh[3];     /* fp16 [n] */
+    int32_t K[3];           /* bits per weight, 1..8 */
+    int32_t pad;
+} exl3_expert;
+
+/* ---- library ---- */
+EXL3_API int exl3_version(void);
+EXL3_API const char* exl3_last_error(void);
+/* Device status word (sticky EXL3_ERR_TIMEOUT from bounded device waits); reset != 0 clears it. Synchronous. */
+EXL3_API int exl3_device_status(int reset);
+
+/* ---- dequantisation ----
+ * W_hat[:, n0 : n0 + n_slice] -> w (fp16 [k][n_slice], row stride ldw elements), Hadamard domain, no scales.
+ * Replaces exl3_reconstruct (glm/xpu/csrc/exl3_ops.sycl:539-555) and exllamav3 reconstruct/reconstruct_slice
+ * (glm/docs/ext-op-inventory.md:597-612). cb must be 2 (mul1). Bit-exact with the reference decode. */
+EXL3_API int exl3_dequant(const void* trellis, int k, int n, int K, int cb, int n0, int n_slice, void* w, int ldw,
+                 void* stream);
+
+/* ---- Hadamard ----
+ * Blockwise 128-point Hadamard, out = H(x [* pre]) * scale/sqrt(128) [* post] (pre wins if both given).
+ * dtype: EXL3_F16 (in/out fp16, products rounded to fp16) or EXL3_F32. cols % 128 == 0. In place allowed.
+ * Replaces had_r_128 (glm/xpu/glm_xpu/ops.py:132-142; glm/docs/ext-op-inventory.md:576-595) and the
+ * exl3_had_in_rm / exl3_had_out_h ops (glm/xpu/csrc/exl3_ops.sycl:781-811). */
+EXL3_API int exl3_had_r_128(const void* in, void* out, int dtype, int rows, int cols, const void* pre, const void* post,
+                   float scale, void* stream);
+
+/* ---- EXL3 linear, decode sizes ----
+ * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for M <= 8 rows (larger M: call per 8-row chunk, or use
+ * exl3_grouped_gemm); x fp16 or bf16 (x_dtype), y fp16/bf16/fp32 (y_dtype) with row strides ldx, ldy.
+ * k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2. split_k = CTAs per cluster along k (0 = auto).
+ * Replaces exl3_gemm_small (glm/xpu/csrc/exl3_ops.sycl:258-321) / exllamav3 exl3_gemm
+ * (glm/docs/ext-op-inventory.md:498-557) as called by BC_LinearEXL3.run (glm/xpu/glm_xpu/ops.py:60-80). */
+EXL3_API int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* trellis, const void* suh, const void* svh,
+              int k, int n, int K, int cb, void* y, int y_dtype, int ldy, int split_k, void* stream);
+
+/* ---- activation ----
+ * z = fp16(min(silu(g), L) * clamp(u, -L, L)), L = act_limit (0 disables the clamps); fp32 math.
+ * g, u, z fp16 [count]; z may alias u. Replaces silu_mul (glm/xpu/glm_xpu/ops.py:147-154). */
+EXL3_API int exl3_silu_mul(const void* g, const void* u, void* z, int64_t count, float act_limit, void* stream);
+
+/* ---- router ----
+ * Top-k per row of logits fp32 [R][E] (row stride ld), E <= 1024, k <= 32.
+ * score = sigmoid(l) | l (softmax kind) | sqrt(softplus(l)) (l > 20 -> l), evaluated in fp64 and rounded once;
+ * key = score * mul + bias + res (each optional, fp32 [E]); res is the residency (locality) bias:
+ * 0 resident, -margin slower tier, -inf unreadable, or +b on a resident subset.
+ * picks: k argmax passes, ties to the lowest expert index; ids[r][j] = j-th best (int32, or int64 if ids64).
+ * weights from the unbiased score: sigmoid / sqrt-softplus: w = s * scale / (sum + 1e-20);
+ * softmax: w = p / (sum p + 1e-20) if renorm else p. want (optional) = top-k of score + bias.
+ * Replaces routing_ds3_nogroup (glm/xpu/glm_xpu/ops.py:177-193) with the residency variant
+ * (glm/xpu/glm_xpu/block_graphs.py:146-179), dsv_glue::moe_route (dsv41/xpu/csrc/dsv_moe_glue.sycl:426-440)
+ * and fused_xpu.router (trellis-serve.patch:427-441). */
+EXL3_API int exl3_route(const float* logits, int ld, int R, int E, int kind, int k, const float* bias, const float* res,
+               const float* mul, float scale, int renorm, void* ids, int ids64, float* w, void* want,
+               void* stream);
+
+/* ---- MoE decode ----
+ * Routed MoE layer for decode batches: out[M][H] (fp32 or fp16) = sum_j w[m][j] * expert_{ids[m][j]}(x[m])
+ * (+ expert E, the shared expert, with weight 1 when shared != 0), summed in slot order.
+ * expert(x) = down(fp16(min(silu(gate(x)), L) * clamp(up(x), -L, L))), gate/up outputs rounded to fp16.
+ * x fp16/bf16 [M][H] (row stride ldx); ids int32 [M][topk] (ids < 0 or >= E skipped); w fp32 [M][topk];
+ * experts: device array of E (+1 shared) exl3_expert. H % 128 == 0, I % 128 == 0.
+ * Each expert is read once per call whatever number of rows picked it (rows grouped 8 per work item).
+ * Replaces exl3xpu_moe::moe_forward (glm/xpu/csrc/exl3_moe.n128.sycl:1338-1439) and exllamav3
+ * BC_BlockSparseMLP::run_bszN (glm/docs/ext-op-inventory.md:1030-1041). */
+EXL3_API size_t exl3_moe_workspace_size(int M, int topk, int E, int H, int I, int shared);
+EXL3_API int exl3_moe_decode(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w, int topk,
+                    const exl3_expert* experts, int E, int shared, int H, int I, float act_limit, void* out,
+                    int out_dtype, void* workspace, size_t ws_bytes, int split_k, void* stream);
+
+/* The phases of exl3_moe_decode as separate launches on one workspace, in order: exl3_moe_align (below),
+ * exl3_moe_gateup (gate|up GEMVs + activation + down-input rotation -> activation rows in the workspace),
+ * exl3_moe_down (down GEMVs x routing weight -> per-pair rows), exl3_moe_combine (fixed-order sum into out).
+ * Same arguments and constraints as exl3_moe_decode; exl3_moe_align must use chunk = 8.
+ * Replace the reference's GateUpKernel / DownKernel / CombineKernel launches
+ * (glm/xpu/csrc/exl3_moe.n128.sycl:736-790,1418-1438). */
+EXL3_API int exl3_moe_gateup(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
+                             int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes, int split_k,
+                             void* stream);
+EXL3_API int exl3_moe_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I,
+                           void* workspace, size_t ws_bytes, int split_k, void* stream);
+EXL3_API int exl3_moe_combine(int M, int topk, int E, int shared, int H, int I, void* out, int out_dtype,
+                              void* workspace, size_t ws_bytes, void* stream);
+
+/* Alignment step of exl3_moe_decode on its own (debug / reuse): writes into the workspace the item table and the
+ * pair permutation, in the layout documented in moe.cu. Replaces moe_align
+ * (glm/xpu/csrc/exl3_moe.n128.sycl:1442-1450). */
+EXL3_API int exl3_moe_align(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
+                   void* workspace, size_t ws_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EXL3_B200_H */

@@ -1,0 +1,162 @@
+"""Generate the golden fixtures in this directory by running the REFERENCE's own Python code on CPU.
+
+Run in a container where the reference tree is mounted (default /root/reference, or $B70_REFERENCE):
+
+    python tests/golden/make_golden.py
+
+What runs (all from horvay/b70-inference, unmodified, imported or exec'd from its files):
+  * glm/xpu/tests/units.py:42-89  -- mul1_lut, w_hat, H128, ref_linear (the reference's own torch restatement of
+    the EXL3 linear, fp64); the module body needs an XPU, so only that line range is exec'd;
+  * glm/xpu/glm_xpu/ops.py        -- routing_ds3_nogroup (sigmoid router), silu_mul, had_r_128;
+  * dsv41/xpu/dsv_xpu/moe.py      -- route() (sqrt-softplus router with the residency bias), its torch path.
+The outputs are small .npz files with seeded inputs and the reference's outputs; tests compare the oracle and the
+CUDA path against them. Nothing here runs at test time.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+import types
+
+import numpy as np
+import torch
+
+REF = os.environ.get("B70_REFERENCE", "/root/reference")
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def load_units_slice():
+    """exec glm/xpu/tests/units.py lines 42-89 (MUL1 .. ref_linear) in a fresh namespace."""
+    path = os.path.join(REF, "glm/xpu/tests/units.py")
+    lines = open(path).read().splitlines()
+    src = "\n".join(lines[41:89])
+    assert "def mul1_lut" in src and "def ref_linear" in src and "def w_hat" in src, "units.py layout changed"
+    ns = {"torch": torch, "math": __import__("math")}
+    exec(compile(src, path, "exec"), ns)
+    return ns
+
+
+def main():
+    sys.path.insert(0, os.path.join(REF, "glm/xpu"))
+    sys.path.insert(0, os.path.join(REF, "dsv41/xpu"))
+    from glm_xpu import ops as glm_ops            # noqa: E402
+    from dsv_xpu import moe as dsv_moe            # noqa: E402
+    U = load_units_slice()
+    rng = np.random.default_rng(20261201)
+    torch.manual_seed(1234)
+    meta = {}
+
+    # 1. codebook known answers (units.py mul1_lut)
+    lut = U["LUT"].numpy()
+    bits = lut.view(np.uint16).astype(np.uint64)
+    meta["lut"] = {"first8_bits": [int(b) for b in bits[:8]], "checksum_u64": int(bits.sum()),
+                   "weighted_checksum": int((bits * np.arange(65536, dtype=np.uint64)).sum() % (1 << 61)),
+                   "min": float(lut.astype(np.float32).min()), "max": float(lut.astype(np.float32).max()),
+                   "std": float(lut.astype(np.float64).std())}
+
+    # 2. decoded tiles for every K = 1..8 (units.py w_hat)
+    for K in range(1, 9):
+        tr = rng.integers(0, 65536, size=(2, 3, 16 * K), dtype=np.uint16)
+        w = U["w_hat"](torch.from_numpy(tr.view(np.int16).copy()), K).numpy()
+        np.savez_compressed(os.path.join(HERE, f"w_hat_K{K}.npz"), trellis=tr, w_hat=w)
+
+    # 3. EXL3 linear, fp64 reference (units.py ref_linear), k = n = 256
+    for K in (2, 3, 4, 5, 6):
+        k, n, M = 256, 384, 4
+        tr = rng.integers(0, 65536, size=(k // 16, n // 16, 16 * K), dtype=np.uint16)
+        suh = np.where(rng.integers(0, 2, k) == 1, 1.0, -1.0).astype(np.float16)
+        svh = (np.where(rng.integers(0, 2, n) == 1, 1.0, -1.0) * rng.uniform(0.5, 1.5, n)).astype(np.float16)
+        x = rng.standard_normal((M, k)).astype(np.float16)
+        y = U["ref_linear"](torch.from_numpy(x), torch.from_numpy(tr.view(np.int16).copy()), torch.from_numpy(suh),
+                            torch.from_numpy(svh), K).numpy()
+        np.savez_compressed(os.path.join(HERE, f"linear_K{K}.npz"), trellis=tr, suh=suh, svh=svh, x=x, y=y)
+
+    # 4. sigmoid router with e_score_correction_bias (glm_xpu.ops.routing_ds3_nogroup)
+    R, H, E, k = 16, 256, 160, 8
+    hidden = torch.from_numpy(rng.standard_normal((R, H)).astype(np.float16))
+    gate = torch.from_numpy((rng.standard_normal((H, E)) * 0.1).astype(np.float16))
+    bias = torch.from_numpy((rng.standard_normal(E) * 0.05).astype(np.float32))
+    scores = torch.empty((R, E), dtype=torch.half)
+    ids = torch.empty((R, k), dtype=torch.int64)
+    wts = torch.empty((R, k), dtype=torch.float32)
+    glm_ops.routing_ds3_nogroup(hidden, gate, scores, bias, ids, wts, 2.5, None, 0, None, None)
+    np.savez_compressed(os.path.join(HERE, "route_sigmoid.npz"), logits=scores.float().numpy(), bias=bias.numpy(),
+                        ids=ids.numpy(), w=wts.numpy(), k=k, scale=2.5)
+
+    # 5. sqrt-softplus router with residency bias (dsv_xpu.moe.route, torch path), exact and no-sync
+    R, H, E, k = 16, 256, 256, 8
+    y = torch.from_numpy(rng.standard_normal((R, H)).astype(np.float16))
+    gate_t = torch.from_numpy((rng.standard_normal((H, E)) * 0.1).astype(np.float16))
+    dbias = torch.from_numpy((rng.standard_normal(E) * 0.05).astype(np.float32))
+    res = np.zeros(E, dtype=np.float32)
+    res[rng.random(E) < 0.5] = -0.2                   # slower tier: -margin
+    res[rng.random(E) < 0.1] = -np.inf                # not readable
+    mod = types.SimpleNamespace(_gate_t=gate_t, num_experts_per_tok=k, routed_scaling_factor=1.5, _bias=dbias, _li=0)
+    dsv_moe.TIER = types.SimpleNamespace(nosync=False, res_pin=[torch.from_numpy(res)], res=[torch.from_numpy(res)])
+    dsv_moe.IN_PREFILL[0] = False
+    ids0, w0, _ = dsv_moe.route(mod, y, nosync=False)
+    ids1, w1, want1 = dsv_moe.route(mod, y, nosync=True)
+    logits = torch.matmul(y, gate_t).float().numpy()
+    np.savez_compressed(os.path.join(HERE, "route_sqrt_softplus.npz"), logits=logits, bias=dbias.numpy(), res=res,
+                        ids_exact=ids0.numpy(), w_exact=w0.numpy(), ids_nosync=ids1.numpy(), w_nosync=w1.numpy(),
+                        want_nosync=want1.numpy(), k=k, scale=1.5)
+
+    # 6. silu_mul (glm_xpu.ops.silu_mul) with and without the clamp
+    g = torch.from_numpy((rng.standard_normal(4096) * 6).astype(np.float16))
+    u = torch.from_numpy((rng.standard_normal(4096) * 6).astype(np.float16))
+    z10 = torch.empty_like(g)
+    z0 = torch.empty_like(g)
+    glm_ops.silu_mul(g, u, z10, 10.0)
+    glm_ops.silu_mul(g, u, z0, 0.0)
+    np.savez_compressed(os.path.join(HERE, "silu_mul.npz"), g=g.numpy(), u=u.numpy(), z10=z10.numpy(), z0=z0.numpy())
+
+    # 7. had_r_128 (glm_xpu.ops.had_r_128): pre-scaled fp16, post-scaled fp32
+    x16 = torch.from_numpy(rng.standard_normal((4, 512)).astype(np.float16))
+    pre = torch.from_numpy(np.where(rng.integers(0, 2, 512) == 1, 1.0, -1.0).astype(np.float16))
+    o16 = torch.empty_like(x16)
+    glm_ops.had_r_128(x16, o16, pre, None, 1.0)
+    x32 = torch.from_numpy(rng.standard_normal((4, 512)).astype(np.float32))
+    post = torch.from_numpy(rng.uniform(-2, 2, 512).astype(np.float32))
+    o32 = torch.empty_like(x32)
+    glm_ops.had_r_128(x32, o32, None, post, 1.0)
+    np.savez_compressed(os.path.join(HERE, "had_r_128.npz"), x16=x16.numpy(), pre=pre.numpy(), o16=o16.numpy(),
+                        x32=x32.numpy(), post=post.numpy(), o32=o32.numpy())
+
+    # 8. MoE expert math from reference pieces (units.py ref_linear + glm_xpu.ops.silu_mul), as units.py:140-157 does
+    H, I, E, M, topk, L = 256, 128, 4, 3, 2, 10.0
+    Ks = [2, 3, 4, 3]
+    ex = {}
+    for e in range(E):
+        K = Ks[e]
+        for nm, (kk, nn) in (("gate", (H, I)), ("up", (H, I)), ("down", (I, H))):
+            ex[f"{e}_{nm}_tr"] = rng.integers(0, 65536, size=(kk // 16, nn // 16, 16 * K), dtype=np.uint16)
+            ex[f"{e}_{nm}_suh"] = np.where(rng.integers(0, 2, kk) == 1, 1.0, -1.0).astype(np.float16)
+            ex[f"{e}_{nm}_svh"] = np.where(rng.integers(0, 2, nn) == 1, 1.0, -1.0).astype(np.float16)
+    x = rng.standard_normal((M, H)).astype(np.float16)
+    sel = np.stack([rng.permutation(E)[:topk] for _ in range(M)]).astype(np.int32)
+    wsel = rng.random((M, topk)).astype(np.float32)
+
+    def lin(xx, e, nm):
+        return U["ref_linear"](torch.from_numpy(xx), torch.from_numpy(ex[f"{e}_{nm}_tr"].view(np.int16).copy()),
+                               torch.from_numpy(ex[f"{e}_{nm}_suh"]), torch.from_numpy(ex[f"{e}_{nm}_svh"]), Ks[e])
+
+    out = np.zeros((M, H), dtype=np.float64)
+    for m in range(M):
+        for j in range(topk):
+            e = int(sel[m, j])
+            gg = lin(x[m:m + 1], e, "gate").half()
+            uu = lin(x[m:m + 1], e, "up").half()
+            glm_ops.silu_mul(gg, uu, uu, L)
+            d = lin(uu.numpy(), e, "down").numpy()[0]
+            out[m] += float(wsel[m, j]) * d
+    np.savez_compressed(os.path.join(HERE, "moe_expert.npz"), x=x, sel=sel, w=wsel, out=out, Ks=np.array(Ks),
+                        H=H, I=I, act_limit=L, **ex)
+
+    with open(os.path.join(HERE, "known_answers.json"), "w") as f:
+        json.dump(meta, f, indent=1, sort_keys=True)
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,86 @@
+"""The C-ABI library loads, exports every entry point include/exl3_b200.h declares, and rejects bad arguments with
+status codes before touching a GPU. CPU only: no compute call reaches a device."""
+import os
+import re
+
+import pytest
+import torch
+
+from exl3_b200 import _lib as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "exl3_b200.h")).read()
+    return sorted(set(re.findall(r"EXL3_API\s+[\w\s\*]*?\b(exl3_\w+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = L.lib()
+    decl = declared_symbols()
+    assert len(decl) >= 10
+    for name in decl:
+        assert hasattr(lib, name), name
+    assert sorted(L.exported_symbols()) == decl
+
+
+def test_version_and_error_text():
+    assert L.lib().exl3_version() >= 100
+    assert isinstance(L.lib().exl3_last_error(), bytes)
+
+
+def test_argument_validation_returns_status_codes():
+    lib = L.lib()
+    # codebook other than mul1
+    assert lib.exl3_gemv(16, 0, 128, 1, 16, 16, 16, 128, 128, 3, 1, 16, 0, 128, 0, None) == L.EXL3_ERR_UNSUPPORTED
+    assert b"mul1" in lib.exl3_last_error()
+    # K out of range
+    assert lib.exl3_dequant(16, 128, 128, 9, 2, 0, 128, 16, 128, None) == L.EXL3_ERR_UNSUPPORTED
+    # k not a multiple of 128
+    assert lib.exl3_gemv(16, 0, 128, 1, 16, 16, 16, 100, 128, 3, 2, 16, 0, 128, 0, None) == L.EXL3_ERR_ARG
+    # too many rows per call
+    assert lib.exl3_gemv(16, 0, 128, 9, 16, 16, 16, 128, 128, 3, 2, 16, 0, 128, 0, None) == L.EXL3_ERR_ARG
+    # misaligned trellis
+    assert lib.exl3_gemv(16, 0, 128, 1, 18, 16, 16, 128, 128, 3, 2, 16, 0, 128, 0, None) == L.EXL3_ERR_ARG
+    # dequant slice outside the matrix
+    assert lib.exl3_dequant(16, 128, 128, 3, 2, 64, 128, 16, 128, None) == L.EXL3_ERR_ARG
+    # router: too many experts, k > E
+    assert lib.exl3_route(16, 2048, 1, 2048, 0, 8, None, None, None, 1.0, 1, 16, 0, 16, None, None) == \
+        L.EXL3_ERR_UNSUPPORTED
+    assert lib.exl3_route(16, 4, 1, 4, 0, 8, None, None, None, 1.0, 1, 16, 0, 16, None, None) == L.EXL3_ERR_ARG
+    # MoE: missing workspace
+    assert lib.exl3_moe_decode(16, 0, 128, 1, 16, 16, 2, 16, 4, 0, 128, 128, 0.0, 16, 2, None, 0, 0, None) == \
+        L.EXL3_ERR_WORKSPACE
+    # zero rows is a no-op
+    assert lib.exl3_gemv(16, 0, 128, 0, 16, 16, 16, 128, 128, 3, 2, 16, 0, 128, 0, None) == L.EXL3_OK
+
+
+def test_workspace_size_grows_with_batch():
+    lib = L.lib()
+    a = lib.exl3_moe_workspace_size(1, 10, 512, 2048, 512, 0)
+    b = lib.exl3_moe_workspace_size(4, 10, 512, 2048, 512, 1)
+    assert 0 < a < b
+    assert lib.exl3_moe_workspace_size(0, 10, 512, 2048, 512, 0) == 0
+
+
+def test_ops_refuse_cpu_tensors():
+    from exl3_b200 import ops
+    x = torch.zeros(1, 128, dtype=torch.half)
+    tr = torch.zeros(8, 8, 48, dtype=torch.int16)
+    with pytest.raises(L.Exl3Error):
+        ops.exl3_gemv(x, tr, torch.ones(128, dtype=torch.half), torch.ones(128, dtype=torch.half), 3,
+                      torch.zeros(1, 128, dtype=torch.half))
+    with pytest.raises(L.Exl3Error):
+        ops.route(torch.zeros(1, 16), 0, 2)
+
+
+def test_bc_linear_rejects_unsupported_codebooks():
+    from exl3_b200 import ops
+    tr = torch.zeros(8, 8, 48, dtype=torch.int16)
+    with pytest.raises(L.Exl3Error):
+        ops.BC_LinearEXL3(tr, None, None, 3, None, True, False, None)
+    with pytest.raises(L.Exl3Error):
+        ops.BC_LinearEXL3(tr, None, None, 3.5, None, False, True, None)
+    bc = ops.BC_LinearEXL3(tr, None, None, 3, None, False, True, None)
+    assert (bc.in_features, bc.out_features) == (128, 128)
