@@ -115,7 +115,8 @@ def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, t
     topk_ids int32 [M, k] (other int types converted; ids < 0 or >= E skipped), topk_w fp32 [M, k].
     The exl3xpu_moe.moe_forward contract (glm/xpu/csrc/exl3_moe.n128.sycl:1338-1341) over ExpertTable descriptors.
     events: if a dict is given, the phases run as separate C-ABI calls and (start, end) CUDA event pairs around the
-    gate|up and down GEMV launches are appended to events["gateup"] / events["down"] (benchmark instrumentation)."""
+    gate|up and down GEMV launches are appended to events["gateup"] / events["down"] (benchmark instrumentation;
+    events["external"] = True makes them event-record nodes when the call is captured in a CUDA graph)."""
     L.require_cuda(x, topk_ids, topk_w)
     x2 = x.reshape(-1, x.shape[-1])
     if x2.dtype not in (torch.float16, torch.bfloat16):
@@ -146,7 +147,8 @@ def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, t
     # the same launches one phase at a time, with CUDA events around the two GEMV kernels
     L.check(lib.exl3_moe_align(ids.data_ptr(), w.data_ptr(), M, k, table.E, shared, 8, ws.data_ptr(), ws.numel(), st),
             "moe_forward align")
-    e0, e1, e2, e3 = (torch.cuda.Event(enable_timing=True) for _ in range(4))
+    ext = bool(events.get("external", False))      # event record nodes when captured in a CUDA graph
+    e0, e1, e2, e3 = (torch.cuda.Event(enable_timing=True, external=ext) for _ in range(4))
     e0.record()
     L.check(lib.exl3_moe_gateup(x2.data_ptr(), L.dtype_code(x2.dtype), x2.stride(0), M, k, table.table.data_ptr(),
                                 table.E, shared, H, table.I, float(act_limit), ws.data_ptr(), ws.numel(),
