@@ -89,11 +89,64 @@ __global__ void k_silu_mul(const __half* g, const __half* u, __half* z, int64_t 
     z[i] = __float2half_rn(s * uu);
 }
 
+// ------------------------------------------------------------------------------------------------ packing
+
+// exllamav3 [k/16][n/16][8K words] -> column-block-major [n/128][k/16][mats x 8 tiles][8K words]. The 8 tiles of one
+// (tile-row, 128-column block) are contiguous on both sides, so the permutation moves whole chunks: one warp per
+// destination chunk copies the chunk of every matrix (gate then up for a fused pair) with 16-byte loads.
+__global__ void __launch_bounds__(256) k_pack(const uint4* __restrict__ a, const uint4* __restrict__ b, int R,
+                                              int NB, int Ka, int Kb, uint4* __restrict__ out) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= R * NB) return;
+    const int cb = warp / R, r = warp % R;
+    const int ca = 16 * Ka, cbn = 16 * Kb;            // uint4 per chunk (8 tiles x 32K bytes / 16)
+    uint4* dst = out + (size_t)warp * (ca + cbn);
+    const uint4* sa = a + ((size_t)r * NB + cb) * ca;
+    for (int i = lane; i < ca; i += 32) dst[i] = __ldg(sa + i);
+    if (b) {
+        const uint4* sb = b + ((size_t)r * NB + cb) * cbn;
+        for (int i = lane; i < cbn; i += 32) dst[ca + i] = __ldg(sb + i);
+    }
+}
+
 }  // namespace exl3
 
 using namespace exl3;
 
 extern "C" {
+
+int exl3_pack(const void* trellis, int k, int n, int K, void* out, void* stream) {
+    EXL3_REQUIRE(trellis && out && k > 0 && n > 0 && k % 16 == 0 && n % 128 == 0, EXL3_ERR_ARG,
+                 "exl3_pack: k=%d must be a multiple of 16 and n=%d of 128", k, n);
+    EXL3_REQUIRE(K >= 1 && K <= 8, EXL3_ERR_UNSUPPORTED, "exl3_pack: K=%d not in 1..8", K);
+    EXL3_REQUIRE(aligned16(trellis) && aligned16(out) && trellis != out, EXL3_ERR_ARG,
+                 "exl3_pack: 16-byte aligned, non-overlapping buffers required");
+    const int R = k / 16, NB = n / 128;
+    const long warps = (long)R * NB;
+    k_pack<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(trellis), nullptr, R, NB, K, 0, static_cast<uint4*>(out));
+    EXL3_LAUNCH_CHECK("exl3_pack");
+    return EXL3_OK;
+}
+
+int exl3_pack_gateup(const void* gate, const void* up, int H, int I, int Kg, int Ku, void* out, void* stream) {
+    EXL3_REQUIRE(gate && up && out && H > 0 && I > 0 && H % 16 == 0 && I % 128 == 0, EXL3_ERR_ARG,
+                 "exl3_pack_gateup: H=%d must be a multiple of 16 and I=%d of 128", H, I);
+    EXL3_REQUIRE(Kg >= 1 && Kg <= 8 && Ku >= 1 && Ku <= 8, EXL3_ERR_UNSUPPORTED, "exl3_pack_gateup: K out of 1..8");
+    EXL3_REQUIRE(aligned16(gate) && aligned16(up) && aligned16(out), EXL3_ERR_ARG,
+                 "exl3_pack_gateup: 16-byte aligned buffers required");
+    const int R = H / 16, NB = I / 128;
+    const long warps = (long)R * NB;
+    k_pack<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<const uint4*>(gate), static_cast<const uint4*>(up), R, NB, Kg, Ku, static_cast<uint4*>(out));
+    EXL3_LAUNCH_CHECK("exl3_pack_gateup");
+    return EXL3_OK;
+}
+
+size_t exl3_gemv_workspace_size(int M, int k) {
+    if (M <= 0 || k <= 0) return 0;
+    return (size_t)M * k * 2 + 256;
+}
 
 int exl3_dequant(const void* trellis, int k, int n, int K, int cb, int n0, int n_slice, void* w, int ldw,
                  void* stream) {
@@ -154,15 +207,16 @@ int exl3_silu_mul(const void* g, const void* u, void* z, int64_t count, float ac
     return EXL3_OK;
 }
 
-int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* trellis, const void* suh, const void* svh,
-              int k, int n, int K, int cb, void* y, int y_dtype, int ldy, int split_k, void* stream) {
+int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* packed, const void* suh, const void* svh,
+              int k, int n, int K, int cb, void* y, int y_dtype, int ldy, void* workspace, size_t ws_bytes,
+              int split_k, void* stream) {
     EXL3_REQUIRE(cb == 2, EXL3_ERR_UNSUPPORTED, "exl3_gemv: only the mul1 codebook (cb=2) is supported");
     EXL3_REQUIRE(K >= 1 && K <= 8, EXL3_ERR_UNSUPPORTED, "exl3_gemv: K=%d not in 1..8", K);
     EXL3_REQUIRE(M >= 0 && M <= kMaxRows, EXL3_ERR_ARG, "exl3_gemv: M=%d rows (1..8 per call)", M);
     EXL3_REQUIRE(k > 0 && n > 0 && k % 128 == 0 && n % 128 == 0, EXL3_ERR_ARG,
                  "exl3_gemv: k=%d, n=%d must be multiples of 128", k, n);
-    EXL3_REQUIRE(x && trellis && svh && y, EXL3_ERR_ARG, "exl3_gemv: null pointer");
-    EXL3_REQUIRE(aligned16(trellis), EXL3_ERR_ARG, "exl3_gemv: trellis must be 16-byte aligned");
+    EXL3_REQUIRE(x && packed && svh && y, EXL3_ERR_ARG, "exl3_gemv: null pointer");
+    EXL3_REQUIRE(aligned16(packed), EXL3_ERR_ARG, "exl3_gemv: packed trellis must be 16-byte aligned");
     EXL3_REQUIRE(x_dtype == EXL3_F16 || x_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "exl3_gemv: x dtype %d", x_dtype);
     EXL3_REQUIRE(y_dtype == EXL3_F16 || y_dtype == EXL3_BF16 || y_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED,
                  "exl3_gemv: y dtype %d", y_dtype);
@@ -172,26 +226,39 @@ int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* trellis, c
                  EXL3_ERR_ARG, "exl3_gemv: x must be 8-byte and y 16-byte aligned");
     EXL3_REQUIRE(split_k >= 0 && split_k <= kMaxCluster, EXL3_ERR_ARG, "exl3_gemv: split_k=%d (0..8)", split_k);
     if (M == 0) return EXL3_OK;
+    const size_t need = exl3_gemv_workspace_size(M, k);
+    EXL3_REQUIRE(workspace && ws_bytes >= need && aligned16(workspace), EXL3_ERR_WORKSPACE,
+                 "exl3_gemv: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, need);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    __half* xf = static_cast<__half*>(workspace);
+
+    PrepArgs pa = {};
+    pa.x = x;
+    pa.ldx = ldx;
+    pa.x_bf16 = x_dtype == EXL3_BF16;
+    pa.rows = M;
+    pa.nmat = 1;
+    pa.k = k;
+    pa.suh0 = static_cast<const __half*>(suh);
+    pa.xf = xf;
+    int rc = launch_prep(pa, st, "exl3_gemv", true);
+    if (rc) return rc;
+
     GemvArgs a = {};
-    a.tr = static_cast<const uint32_t*>(trellis);
-    a.suh = static_cast<const __half*>(suh);
+    a.tr = static_cast<const uint32_t*>(packed);
     a.svh = static_cast<const __half*>(svh);
     a.K = K;
-    a.x = x;
-    a.ldx = ldx;
-    a.x_bf16 = x_dtype == EXL3_BF16;
     a.y = y;
     a.ldy = ldy;
     a.y_dtype = y_dtype;
     a.M = M;
+    a.xf = xf;
     a.k = k;
     a.n = n;
-    const int units = n / 128;
-    a.split = choose_split(units, k, 1, split_k);
     a.status = device_status_ptr();
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return a.x_bf16 ? launch_gemv<EPI_LINEAR, __nv_bfloat16>(a, units, st, "exl3_gemv")
-                    : launch_gemv<EPI_LINEAR, __half>(a, units, st, "exl3_gemv");
+    const int units = n / 128;
+    const GemvPlan pl = plan_gemv(EPI_LINEAR, units, k, 256 * K, split_k);
+    return launch_gemv<EPI_LINEAR>(a, units, pl, st, "exl3_gemv");
 }
 
 }  // extern "C"

@@ -1,19 +1,22 @@
 // MoE decode path: top-k router with residency bias, token/expert alignment, grouped gate|up and down GEMVs
 // (gemv.cuh), and the fixed-order combine.
 //
-// Workspace layout of exl3_moe_align / exl3_moe_decode (int32 words unless noted; P = valid pairs + shared rows):
-//   [0] n_items  [1] n_pairs_valid  [2..7] reserved
+// Workspace layout of exl3_moe_align / exl3_moe_decode (int32 words unless noted; P_max = pairs + shared rows):
+//   [0] n_items  [1] n_pairs_valid  [2] positions in use (valid pairs + shared rows)  [3..7] reserved
 //   item_expert[max_items] item_start[max_items] item_cnt[max_items]
-//   pair_tok[P_max] pair_of[npairs] pair_w[P_max] (fp32)
-//   then (decode only, 256-byte aligned) abuf fp16 [P_max][I], ybuf fp32 [P_max][H]
+//   pair_tok[P_max] pair_expert[P_max] pair_of[npairs] pair_w[P_max] (fp32)
+//   then (decode only, 256-byte aligned): gate|up input rows in xf order fp16 [P_max][2][H], down input rows in xf
+//   order fp16 [P_max][I], ybuf fp32 [P_max][H]
 #include "gemv.cuh"
 
 namespace exl3 {
 
-constexpr int kItemRows = 8;     // rows per GEMV work item (the MMA's N)
+// Rows per GEMV work item: the MMA's N (8), or fewer when the batch is smaller (an item never holds more rows than
+// the launch's activation buffer, which is sized for min(8, M) rows).
+inline int item_rows(int M) { return M < 8 ? (M > 0 ? M : 1) : 8; }
 
 struct WsLayout {
-    size_t item_expert, item_start, item_cnt, pair_tok, pair_of, pair_w, abuf, ybuf, total;
+    size_t item_expert, item_start, item_cnt, pair_tok, pair_expert, pair_of, pair_w, xf_gu, xf_dn, ybuf, total;
     int max_items, p_max;
 };
 
@@ -30,10 +33,12 @@ inline WsLayout ws_layout(int M, int topk, int E, int H, int I, int shared, int 
     L.item_start = o; o += (size_t)L.max_items * 4;
     L.item_cnt = o; o += (size_t)L.max_items * 4;
     L.pair_tok = o; o += (size_t)L.p_max * 4;
+    L.pair_expert = o; o += (size_t)L.p_max * 4;
     L.pair_of = o; o += (size_t)npairs * 4;
     L.pair_w = o; o += (size_t)L.p_max * 4;
     o = align_up(o, 256);
-    L.abuf = o; o += align_up((size_t)L.p_max * I * 2, 256);
+    L.xf_gu = o; o += align_up((size_t)L.p_max * 2 * H * 2, 256);
+    L.xf_dn = o; o += align_up((size_t)L.p_max * I * 2, 256);
     L.ybuf = o; o += (size_t)L.p_max * H * 4;
     L.total = o;
     return L;
@@ -211,7 +216,8 @@ __device__ __forceinline__ int block_excl_scan(int v, int* scan, int* total) {
 __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restrict__ ids, const float* __restrict__ w,
                                                          int npairs, int topk, int E, int M, int shared, int chunk,
                                                          int* ws_i, int* item_expert, int* item_start, int* item_cnt,
-                                                         int* pair_tok, int* pair_of, float* pair_w) {
+                                                         int* pair_tok, int* pair_expert, int* pair_of,
+                                                         float* pair_w) {
     extern __shared__ int sm[];
     int* cnt = sm;                             // [kAlignWarps][E]
     int* scan = sm + kAlignWarps * E;          // [kAlignThreads]
@@ -244,6 +250,7 @@ __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restri
     if (t == 0) {
         ws_i[0] = n_routed_items + shared_items;
         ws_i[1] = n_valid;
+        ws_i[2] = n_valid + (shared ? M : 0);
     }
     __syncthreads();
     // stable placement: each warp walks its segment in order, 32 pairs at a time
@@ -259,6 +266,7 @@ __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restri
             if (valid) {
                 const int pos = cnt[warp * E + e] + __popc(before);
                 pair_tok[pos] = i / topk;
+                pair_expert[pos] = e;
                 pair_w[pos] = w[i];
                 pair_of[i] = pos;
             } else {
@@ -278,6 +286,7 @@ __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restri
     if (shared) {
         for (int m = t; m < M; m += kAlignThreads) {
             pair_tok[n_valid + m] = m;
+            pair_expert[n_valid + m] = E;
             pair_w[n_valid + m] = 1.0f;
         }
         for (int c = t; c < shared_items; c += kAlignThreads) {
@@ -294,6 +303,7 @@ __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restri
 template <typename TOut>
 __global__ void k_combine(const float* __restrict__ ybuf, const int* __restrict__ pair_of, const int* ws_i, int M,
                           int H, int topk, int shared, TOut* out) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");       // ybuf comes from the down kernel
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;     // one float4 of one row
     const int per_row = H / 4;
     if (idx >= M * per_row) return;
@@ -338,6 +348,7 @@ static int launch_align(const int32_t* ids, const float* w, int M, int topk, int
                                             reinterpret_cast<int*>(ws + L.item_start),
                                             reinterpret_cast<int*>(ws + L.item_cnt),
                                             reinterpret_cast<int*>(ws + L.pair_tok),
+                                            reinterpret_cast<int*>(ws + L.pair_expert),
                                             reinterpret_cast<int*>(ws + L.pair_of),
                                             reinterpret_cast<float*>(ws + L.pair_w));
     EXL3_LAUNCH_CHECK("moe align");
@@ -366,7 +377,7 @@ int exl3_route(const float* logits, int ld, int R, int E, int kind, int k, const
 
 size_t exl3_moe_workspace_size(int M, int topk, int E, int H, int I, int shared) {
     if (M <= 0 || topk <= 0 || E <= 0) return 0;
-    return ws_layout(M, topk, E, H, I, shared, kItemRows).total;
+    return ws_layout(M, topk, E, H, I, shared, item_rows(M)).total;
 }
 
 int exl3_moe_align(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
@@ -374,8 +385,8 @@ int exl3_moe_align(const int32_t* ids, const float* w, int M, int topk, int E, i
     EXL3_REQUIRE(ids && w && M > 0 && topk > 0 && E > 0 && chunk > 0, EXL3_ERR_ARG, "exl3_moe_align: bad arguments");
     EXL3_REQUIRE(E <= 1024, EXL3_ERR_UNSUPPORTED, "exl3_moe_align: E=%d > 1024", E);
     const WsLayout L = ws_layout(M, topk, E, 128, 128, shared, chunk);
-    EXL3_REQUIRE(workspace && ws_bytes >= L.abuf, EXL3_ERR_WORKSPACE, "exl3_moe_align: workspace %zu < %zu",
-                 ws_bytes, L.abuf);
+    EXL3_REQUIRE(workspace && ws_bytes >= L.xf_gu, EXL3_ERR_WORKSPACE, "exl3_moe_align: workspace %zu < %zu",
+                 ws_bytes, L.xf_gu);
     return launch_align(ids, w, M, topk, E, shared, chunk, static_cast<uint8_t*>(workspace), L,
                         static_cast<cudaStream_t>(stream));
 }
@@ -395,12 +406,8 @@ static int moe_check(const void* x, int x_dtype, int ldx, int M, int topk, const
     return EXL3_OK;
 }
 
-static GemvArgs moe_args(const void* x, int x_dtype, int ldx, const exl3_expert* experts, float act_limit,
-                         uint8_t* ws, const WsLayout& L) {
+static GemvArgs moe_args(const exl3_expert* experts, float act_limit, uint8_t* ws, const WsLayout& L) {
     GemvArgs a = {};
-    a.x = x;
-    a.ldx = ldx;
-    a.x_bf16 = x_dtype == EXL3_BF16;
     a.experts = reinterpret_cast<const ExpertDesc*>(experts);
     a.items.n_items = reinterpret_cast<const int*>(ws);
     a.items.item_expert = reinterpret_cast<const int*>(ws + L.item_expert);
@@ -408,43 +415,64 @@ static GemvArgs moe_args(const void* x, int x_dtype, int ldx, const exl3_expert*
     a.items.item_cnt = reinterpret_cast<const int*>(ws + L.item_cnt);
     a.items.pair_tok = reinterpret_cast<const int*>(ws + L.pair_tok);
     a.items.pair_w = reinterpret_cast<const float*>(ws + L.pair_w);
-    a.abuf = reinterpret_cast<__half*>(ws + L.abuf);
     a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
     a.act_limit = act_limit;
     a.status = device_status_ptr();
     return a;
 }
 
+static int bits_hint(int max_bits) { return max_bits >= 1 && max_bits <= 8 ? max_bits : 8; }
+
 static int run_gateup(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
-                      int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes, int split_k,
-                      cudaStream_t st) {
+                      int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes, int max_bits,
+                      int split_k, cudaStream_t st) {
     int rc = moe_check(x, x_dtype, ldx, M, topk, experts, E, H, I, split_k, "exl3_moe_gateup");
     if (rc || M == 0) return rc;
     EXL3_REQUIRE(x, EXL3_ERR_ARG, "exl3_moe_gateup: null x");
-    const WsLayout L = ws_layout(M, topk, E, H, I, shared, kItemRows);
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
     EXL3_REQUIRE(workspace && ws_bytes >= L.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
                  "exl3_moe_gateup: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, L.total);
-    GemvArgs a = moe_args(x, x_dtype, ldx, experts, act_limit, static_cast<uint8_t*>(workspace), L);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    // rotated, quantised input rows of every pair position (gate and up signs of the position's expert)
+    PrepArgs pa = {};
+    pa.x = x;
+    pa.ldx = ldx;
+    pa.x_bf16 = x_dtype == EXL3_BF16;
+    pa.rows = L.p_max;
+    pa.nmat = 2;
+    pa.k = H;
+    pa.row_tok = reinterpret_cast<const int*>(ws + L.pair_tok);
+    pa.row_expert = reinterpret_cast<const int*>(ws + L.pair_expert);
+    pa.experts = reinterpret_cast<const ExpertDesc*>(experts);
+    pa.n_rows_dev = reinterpret_cast<const int*>(ws) + 2;
+    pa.xf = reinterpret_cast<__half*>(ws + L.xf_gu);
+    rc = launch_prep(pa, st, "exl3_moe_gateup", false);
+    if (rc) return rc;
+    GemvArgs a = moe_args(experts, act_limit, ws, L);
+    a.xf = pa.xf;
+    a.xf_out = reinterpret_cast<__half*>(ws + L.xf_dn);
     a.k = H;
     a.n = I;
     const int units = L.max_items * (I / 128);
-    a.split = choose_split(units, H, 2, split_k);
-    return launch_gemv<EPI_GATEUP, __half>(a, units, st, "exl3_moe_gateup");
+    const GemvPlan pl = plan_gemv(EPI_GATEUP, units, H, 512 * bits_hint(max_bits), split_k);
+    return launch_gemv<EPI_GATEUP>(a, units, pl, st, "exl3_moe_gateup");
 }
 
 static int run_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
-                    size_t ws_bytes, int split_k, cudaStream_t st) {
+                    size_t ws_bytes, int max_bits, int split_k, cudaStream_t st) {
     int rc = moe_check(nullptr, 0, 0, M, topk, experts, E, H, I, split_k, "exl3_moe_down");
     if (rc || M == 0) return rc;
-    const WsLayout L = ws_layout(M, topk, E, H, I, shared, kItemRows);
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
     EXL3_REQUIRE(workspace && ws_bytes >= L.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
                  "exl3_moe_down: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, L.total);
-    GemvArgs a = moe_args(nullptr, 0, 0, experts, 0.f, static_cast<uint8_t*>(workspace), L);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    GemvArgs a = moe_args(experts, 0.f, ws, L);
+    a.xf = reinterpret_cast<const __half*>(ws + L.xf_dn);
     a.k = I;
     a.n = H;
     const int units = L.max_items * (H / 128);
-    a.split = choose_split(units, I, 1, split_k);
-    return launch_gemv<EPI_DOWN, __half>(a, units, st, "exl3_moe_down");
+    const GemvPlan pl = plan_gemv(EPI_DOWN, units, I, 256 * bits_hint(max_bits), split_k);
+    return launch_gemv<EPI_DOWN>(a, units, pl, st, "exl3_moe_down");
 }
 
 static int run_combine(int M, int topk, int E, int shared, int H, int I, void* out, int out_dtype, void* workspace,
@@ -452,32 +480,35 @@ static int run_combine(int M, int topk, int E, int shared, int H, int I, void* o
     EXL3_REQUIRE(out && M >= 0 && topk > 0 && H % 128 == 0, EXL3_ERR_ARG, "exl3_moe_combine: bad arguments");
     EXL3_REQUIRE(out_dtype == EXL3_F16 || out_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED, "exl3_moe_combine: out dtype");
     if (M == 0) return EXL3_OK;
-    const WsLayout L = ws_layout(M, topk, E, H, I, shared, kItemRows);
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
     EXL3_REQUIRE(workspace && ws_bytes >= L.total, EXL3_ERR_WORKSPACE, "exl3_moe_combine: workspace too small");
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const float* ybuf = reinterpret_cast<const float*>(ws + L.ybuf);
     const int* pair_of = reinterpret_cast<const int*>(ws + L.pair_of);
+    const int* wi = reinterpret_cast<const int*>(ws);
     const int n4 = M * (H / 4);
+    const dim3 grid((n4 + 255) / 256);
+    cudaError_t e;
     if (out_dtype == EXL3_F32)
-        k_combine<float><<<(n4 + 255) / 256, 256, 0, st>>>(ybuf, pair_of, reinterpret_cast<const int*>(ws), M, H,
-                                                           topk, shared, static_cast<float*>(out));
+        e = launch_pdl(k_combine<float>, grid, dim3(256), 0, st, 1, ybuf, pair_of, wi, M, H, topk, shared,
+                       static_cast<float*>(out));
     else
-        k_combine<__half><<<(n4 + 255) / 256, 256, 0, st>>>(ybuf, pair_of, reinterpret_cast<const int*>(ws), M, H,
-                                                            topk, shared, static_cast<__half*>(out));
-    EXL3_LAUNCH_CHECK("exl3_moe_combine");
+        e = launch_pdl(k_combine<__half>, grid, dim3(256), 0, st, 1, ybuf, pair_of, wi, M, H, topk, shared,
+                       static_cast<__half*>(out));
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_moe_combine: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }
 
 int exl3_moe_gateup(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
-                    int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes, int split_k,
-                    void* stream) {
-    return run_gateup(x, x_dtype, ldx, M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, split_k,
-                      static_cast<cudaStream_t>(stream));
+                    int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes, int max_bits,
+                    int split_k, void* stream) {
+    return run_gateup(x, x_dtype, ldx, M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, max_bits,
+                      split_k, static_cast<cudaStream_t>(stream));
 }
 
 int exl3_moe_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
-                  size_t ws_bytes, int split_k, void* stream) {
-    return run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, split_k,
+                  size_t ws_bytes, int max_bits, int split_k, void* stream) {
+    return run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, max_bits, split_k,
                     static_cast<cudaStream_t>(stream));
 }
 
@@ -489,21 +520,22 @@ int exl3_moe_combine(int M, int topk, int E, int shared, int H, int I, void* out
 
 int exl3_moe_decode(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w, int topk,
                     const exl3_expert* experts, int E, int shared, int H, int I, float act_limit, void* out,
-                    int out_dtype, void* workspace, size_t ws_bytes, int split_k, void* stream) {
+                    int out_dtype, void* workspace, size_t ws_bytes, int max_bits, int split_k, void* stream) {
     int rc = moe_check(x, x_dtype, ldx, M, topk, experts, E, H, I, split_k, "exl3_moe_decode");
     if (rc) return rc;
     EXL3_REQUIRE(x && ids && w && out, EXL3_ERR_ARG, "exl3_moe_decode: null pointer");
     EXL3_REQUIRE(out_dtype == EXL3_F16 || out_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED, "exl3_moe_decode: out dtype");
     if (M == 0) return EXL3_OK;
-    const WsLayout L = ws_layout(M, topk, E, H, I, shared, kItemRows);
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
     EXL3_REQUIRE(workspace && ws_bytes >= L.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
                  "exl3_moe_decode: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, L.total);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    rc = launch_align(ids, w, M, topk, E, shared, kItemRows, static_cast<uint8_t*>(workspace), L, st);
+    rc = launch_align(ids, w, M, topk, E, shared, item_rows(M), static_cast<uint8_t*>(workspace), L, st);
     if (rc) return rc;
-    rc = run_gateup(x, x_dtype, ldx, M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, split_k, st);
+    rc = run_gateup(x, x_dtype, ldx, M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, max_bits,
+                    split_k, st);
     if (rc) return rc;
-    rc = run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, split_k, st);
+    rc = run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, max_bits, split_k, st);
     if (rc) return rc;
     return run_combine(M, topk, E, shared, H, I, out, out_dtype, workspace, ws_bytes, st);
 }

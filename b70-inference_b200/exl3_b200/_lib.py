@@ -34,15 +34,18 @@ _PROTOS = [
     ("exl3_device_status", i32, [i32]),
     ("exl3_dequant", i32, [vp, i32, i32, i32, i32, i32, i32, vp, i32, vp]),
     ("exl3_had_r_128", i32, [vp, vp, i32, i32, i32, vp, vp, f32, vp]),
-    ("exl3_gemv", i32, [vp, i32, i32, i32, vp, vp, vp, i32, i32, i32, i32, vp, i32, i32, i32, vp]),
+    ("exl3_pack", i32, [vp, i32, i32, i32, vp, vp]),
+    ("exl3_pack_gateup", i32, [vp, vp, i32, i32, i32, i32, vp, vp]),
+    ("exl3_gemv_workspace_size", sz, [i32, i32]),
+    ("exl3_gemv", i32, [vp, i32, i32, i32, vp, vp, vp, i32, i32, i32, i32, vp, i32, i32, vp, sz, i32, vp]),
     ("exl3_silu_mul", i32, [vp, vp, vp, i64, f32, vp]),
     ("exl3_route", i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp, f32, i32, vp, i32, vp, vp, vp]),
     ("exl3_moe_workspace_size", sz, [i32, i32, i32, i32, i32, i32]),
     ("exl3_moe_decode", i32, [vp, i32, i32, i32, vp, vp, i32, vp, i32, i32, i32, i32, f32, vp, i32, vp, sz, i32,
-                              vp]),
+                              i32, vp]),
     ("exl3_moe_align", i32, [vp, vp, i32, i32, i32, i32, i32, vp, sz, vp]),
-    ("exl3_moe_gateup", i32, [vp, i32, i32, i32, i32, vp, i32, i32, i32, i32, f32, vp, sz, i32, vp]),
-    ("exl3_moe_down", i32, [i32, i32, vp, i32, i32, i32, i32, vp, sz, i32, vp]),
+    ("exl3_moe_gateup", i32, [vp, i32, i32, i32, i32, vp, i32, i32, i32, i32, f32, vp, sz, i32, i32, vp]),
+    ("exl3_moe_down", i32, [i32, i32, vp, i32, i32, i32, i32, vp, sz, i32, i32, vp]),
     ("exl3_moe_combine", i32, [i32, i32, i32, i32, i32, i32, vp, i32, vp, sz, vp]),
 ]
 
@@ -92,6 +95,20 @@ def dtype_code(dt: torch.dtype) -> int:
     if dt not in _DTYPE:
         raise Exl3Error(f"unsupported dtype {dt}")
     return _DTYPE[dt]
+
+
+_WS: dict = {}
+
+
+def workspace(device, nbytes: int, key: str = "ws") -> torch.Tensor:
+    """A cached device byte buffer of at least nbytes (grown on demand, reused across calls on the same stream).
+    Calls that overlap on different streams must pass their own workspace."""
+    k = (str(device), key)
+    buf = _WS.get(k)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(int(nbytes), 1 << 20), dtype=torch.uint8, device=device)
+        _WS[k] = buf
+    return buf
 
 
 def require_cuda(*ts: torch.Tensor) -> None:

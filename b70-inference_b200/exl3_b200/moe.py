@@ -13,7 +13,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib as L
-from .ops import route
+from .ops import pack, pack_gateup, route
 
 ROUTE_SIGMOID, ROUTE_SOFTMAX, ROUTE_SQRT_SOFTPLUS = L.ROUTE_SIGMOID, L.ROUTE_SOFTMAX, L.ROUTE_SQRT_SOFTPLUS
 
@@ -74,13 +74,21 @@ class ExpertTable:
             raise L.Exl3Error("ExpertTable: the shared expert must have the routed intermediate size "
                               "(run a wider shared expert as its own BC_GatedMLP)")
         self.E = len(self.experts)
+        # packed copies the kernels stream: gate|up fused per 128-column block, down column-block-major
+        self.packed = []
         arr = (L.Expert * len(allx))()
         for i, ex in enumerate(allx):
+            gu = pack_gateup(ex.gate.trellis, ex.up.trellis, ex.gate.K, ex.up.K)
+            dn = pack(ex.down.trellis, ex.down.K)
+            self.packed.append((gu, dn))
+            arr[i].trellis[0] = gu.data_ptr()
+            arr[i].trellis[1] = gu.data_ptr()
+            arr[i].trellis[2] = dn.data_ptr()
             for j, m in enumerate((ex.gate, ex.up, ex.down)):
-                arr[i].trellis[j] = m.trellis.data_ptr()
                 arr[i].suh[j] = m.suh.data_ptr()
                 arr[i].svh[j] = m.svh.data_ptr()
                 arr[i].K[j] = int(m.K)
+        self.max_bits = max(int(m.K) for ex in allx for m in (ex.gate, ex.up, ex.down))
         raw = bytes(C.string_at(C.addressof(arr), C.sizeof(arr)))
         dev = device or self.experts[0].gate.trellis.device
         self.table = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(dev)
@@ -94,17 +102,6 @@ class ExpertTable:
             for m in (self.experts[e].gate, self.experts[e].up, self.experts[e].down):
                 tot += m.trellis.numel() * 2 + (m.k + m.n) * 2
         return tot
-
-
-_WS: dict = {}
-
-
-def _workspace(device, nbytes: int) -> torch.Tensor:
-    buf = _WS.get(device)
-    if buf is None or buf.numel() < nbytes:
-        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-        _WS[device] = buf
-    return buf
 
 
 def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, table: ExpertTable,
@@ -135,28 +132,29 @@ def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, t
     shared = int(table.shared is not None)
     lib = L.lib()
     need = lib.exl3_moe_workspace_size(M, k, table.E, H, table.I, shared)
-    ws = workspace if workspace is not None else _workspace(x2.device, need)
+    ws = workspace if workspace is not None else L.workspace(x2.device, need, "moe")
     st = L.stream_of(x2)
     if events is None:
         rc = lib.exl3_moe_decode(x2.data_ptr(), L.dtype_code(x2.dtype), x2.stride(0), M, ids.data_ptr(),
                                  w.data_ptr(), k, table.table.data_ptr(), table.E, shared, H, table.I,
                                  float(act_limit), out.data_ptr(), L.dtype_code(out.dtype), ws.data_ptr(), ws.numel(),
-                                 int(split_k), st)
+                                 table.max_bits, int(split_k), st)
         L.check(rc, "moe_forward")
         return out
     # the same launches one phase at a time, with CUDA events around the two GEMV kernels
-    L.check(lib.exl3_moe_align(ids.data_ptr(), w.data_ptr(), M, k, table.E, shared, 8, ws.data_ptr(), ws.numel(), st),
+    L.check(lib.exl3_moe_align(ids.data_ptr(), w.data_ptr(), M, k, table.E, shared, min(8, M), ws.data_ptr(),
+                                ws.numel(), st),
             "moe_forward align")
     ext = bool(events.get("external", False))      # event record nodes when captured in a CUDA graph
     e0, e1, e2, e3 = (torch.cuda.Event(enable_timing=True, external=ext) for _ in range(4))
     e0.record()
     L.check(lib.exl3_moe_gateup(x2.data_ptr(), L.dtype_code(x2.dtype), x2.stride(0), M, k, table.table.data_ptr(),
                                 table.E, shared, H, table.I, float(act_limit), ws.data_ptr(), ws.numel(),
-                                int(split_k), st), "moe_forward gate|up")
+                                table.max_bits, int(split_k), st), "moe_forward gate|up")
     e1.record()
     e2.record()
     L.check(lib.exl3_moe_down(M, k, table.table.data_ptr(), table.E, shared, H, table.I, ws.data_ptr(), ws.numel(),
-                              int(split_k), st), "moe_forward down")
+                              table.max_bits, int(split_k), st), "moe_forward down")
     e3.record()
     L.check(lib.exl3_moe_combine(M, k, table.E, shared, H, table.I, out.data_ptr(), L.dtype_code(out.dtype),
                                  ws.data_ptr(), ws.numel(), st), "moe_forward combine")
@@ -175,7 +173,7 @@ def moe_align(topk_ids: torch.Tensor, topk_w: torch.Tensor, E: int, shared: bool
     active = min(npairs, E)
     max_items = active + (npairs + chunk - 1) // chunk + ((M + chunk - 1) // chunk if shared else 0)
     p_max = npairs + (M if shared else 0)
-    nbytes = 32 + 4 * (3 * max_items + 2 * p_max + npairs) + 256
+    nbytes = 32 + 4 * (3 * max_items + 3 * p_max + npairs) + 256
     ws = torch.zeros(nbytes + 4096, dtype=torch.uint8, device=ids.device)
     rc = L.lib().exl3_moe_align(ids.data_ptr(), w.data_ptr(), M, k, E, int(shared), chunk, ws.data_ptr(), ws.numel(),
                                 L.stream_of(ids))
@@ -186,11 +184,14 @@ def moe_align(topk_ids: torch.Tensor, topk_w: torch.Tensor, E: int, shared: bool
     item_start = wi[o:o + max_items]; o += max_items
     item_cnt = wi[o:o + max_items]; o += max_items
     pair_tok = wi[o:o + p_max]; o += p_max
+    pair_expert = wi[o:o + p_max]; o += p_max
     pair_of = wi[o:o + npairs]; o += npairs
     pair_w = wi[o:o + p_max].view(torch.float32)
     n_items = int(wi[0])
     n_valid = int(wi[1])
-    return dict(n_items=n_items, n_valid=n_valid, item_expert=item_expert[:n_items].clone(),
+    n_pos = n_valid + (M if shared else 0)
+    return dict(n_items=n_items, n_valid=n_valid, pair_expert=pair_expert[:n_pos].clone(),
+                item_expert=item_expert[:n_items].clone(),
                 item_start=item_start[:n_items].clone(), item_cnt=item_cnt[:n_items].clone(),
                 pair_tok=pair_tok[:n_valid + (M if shared else 0)].clone(), pair_of=pair_of.clone(),
                 pair_w=pair_w[:n_valid + (M if shared else 0)].clone())

@@ -23,15 +23,42 @@ def _f16(t: torch.Tensor) -> torch.Tensor:
 
 # ----------------------------------------------------------------------------------------------- EXL3 linear
 
-def exl3_gemv(x: torch.Tensor, trellis: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
-              y: torch.Tensor, split_k: int = 0) -> None:
-    """y[M, n] = Had(Had(x * suh) @ W_hat) * svh for M <= 8 rows; y fp16/bf16/fp32 preallocated (C ABI exl3_gemv)."""
-    L.require_cuda(x, trellis, y)
+def pack(trellis: torch.Tensor, K: int) -> torch.Tensor:
+    """exllamav3 trellis [k/16, n/16, 16K] int16 -> the GEMV's column-block-major layout (same bytes, permuted)."""
+    L.require_cuda(trellis)
+    tr = trellis.contiguous()
+    k, n = tr.shape[0] * 16, tr.shape[1] * 16
+    out = torch.empty(n // 128, k // 16, 8 * 16 * int(K), dtype=torch.int16, device=tr.device)
+    L.check(L.lib().exl3_pack(tr.data_ptr(), k, n, int(K), out.data_ptr(), L.stream_of(tr)), "exl3_pack")
+    return out
+
+
+def pack_gateup(gate: torch.Tensor, up: torch.Tensor, Kg: int, Ku: int) -> torch.Tensor:
+    """Fused gate|up packing: [I/128, H/16, 8 gate tiles | 8 up tiles] (int16 view)."""
+    L.require_cuda(gate, up)
+    g, u = gate.contiguous(), up.contiguous()
+    H, I = g.shape[0] * 16, g.shape[1] * 16
+    if u.shape[0] * 16 != H or u.shape[1] * 16 != I:
+        raise L.Exl3Error("pack_gateup: gate and up shapes differ")
+    out = torch.empty(I // 128, H // 16, 8 * 16 * (int(Kg) + int(Ku)), dtype=torch.int16, device=g.device)
+    L.check(L.lib().exl3_pack_gateup(g.data_ptr(), u.data_ptr(), H, I, int(Kg), int(Ku), out.data_ptr(),
+                                     L.stream_of(g)), "exl3_pack_gateup")
+    return out
+
+
+def exl3_gemv(x: torch.Tensor, packed: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
+              y: torch.Tensor, split_k: int = 0, workspace: torch.Tensor | None = None) -> None:
+    """y[M, n] = Had(Had(x * suh) @ W_hat) * svh for M <= 8 rows; packed = pack(trellis, K); y fp16/bf16/fp32
+    preallocated (C ABI exl3_gemv)."""
+    L.require_cuda(x, packed, y)
     M, k = x.shape
     n = svh.shape[0]
-    rc = L.lib().exl3_gemv(x.data_ptr(), L.dtype_code(x.dtype), x.stride(0), M, trellis.data_ptr(),
-                           L.ptr(suh), svh.data_ptr(), k, n, int(K), 2, y.data_ptr(), L.dtype_code(y.dtype),
-                           y.stride(0), int(split_k), L.stream_of(x))
+    lib = L.lib()
+    need = lib.exl3_gemv_workspace_size(M, k)
+    ws = workspace if workspace is not None else L.workspace(x.device, need, "gemv")
+    rc = lib.exl3_gemv(x.data_ptr(), L.dtype_code(x.dtype), x.stride(0), M, packed.data_ptr(), L.ptr(suh),
+                       svh.data_ptr(), k, n, int(K), 2, y.data_ptr(), L.dtype_code(y.dtype), y.stride(0),
+                       ws.data_ptr(), ws.numel(), int(split_k), L.stream_of(x))
     L.check(rc, "exl3_gemv")
 
 
@@ -103,6 +130,13 @@ class BC_LinearEXL3:
         self.out_features = trellis.shape[1] * 16
         if trellis.shape[2] != 16 * self.Ki:
             raise L.Exl3Error(f"BC_LinearEXL3: trellis {tuple(trellis.shape)} does not match K={K}")
+        # the decode GEMV reads a column-block-major copy of the trellis (packed once, on first use)
+        self._packed = None
+
+    def packed(self) -> torch.Tensor:
+        if self._packed is None or self._packed.device != self.trellis.device:
+            self._packed = pack(self.trellis, self.Ki)
+        return self._packed
 
     def run(self, x: torch.Tensor, y: torch.Tensor) -> None:
         x2 = _f16(x.reshape(-1, self.in_features))
@@ -111,8 +145,9 @@ class BC_LinearEXL3:
         if M == 0:
             return
         if M <= SMALL_M_MAX:
+            pk = self.packed()
             for m0 in range(0, M, 8):
-                exl3_gemv(x2[m0:m0 + 8], self.trellis, self.suh, self.svh, self.Ki, y2[m0:m0 + 8])
+                exl3_gemv(x2[m0:m0 + 8], pk, self.suh, self.svh, self.Ki, y2[m0:m0 + 8])
         else:
             self._run_recon(x2, y2)
         if self.bias is not None:

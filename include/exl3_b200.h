@@ -45,12 +45,13 @@ extern "C" {
 #define EXL3_ROUTE_SQRT_SOFTPLUS 2 /* DeepSeek-V4 sqrt(softplus): dsv41/xpu/csrc/dsv_moe_glue.sycl:155-193 */
 
 /* One expert's three EXL3 matrices (device addresses). The shared expert is an ordinary entry.
+ * trellis[0] = gate|up packed by exl3_pack_gateup, trellis[1] unused, trellis[2] = down packed by exl3_pack.
  * Replaces the int64 pointer tables of exllamav3's BC_BlockSparseMLP / exl3_mgemm
  * (glm/docs/ext-op-inventory.md:1018-1024,1104-1120) and the per-expert blob of
  * glm/xpu/csrc/exl3_moe.n128.sycl:3-13 (K may differ per matrix, as the DSV piece tables allow,
  * dsv41/xpu/csrc/dsv_moe.sycl:24-143). */
 typedef struct exl3_expert {
-    const void* trellis[3]; /* gate, up, down: int16 [k/16][n/16][16K]; gate/up k = hidden, n = interm */
+    const void* trellis[3]; /* packed gate|up, (unused), packed down; gate/up k = hidden, n = interm */
     const void* suh[3];     /* fp16 [k] */
     const void* svh[3];     /* fp16 [n] */
     int32_t K[3];           /* bits per weight, 1..8 */
@@ -78,14 +79,29 @@ EXL3_API int exl3_dequant(const void* trellis, int k, int n, int K, int cb, int 
 EXL3_API int exl3_had_r_128(const void* in, void* out, int dtype, int rows, int cols, const void* pre, const void* post,
                    float scale, void* stream);
 
+/* ---- packed trellis layout ----
+ * The GEMV kernels read weights column-block-major: for each 128-column block cb and tile-row r (16 input rows) the
+ * 8 tiles of the block are contiguous, [n/128][k/16][8 tiles][8K words] (a fused gate|up pair: [I/128][H/16]
+ * [8 gate tiles | 8 up tiles]), so that each CTA streams one contiguous slice with large TMA bulk copies. It is a
+ * byte permutation of the exllamav3 layout, made once at load time, like the reference's expert blob packing
+ * (pack_expert / planar4, glm/xpu/exl3xpu/moe_offload.py:68-94). out must not alias the input. */
+EXL3_API int exl3_pack(const void* trellis, int k, int n, int K, void* out, void* stream);
+EXL3_API int exl3_pack_gateup(const void* gate, const void* up, int H, int I, int Kg, int Ku, void* out,
+                              void* stream);
+
 /* ---- EXL3 linear, decode sizes ----
- * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for M <= 8 rows (larger M: call per 8-row chunk, or use
- * exl3_grouped_gemm); x fp16 or bf16 (x_dtype), y fp16/bf16/fp32 (y_dtype) with row strides ldx, ldy.
- * k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2. split_k = CTAs per cluster along k (0 = auto).
+ * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for M <= 8 rows (larger M: call per 8-row chunk, or use the
+ * reconstruct + GEMM path); x fp16 or bf16 (x_dtype), y fp16/bf16/fp32 (y_dtype) with row strides ldx, ldy.
+ * packed = the weights in the packed layout (exl3_pack). k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2.
+ * workspace >= exl3_gemv_workspace_size(M, k) bytes (the rotated input rows). split_k = CTAs per cluster along k
+ * (0 = auto). Weights are decoded to the reference's fp16 values bit for bit and multiplied with fp32
+ * accumulation; results differ from the reference only by summation order.
  * Replaces exl3_gemm_small (glm/xpu/csrc/exl3_ops.sycl:258-321) / exllamav3 exl3_gemm
  * (glm/docs/ext-op-inventory.md:498-557) as called by BC_LinearEXL3.run (glm/xpu/glm_xpu/ops.py:60-80). */
-EXL3_API int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* trellis, const void* suh, const void* svh,
-              int k, int n, int K, int cb, void* y, int y_dtype, int ldy, int split_k, void* stream);
+EXL3_API size_t exl3_gemv_workspace_size(int M, int k);
+EXL3_API int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* packed, const void* suh,
+                       const void* svh, int k, int n, int K, int cb, void* y, int y_dtype, int ldy, void* workspace,
+                       size_t ws_bytes, int split_k, void* stream);
 
 /* ---- activation ----
  * z = fp16(min(silu(g), L) * clamp(u, -L, L)), L = act_limit (0 disables the clamps); fp32 math.
@@ -114,24 +130,25 @@ EXL3_API int exl3_route(const float* logits, int ld, int R, int E, int kind, int
  * x fp16/bf16 [M][H] (row stride ldx); ids int32 [M][topk] (ids < 0 or >= E skipped); w fp32 [M][topk];
  * experts: device array of E (+1 shared) exl3_expert. H % 128 == 0, I % 128 == 0.
  * Each expert is read once per call whatever number of rows picked it (rows grouped 8 per work item).
+ * max_bits = the largest K of any expert matrix (sizes the launch; 0 = assume 8).
  * Replaces exl3xpu_moe::moe_forward (glm/xpu/csrc/exl3_moe.n128.sycl:1338-1439) and exllamav3
  * BC_BlockSparseMLP::run_bszN (glm/docs/ext-op-inventory.md:1030-1041). */
 EXL3_API size_t exl3_moe_workspace_size(int M, int topk, int E, int H, int I, int shared);
 EXL3_API int exl3_moe_decode(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w, int topk,
                     const exl3_expert* experts, int E, int shared, int H, int I, float act_limit, void* out,
-                    int out_dtype, void* workspace, size_t ws_bytes, int split_k, void* stream);
+                    int out_dtype, void* workspace, size_t ws_bytes, int max_bits, int split_k, void* stream);
 
 /* The phases of exl3_moe_decode as separate launches on one workspace, in order: exl3_moe_align (below),
  * exl3_moe_gateup (gate|up GEMVs + activation + down-input rotation -> activation rows in the workspace),
  * exl3_moe_down (down GEMVs x routing weight -> per-pair rows), exl3_moe_combine (fixed-order sum into out).
- * Same arguments and constraints as exl3_moe_decode; exl3_moe_align must use chunk = 8.
+ * Same arguments and constraints as exl3_moe_decode; exl3_moe_align must use chunk = min(8, M).
  * Replace the reference's GateUpKernel / DownKernel / CombineKernel launches
  * (glm/xpu/csrc/exl3_moe.n128.sycl:736-790,1418-1438). */
 EXL3_API int exl3_moe_gateup(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
-                             int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes, int split_k,
-                             void* stream);
+                             int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes,
+                             int max_bits, int split_k, void* stream);
 EXL3_API int exl3_moe_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I,
-                           void* workspace, size_t ws_bytes, int split_k, void* stream);
+                           void* workspace, size_t ws_bytes, int max_bits, int split_k, void* stream);
 EXL3_API int exl3_moe_combine(int M, int topk, int E, int shared, int H, int I, void* out, int out_dtype,
                               void* workspace, size_t ws_bytes, void* stream);
 

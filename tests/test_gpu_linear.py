@@ -54,6 +54,20 @@ def test_dequant_bitexact(K):
     assert (wbuf[:, 128:] == 0).all()
 
 
+@pytest.mark.parametrize("K", [1, 3, 8])
+def test_pack_is_the_column_block_permutation(K):
+    rng = np.random.default_rng(K)
+    k, n = 64, 384
+    tr = O.random_trellis(rng, k, n, K)
+    pk = ops.pack(to_dev(tr), K).cpu().numpy().view(np.uint16)
+    exp = tr.reshape(k // 16, n // 128, 8 * 16 * K).transpose(1, 0, 2)
+    assert np.array_equal(pk.reshape(exp.shape), exp)
+    tr2 = O.random_trellis(rng, k, n, 2)
+    gu = ops.pack_gateup(to_dev(tr), to_dev(tr2), K, 2).cpu().numpy().view(np.uint16)
+    exp2 = np.concatenate([exp, tr2.reshape(k // 16, n // 128, 8 * 32).transpose(1, 0, 2)], axis=2)
+    assert np.array_equal(gu.reshape(exp2.shape), exp2)
+
+
 @pytest.mark.parametrize("K", range(1, 9))
 def test_dequant_golden(K):
     d = np.load(os.path.join(G, f"w_hat_K{K}.npz"))
@@ -95,7 +109,7 @@ def test_gemv_matches_oracle(K, M):
     x = rng.standard_normal((M, k)).astype(np.float16)
     for y_dt, np_dt in ((torch.float32, np.float32), (torch.float16, np.float16)):
         y = torch.empty((M, n), dtype=y_dt, device=DEV)
-        ops.exl3_gemv(to_dev(x), to_dev(tr), to_dev(suh), to_dev(svh), K, y)
+        ops.exl3_gemv(to_dev(x), ops.pack(to_dev(tr), K), to_dev(suh), to_dev(svh), K, y)
         ref = O.exl3_linear(x, tr, suh, svh, K, np_dt)
         assert_close(y.float().cpu().numpy(), ref.astype(np.float32), what=f"gemv K={K} M={M} {y_dt}")
 
@@ -107,10 +121,11 @@ def test_gemv_split_k_is_consistent(split):
     tr, suh, svh = rand_linear(rng, k, n, K)
     x = rng.standard_normal((M, k)).astype(np.float16)
     y = torch.empty((M, n), dtype=torch.float32, device=DEV)
-    ops.exl3_gemv(to_dev(x), to_dev(tr), to_dev(suh), to_dev(svh), K, y, split_k=split)
+    pk = ops.pack(to_dev(tr), K)
+    ops.exl3_gemv(to_dev(x), pk, to_dev(suh), to_dev(svh), K, y, split_k=split)
     assert_close(y.cpu().numpy(), O.exl3_linear(x, tr, suh, svh, K, np.float32), what=f"split {split}")
     y2 = torch.empty_like(y)
-    ops.exl3_gemv(to_dev(x), to_dev(tr), to_dev(suh), to_dev(svh), K, y2, split_k=split)
+    ops.exl3_gemv(to_dev(x), pk, to_dev(suh), to_dev(svh), K, y2, split_k=split)
     assert torch.equal(y, y2), "fixed-order split-K reduction must be deterministic"
 
 
@@ -120,7 +135,7 @@ def test_gemv_bf16_input_and_output():
     tr, suh, svh = rand_linear(rng, k, n, K)
     xb = torch.randn((M, k), generator=torch.Generator().manual_seed(3)).to(torch.bfloat16)
     y = torch.empty((M, n), dtype=torch.bfloat16, device=DEV)
-    ops.exl3_gemv(xb.to(DEV), to_dev(tr), to_dev(suh), to_dev(svh), K, y)
+    ops.exl3_gemv(xb.to(DEV), ops.pack(to_dev(tr), K), to_dev(suh), to_dev(svh), K, y)
     ref = O.exl3_linear(xb.float().numpy(), tr, suh, svh, K, np.float32)
     assert_close(y.float().cpu().numpy(), ref, rel_tol=5e-3, what="bf16")     # bf16 output rounding (8 bits)
 
@@ -171,7 +186,7 @@ def test_gemv_full_size_against_torch(k, n, K):
     svh = (torch.randint(0, 2, (n,), device=DEV, generator=g) * 2 - 1).half()
     x = torch.randn((4, k), device=DEV, generator=g).half()
     y = torch.empty((4, n), dtype=torch.float32, device=DEV)
-    ops.exl3_gemv(x, tr, suh, svh, K, y)
+    ops.exl3_gemv(x, ops.pack(tr, K), suh, svh, K, y)
     W = torch.empty((k, n), dtype=torch.half, device=DEV)
     ops.exl3_reconstruct(tr, W, 0, K)
     xh = torch.empty_like(x)

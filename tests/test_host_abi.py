@@ -32,32 +32,44 @@ def test_version_and_error_text():
 
 def test_argument_validation_returns_status_codes():
     lib = L.lib()
+
+    def gemv(x=16, M=1, packed=16, k=128, n=128, K=3, cb=2, ws=16, ws_bytes=1 << 20, split=0):
+        return lib.exl3_gemv(x, 0, k, M, packed, 16, 16, k, n, K, cb, 16, 0, n, ws, ws_bytes, split, None)
+
     # codebook other than mul1
-    assert lib.exl3_gemv(16, 0, 128, 1, 16, 16, 16, 128, 128, 3, 1, 16, 0, 128, 0, None) == L.EXL3_ERR_UNSUPPORTED
+    assert gemv(cb=1) == L.EXL3_ERR_UNSUPPORTED
     assert b"mul1" in lib.exl3_last_error()
     # K out of range
     assert lib.exl3_dequant(16, 128, 128, 9, 2, 0, 128, 16, 128, None) == L.EXL3_ERR_UNSUPPORTED
+    assert gemv(K=0) == L.EXL3_ERR_UNSUPPORTED
     # k not a multiple of 128
-    assert lib.exl3_gemv(16, 0, 128, 1, 16, 16, 16, 100, 128, 3, 2, 16, 0, 128, 0, None) == L.EXL3_ERR_ARG
+    assert gemv(k=100) == L.EXL3_ERR_ARG
     # too many rows per call
-    assert lib.exl3_gemv(16, 0, 128, 9, 16, 16, 16, 128, 128, 3, 2, 16, 0, 128, 0, None) == L.EXL3_ERR_ARG
-    # misaligned trellis
-    assert lib.exl3_gemv(16, 0, 128, 1, 18, 16, 16, 128, 128, 3, 2, 16, 0, 128, 0, None) == L.EXL3_ERR_ARG
+    assert gemv(M=9) == L.EXL3_ERR_ARG
+    # misaligned packed weights
+    assert gemv(packed=18) == L.EXL3_ERR_ARG
+    # workspace missing or too small
+    assert gemv(ws=0) == L.EXL3_ERR_WORKSPACE
+    assert gemv(ws_bytes=16) == L.EXL3_ERR_WORKSPACE
     # dequant slice outside the matrix
     assert lib.exl3_dequant(16, 128, 128, 3, 2, 64, 128, 16, 128, None) == L.EXL3_ERR_ARG
+    # packing: n must be a multiple of 128, output must not alias
+    assert lib.exl3_pack(16, 128, 64, 3, 32, None) == L.EXL3_ERR_ARG
+    assert lib.exl3_pack(16, 128, 128, 3, 16, None) == L.EXL3_ERR_ARG
     # router: too many experts, k > E
     assert lib.exl3_route(16, 2048, 1, 2048, 0, 8, None, None, None, 1.0, 1, 16, 0, 16, None, None) == \
         L.EXL3_ERR_UNSUPPORTED
     assert lib.exl3_route(16, 4, 1, 4, 0, 8, None, None, None, 1.0, 1, 16, 0, 16, None, None) == L.EXL3_ERR_ARG
     # MoE: missing workspace
-    assert lib.exl3_moe_decode(16, 0, 128, 1, 16, 16, 2, 16, 4, 0, 128, 128, 0.0, 16, 2, None, 0, 0, None) == \
+    assert lib.exl3_moe_decode(16, 0, 128, 1, 16, 16, 2, 16, 4, 0, 128, 128, 0.0, 16, 2, None, 0, 0, 0, None) == \
         L.EXL3_ERR_WORKSPACE
     # zero rows is a no-op
-    assert lib.exl3_gemv(16, 0, 128, 0, 16, 16, 16, 128, 128, 3, 2, 16, 0, 128, 0, None) == L.EXL3_OK
+    assert gemv(M=0) == L.EXL3_OK
 
 
 def test_workspace_size_grows_with_batch():
     lib = L.lib()
+    assert 0 < lib.exl3_gemv_workspace_size(1, 4096) < lib.exl3_gemv_workspace_size(8, 4096)
     a = lib.exl3_moe_workspace_size(1, 10, 512, 2048, 512, 0)
     b = lib.exl3_moe_workspace_size(4, 10, 512, 2048, 512, 1)
     assert 0 < a < b
@@ -71,6 +83,8 @@ def test_ops_refuse_cpu_tensors():
     with pytest.raises(L.Exl3Error):
         ops.exl3_gemv(x, tr, torch.ones(128, dtype=torch.half), torch.ones(128, dtype=torch.half), 3,
                       torch.zeros(1, 128, dtype=torch.half))
+    with pytest.raises(L.Exl3Error):
+        ops.pack(tr, 3)
     with pytest.raises(L.Exl3Error):
         ops.route(torch.zeros(1, 16), 0, 2)
 
