@@ -1,5 +1,5 @@
 // Shared host/device helpers for the EXL3 B200 library: status codes, error text, launch checks, small PTX
-// wrappers (mbarrier, bulk copy, cluster barrier) used by several kernels.
+// wrappers (mbarrier, bulk copy) used by several kernels.
 #pragma once
 
 #include <cuda.h>
@@ -36,6 +36,7 @@ void set_error(const char* fmt, ...);
     } while (0)
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 // Number of SMs of the current device (cached per device).
 int num_sms();
@@ -100,29 +101,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
         : "memory");
-}
-
-// ---- cluster helpers ----
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-// Address of the same shared variable in CTA `rank` of this cluster (shared::cluster window).
-__device__ __forceinline__ uint32_t map_shared_rank(const void* p, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ float4 ld_dsmem_f4(uint32_t addr) {
-    float4 v;
-    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr));
-    return v;
 }
 
 // Record a device-side failure (first writer wins) in a status word the host reads back.

@@ -1,13 +1,25 @@
-// Fused EXL3 decode GEMV for B200 (sm_100a).
+// Fused EXL3 decode GEMV for B200 (sm_100a), persistent stream-K schedule.
 //
 // Weights use the column-block-major trellis layout of this library ("packed"): for every 128-column block cb and
 // tile-row r (16 input rows) the 8 tiles of that block are contiguous, [n/128][k/16][8 tiles][8K words]; a fused
 // gate|up pair stores both matrices' 8 tiles per (cb, r), [I/128][H/16][gate 8 tiles | up 8 tiles]. It is a
 // permutation of exllamav3's [k/16][n/16][16K] int16 trellis (same bytes), made once at load time (exl3_pack), so
-// that the slice one CTA streams, (cb, tile-rows r0..r1), is ONE contiguous range: the producer moves it with a few
-// large TMA bulk copies (cp.async.bulk, 8 KB stages, up to 128 KB in flight per CTA; no tensor maps, no multicast).
+// that any run of k-blocks of one column block is ONE contiguous range: a producer moves it with large TMA bulk
+// copies (cp.async.bulk, 8 KB stages; no tensor maps, no multicast).
 //
-// Activations arrive pre-rotated in "xf" order (exl3 prep kernel, or the gate|up epilogue for the down projection):
+// Schedule. A unit is (work item, 128-column block): the dense linear has n/128 units, a MoE launch one per
+// (expert item, column block). The launch's work is units x k-blocks (128 input rows each), laid out unit-major and
+// cut into equal contiguous ranges, one per CTA (one CTA per SM). In a CTA one producer warp streams the range through
+// a 16-stage shared-memory ring to 20 consumer warps: five sub-groups of four warps take the stages in turn, the four
+// warps of a sub-group covering all tiles of each tile-row; the shared ring keeps the sub-groups within a few
+// stages of each other. At the end of each segment the consumers park their accumulators in one of two shared-memory
+// slots and go on decoding; four epilogue warps sum them, reduce split units and run the epilogue. A CTA that covers a whole unit
+// finishes it on the spot; units shared by several CTAs are reduced through global memory: each contributor stores
+// its fp32 partial, and the contributor whose atomic ticket completes the count sums all partials in CTA order (a
+// fixed order: results do not depend on timing) and runs the epilogue. No CTA ever waits for another, and every SM
+// has work until the last k-block, whatever the number of units.
+//
+// Activations arrive pre-rotated in "xf" order (prep kernels, or the gate|up epilogue for the down projection):
 // a = fp16(H(fp16(x*suh))/sqrt(128)) (exllamav3's roundings), stored per (row, 16-input tile-row) as 4 quads x 4 fp16
 // {a[2q], a[2q+1], a[2q+8], a[2q+9]}: exactly the two registers of the m16n8k16 MMA B fragment of lane quad q.
 //
@@ -15,25 +27,16 @@
 // dp4a = fp16 bits of 1024 + bytesum, then fma.rn.f16x2 with the fp16 constants 0x1EEE / 0xC931: the reference's fp16
 // weight, bit for bit, written straight into the MMA A fragment (the EXL3 position order is that fragment's layout:
 // lane 4g+q owns positions 8l..8l+7, so no shuffles). One m16n8k16 MMA per 16x16 tile accumulates in fp32; batch
-// rows ride in the MMA's 8 columns, so rows 1..8 cost the same decode. On sm_100 the legacy MMA issue cost per tile
-// is what matters: one fp16 MMA per tile stays far from the tensor pipe's limit.
+// rows ride in the MMA's 8 columns, so rows 1..8 cost the same decode.
 //
-// One CTA = work unit (item x 128-column block x split-K part), made of KI independent k-groups; group ki streams a
-// contiguous, block-aligned share of the CTA's tile-rows:
-//   warp 0 of a group  (producer) streams its share into its part of the shared-memory ring;
-//   warps 1..          consumers, one per tile group (TPW tiles of one matrix): decode, int8 MMAs, fold int32 -> fp32
-//                      at every 128-block boundary with the block scales;
-//   epilogue           fixed-order sum over the groups and over the cluster's split-K CTAs (distributed shared
-//                      memory), then
-//                      the output Hadamard x svh (linear), the gated-MLP activation + the down projection's input
-//                      (MoE gate|up), or Hadamard x svh x routing weight (MoE down).
-// Launched with programmatic stream serialization: the producer starts streaming weights while the previous kernel
-// finishes; consumers execute griddepcontrol.wait before reading activations.
+// Epilogues: the output Hadamard x svh (linear), the gated-MLP activation + the down projection's input rotation
+// (MoE gate|up), or Hadamard x svh x routing weight (MoE down).
+// Launched with programmatic stream serialization: producers start streaming weights while the previous kernel
+// finishes; consumers execute griddepcontrol.wait before reading activations or touching the reduction state.
 //
-// Reference semantics: exllamav3 exl3_gemm (glm/docs/ext-op-inventory.md:498-557; its int8-activation GEMV,
-// :539-549, uses the same byte-sum identity on dp4a), the XPU GemvKernel/HadIn/HadOut (glm/xpu/csrc/exl3_esimd.h:
-// 283-338,444-580) and the MoE GateUp/Down kernels (glm/xpu/csrc/exl3_moe.n128.sycl:136-383). Work partition, the
-// tensor-core byte sum, the packed layout and the data movement are this file's own.
+// Reference semantics: exllamav3 exl3_gemm (glm/docs/ext-op-inventory.md:498-557), the XPU GemvKernel/HadIn/HadOut
+// (glm/xpu/csrc/exl3_esimd.h:283-338,444-580) and the MoE GateUp/Down kernels (glm/xpu/csrc/exl3_moe.n128.sycl:
+// 136-383). Work partition, the packed layout and the data movement are this file's own.
 #pragma once
 
 #include "common.cuh"
@@ -44,19 +47,20 @@ namespace exl3 {
 
 enum { EPI_LINEAR = 0, EPI_GATEUP = 1, EPI_DOWN = 2 };
 
-constexpr int kTilesPerCta = 8;     // 128 output columns per matrix per CTA (one Hadamard block)
-constexpr int kMaxRows = 8;         // MMA N dimension: input rows per CTA
-constexpr int kMaxCluster = 8;      // split-K CTAs per cluster (portable cluster size)
+constexpr int kTilesPerMat = 8;     // 128 output columns per unit and matrix (one Hadamard block)
+constexpr int kMaxRows = 8;         // MMA N dimension: input rows per unit
 constexpr int kStageBytes = 8192;   // ring stage (one bulk copy)
-constexpr int kMaxStages = 16;      // up to 128 KB in flight per CTA
-constexpr int kMaxWarps = 28;       // warps of a one-CTA-per-SM launch (KI groups of 1 producer + tile-group consumers)
+constexpr int kStages = 16;         // ring stages per CTA (128 KB in flight)
+constexpr int kConsumers = 4;       // consumer warps that cover one tile-row (all tiles of all matrices)
+constexpr int kSub = 5;             // consumer sub-groups; sub-group j takes ring stages j, j + kSub, ...
+constexpr int kConsumerWarps = kSub * kConsumers;
+constexpr int kEpilogueWarps = 4;   // reduce and finish units while the consumers decode the next segment
+constexpr int kGemvThreads = (1 + kConsumerWarps + kEpilogueWarps) * 32;   // producer, consumers, epilogue
 
-__host__ __device__ constexpr int tiles_per_warp(int) { return 2; }
 __host__ __device__ constexpr int nmat_of(int epi) { return epi == EPI_GATEUP ? 2 : 1; }
-__host__ __device__ constexpr int tile_groups(int epi) { return nmat_of(epi) * kTilesPerCta / tiles_per_warp(epi); }
-// k-groups per CTA: independent pipelines (producer warp + one consumer warp per tile group), each streaming its own
-// contiguous, block-aligned share of the CTA's tile-rows through its own part of the ring
-__host__ __device__ constexpr int max_ki(int epi) { return kMaxWarps / (tile_groups(epi) + 1); }
+__host__ __device__ constexpr int tiles_per_warp(int epi) { return nmat_of(epi) * kTilesPerMat / kConsumers; }
+// floats of one unit's accumulators (also one partial slot): [nmat][kMaxRows][128]
+__host__ __device__ constexpr int unit_floats(int epi) { return nmat_of(epi) * kMaxRows * 128; }
 
 // Expert descriptor (device table, one entry per expert; the shared expert is an ordinary entry).
 // tr[0] = packed gate|up [I/128][H/16][8 gate tiles | 8 up tiles], tr[1] unused, tr[2] = packed down.
@@ -68,14 +72,15 @@ struct ExpertDesc {
     int pad;
 };
 
-// Grouped work produced by the alignment kernel: item i covers pair positions [start, start + cnt) of expert e.
+// Grouped work produced by the alignment step: item i covers pair positions [start, start + cnt) of expert e.
+// Written by the preceding kernel before it triggers this launch; read with L2 loads.
 struct ItemTable {
     const int* n_items;      // [1]
     const int* item_expert;  // [max_items]
     const int* item_start;   // [max_items]
-    const int* item_cnt;     // [max_items], 1..rows_max
-    const int* pair_tok;     // [pairs] token of a pair position
-    const float* pair_w;     // [pairs] routing weight of a pair position
+    const int* item_cnt;     // [max_items], 1..kMaxRows
+    const int* pair_src;     // [positions] gate|up activation row of a pair position
+    const float* pair_w;     // [positions] routing weight of a pair position
 };
 
 struct GemvArgs {
@@ -90,34 +95,34 @@ struct GemvArgs {
     // EPI_GATEUP / EPI_DOWN: grouped experts
     const ExpertDesc* experts;
     ItemTable items;
-    float* ybuf;            // [pairs, H] fp32 weighted down outputs
+    float* ybuf;            // [positions, H] fp32 weighted down outputs
     float act_limit;
-    // activations in xf order: input rows (linear: row m; gate|up: pair position x matrix; down: pair position)
-    const __half* xf;       // [rows][nmat][k] (k in xf order within each tile-row)
-    __half* xf_out;         // gate|up only: the down input in xf order [pairs][I]
+    // activations in xf order: linear: [M][k]; gate|up: [rows][2][k] (row = pair_src of a position); down: [pos][k]
+    const __half* xf;
+    __half* xf_out;         // gate|up only: the down input in xf order [positions][I]
     // shape of the matrices this launch runs (gate|up: k = H, n = I; down: k = I, n = H)
     int k, n;
-    int split;              // CTAs per cluster along k
-    int stages;             // ring stages (<= kMaxStages)
+    float* partial;         // [2 gridDim.x][unit_floats] split-unit partial sums
+    int* counters;          // [units] tickets, zero before the launch, left zero after it
     int* status;
 };
 
-__host__ __device__ __forceinline__ int klen_alloc_of(int k, int split) {
-    const int KB = k / 128;
-    return ((KB + split - 1) / split) * 128;
-}
-
-// Dynamic shared memory: red [KI][nmat][8][128] fp32 at offset 0 (the same in every CTA of a cluster, read through
-// distributed shared memory), bars full/empty [kMaxStages] each, then the ring [stages][kStageBytes].
+// Dynamic shared memory: red [2][kSub][unit_floats] fp32 (per sub-group accumulators of two segments in flight),
+// bars full/empty [kStages] + acc_full/acc_empty [2], the ticket flag, the ring [kStages][kStageBytes], then the
+// descriptors of the CTA's first kMaxSeg segments.
+constexpr int kMaxSeg = 64;
+constexpr int kDescBytes = 128;     // >= sizeof(UnitInfo<any>)
 struct Smem {
-    int red_off, bar_off, ring_off, total;
+    int red_off, bar_off, flag_off, ring_off, desc_off, total;
 };
-__host__ __device__ __forceinline__ Smem smem_layout(int epi, int KI, int stages) {
+__host__ __device__ __forceinline__ Smem smem_layout(int epi) {
     Smem s;
     s.red_off = 0;
-    s.bar_off = KI * nmat_of(epi) * kMaxRows * 128 * 4;
-    s.ring_off = (s.bar_off + 2 * kMaxStages * 8 + 127) & ~127;
-    s.total = s.ring_off + stages * kStageBytes;
+    s.bar_off = 2 * kSub * unit_floats(epi) * 4;
+    s.flag_off = s.bar_off + (2 * kStages + 4) * 8;
+    s.ring_off = (s.flag_off + 16 + 127) & ~127;
+    s.desc_off = s.ring_off + kStages * kStageBytes;
+    s.total = s.desc_off + kMaxSeg * kDescBytes;
     return s;
 }
 
@@ -133,10 +138,13 @@ __host__ __device__ __forceinline__ Smem smem_layout(int epi, int KI, int stages
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
-    return v;
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+// Named barrier over the epilogue warps (id 1; 0 is __syncthreads, used once before the roles split).
+__device__ __forceinline__ void epilogue_sync() {
+    asm volatile("bar.sync 1, %0;" ::"r"(kEpilogueWarps * 32) : "memory");
 }
 
 // Store one rotated 128-block (lane l holds k = 4l..4l+3) in xf order: tile-row r = l/4, quad q, slot idx with
@@ -165,31 +173,32 @@ __device__ __forceinline__ void rotated_block(const TIn* x, const __half* suh, i
     for (int j = 0; j < 4; ++j) v[j] = __half2float(__float2half_rn(v[j] * kRsqrt128));
 }
 
-// One consumer warp: its TPW tiles of one matrix over the group's tile-rows (all of every stage of the group).
+// One consumer warp over one segment: its TPW tiles of one matrix on every tile-row of the stages its sub-group owns
+// (ring sequence numbers it with it % kSub == sub), continuing the CTA's ring sequence at `it`. The ring couples the
+// sub-groups: one that falls behind holds the producer back, and the others then wait and leave it the issue slots.
 // d[t] = D[16 n x 8 rows] of tile t: d[0], d[1] = (n = g, rows 2q, 2q+1), d[2], d[3] = (n = g + 8, rows 2q, 2q+1).
 template <int K, int TPW>
-__device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, int n_stages, int row_stride,
-                                        int mat_off, int tile0, int n_rows, int rps, uint64_t* full,
-                                        uint64_t* empty, const __half* xf_row, int xf_row_stride, int Mi, int lane,
-                                        bool& timed_out) {
+__device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, int row_stride, int mat_off, int tile0,
+                                        int n_rows, int rps, int sub, uint64_t* full, uint64_t* empty,
+                                        const __half* xf_row, bool has_row, int lane, int& it, bool& timed_out) {
     const LaneWords lw = lane_words<K>(lane);
-    const int g = lane >> 2, q = lane & 3;
-    const bool has_row = g < Mi;
-    // B fragment of tile-row r for this lane: 8 bytes at xf_row + g * stride + r * 16 + q * 4
-    const uint2* bp = reinterpret_cast<const uint2*>(xf_row + (size_t)(has_row ? g : 0) * xf_row_stride + q * 4);
-    uint2 bn = make_uint2(0, 0);
-    if (has_row && n_rows > 0) bn = __ldg(bp);
-    const int n_iter = (n_rows + rps - 1) / rps;
-    int r = 0;
-    for (int it = 0; it < n_iter; ++it) {
-        const int s = it % n_stages;
-        if (!timed_out && !mbar_wait(&full[s], (it / n_stages) & 1)) timed_out = true;
+    const int q = lane & 3;
+    // B fragment of tile-row r for this lane: 8 bytes at xf_row + r * 16 + q * 4
+    const uint2* bp = reinterpret_cast<const uint2*>(xf_row + q * 4);
+    for (int r0 = 0; r0 < n_rows; r0 += rps, ++it) {
+        if (it % kSub != sub) continue;
+        const int s = it % kStages;
+        const int rows = min(rps, n_rows - r0);
+        uint2 bn = make_uint2(0, 0);
+        if (has_row) bn = __ldg(bp + (size_t)r0 * 4);
+        if (!timed_out && !mbar_wait(&full[s], (it / kStages) & 1)) timed_out = true;
         if (!timed_out) {
-            const int rows = min(rps, n_rows - it * rps);
             const uint8_t* base = ring + (size_t)s * kStageBytes + mat_off + tile0 * 32 * K;
-            for (int rr = 0; rr < rows; ++rr, ++r, base += row_stride) {
+            for (int rr = 0; rr < rows; ++rr, base += row_stride) {
+                const int r = r0 + rr;
                 const uint2 b = bn;
-                if (has_row && r + 1 < n_rows) bn = __ldg(bp + (size_t)(r + 1) * 4);   // next row's fragment
+                if (has_row && rr + 1 < rows) bn = __ldg(bp + (size_t)(r + 1) * 4);             // next row's
+                if (has_row && r + kSub * rps < n_rows) prefetch_l1(bp + (size_t)(r + kSub * rps) * 4);
 #pragma unroll
                 for (int t = 0; t < TPW; ++t) {
                     uint32_t a[4];
@@ -204,13 +213,12 @@ __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, in
 }
 
 template <int TPW>
-__device__ __forceinline__ void consume_k(int K, float d[TPW][4], const uint8_t* ring, int n_stages,
-                                          int row_stride, int mat_off, int tile0, int n_rows, int rps,
-                                          uint64_t* full, uint64_t* empty, const __half* xf_row, int xf_row_stride,
-                                          int Mi, int lane, bool& to) {
+__device__ __forceinline__ void consume_k(int K, float d[TPW][4], const uint8_t* ring, int row_stride, int mat_off,
+                                          int tile0, int n_rows, int rps, int sub, uint64_t* full, uint64_t* empty,
+                                          const __half* xf_row, bool has_row, int lane, int& it, bool& to) {
 #define EXL3_CONSUME(KK)                                                                                          \
-    consume<KK, TPW>(d, ring, n_stages, row_stride, mat_off, tile0, n_rows, rps, full, empty, xf_row,             \
-                     xf_row_stride, Mi, lane, to)
+    consume<KK, TPW>(d, ring, row_stride, mat_off, tile0, n_rows, rps, sub, full, empty, xf_row, has_row, lane,    \
+                     it, to)
     switch (K) {
         case 1: EXL3_CONSUME(1); break;
         case 2: EXL3_CONSUME(2); break;
@@ -226,186 +234,116 @@ __device__ __forceinline__ void consume_k(int K, float d[TPW][4], const uint8_t*
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
 
-// Grid: blockIdx.x = unit * split + p, cluster (split, 1, 1). Block: KI groups of (1 producer + tile_groups(EPI)) warps.
+// What a unit needs: packed weights of its column block, bit widths, rows, and the activation row of each MMA
+// column (linear: row g; gate|up: the pair's source row; down: the pair position).
 template <int EPI>
-__global__ void __launch_bounds__(kMaxWarps * 32, 1) k_gemv(const GemvArgs args) {
-    constexpr int NMAT = nmat_of(EPI);
-    constexpr int TPW = tiles_per_warp(EPI);
-    constexpr int NTG = tile_groups(EPI);
-    constexpr int TG_PER_MAT = NTG / NMAT;
-    extern __shared__ __align__(128) uint8_t smem[];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int KI = (int)(blockDim.x >> 5) / (NTG + 1);
-    const int grp = warp / (NTG + 1), wig = warp % (NTG + 1);
-    if (threadIdx.x == 0) EXL3_TRACE_POINT(0);
-    pdl_trigger();
-    const int P = args.split;
-    const int p = blockIdx.x % P;
-    const int unit = blockIdx.x / P;
-    const int NB = args.n / 128;
-    const int cb = unit % NB;
-    const int KB = args.k / 128;
+struct UnitInfo {
+    const uint8_t* w;           // packed weights of the unit's column block (k-block 0)
+    int K[nmat_of(EPI)];
+    int row_stride;             // bytes per tile-row of the block (all matrices)
+    int Mi, s0, expert, cb;
+    int xrow[kMaxRows];
+};
 
-    // ---- work unit: packed weights, rows ----
-    const uint8_t* wbase;
-    const __half* svh[NMAT];
-    int Kb[NMAT];
-    int Mi, s0 = 0, expert = 0;
+template <int EPI>
+__device__ __forceinline__ UnitInfo<EPI> unit_info(const GemvArgs& a, int u, int NB, int KB) {
+    constexpr int NMAT = nmat_of(EPI);
+    UnitInfo<EPI> ui;
+    ui.cb = u % NB;
+    const uint8_t* base;
     if constexpr (EPI == EPI_LINEAR) {
-        wbase = reinterpret_cast<const uint8_t*>(args.tr);
-        svh[0] = args.svh;
-        Kb[0] = args.K;
-        Mi = args.M;
+        base = reinterpret_cast<const uint8_t*>(a.tr);
+        ui.K[0] = a.K;
+        ui.Mi = a.M;
+        ui.s0 = 0;
+        ui.expert = 0;
     } else {
-        // the item table comes from the alignment kernel, complete before the kernel this one overlaps with
-        const int item = unit / NB;
-        if (item >= *args.items.n_items) return;              // uniform over the cluster
-        expert = args.items.item_expert[item];
-        s0 = args.items.item_start[item];
-        Mi = args.items.item_cnt[item];
-        const ExpertDesc& ed = args.experts[expert];
+        const int item = u / NB;
+        ui.expert = __ldcg(a.items.item_expert + item);
+        ui.s0 = __ldcg(a.items.item_start + item);
+        ui.Mi = __ldcg(a.items.item_cnt + item);
+        const ExpertDesc& ed = a.experts[ui.expert];
         if constexpr (EPI == EPI_GATEUP) {
-            wbase = reinterpret_cast<const uint8_t*>(ed.tr[0]);
+            base = reinterpret_cast<const uint8_t*>(ed.tr[0]);
+            ui.K[0] = ed.K[0];
+            ui.K[NMAT - 1] = ed.K[1];
+        } else {
+            base = reinterpret_cast<const uint8_t*>(ed.tr[2]);
+            ui.K[0] = ed.K[2];
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < kMaxRows; ++g) {
+        int r = 0;
+        if (g < ui.Mi) {
+            if constexpr (EPI == EPI_LINEAR) r = g;
+            else if constexpr (EPI == EPI_GATEUP) r = __ldcg(a.items.pair_src + ui.s0 + g);
+            else r = ui.s0 + g;
+        }
+        ui.xrow[g] = r;
+    }
+    ui.row_stride = 0;
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m) ui.row_stride += kTilesPerMat * 32 * ui.K[m];
+    ui.w = base + (size_t)ui.cb * KB * 8 * ui.row_stride;
+    return ui;
+}
+
+// Epilogue of one unit from its summed accumulators red[nmat][kMaxRows][128] (shared memory), one row per warp.
+template <int EPI>
+__device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<EPI>& ui, const float* red, int ew,
+                                              int lane) {
+    constexpr int NMAT = nmat_of(EPI);
+    const int col = ui.cb * 128 + 4 * lane;
+    const __half* svh[NMAT];
+    if constexpr (EPI == EPI_LINEAR) {
+        svh[0] = a.svh;
+    } else {
+        const ExpertDesc& ed = a.experts[ui.expert];
+        if constexpr (EPI == EPI_GATEUP) {
             svh[0] = ed.svh[0];
             svh[NMAT - 1] = ed.svh[1];
-            Kb[0] = ed.K[0];
-            Kb[NMAT - 1] = ed.K[1];
         } else {
-            wbase = reinterpret_cast<const uint8_t*>(ed.tr[2]);
             svh[0] = ed.svh[2];
-            Kb[0] = ed.K[2];
         }
     }
-    int row_stride = 0, mat_off[NMAT];
-#pragma unroll
-    for (int m = 0; m < NMAT; ++m) { mat_off[m] = row_stride; row_stride += kTilesPerCta * 32 * Kb[m]; }
-
-    // ---- k range of this CTA (whole 128-blocks), this group's contiguous share, its slice of the packed weights ----
-    const int kb0 = (p * KB) / P, kb1 = ((p + 1) * KB) / P;
-    const int per_grp = (kb1 - kb0 + KI - 1) / KI;             // blocks per group
-    const int g_kb0 = min(kb1, kb0 + grp * per_grp), g_kb1 = min(kb1, g_kb0 + per_grp);
-    const int n_rows = (g_kb1 - g_kb0) * 8;                    // this group's tile-rows
-    const int rps = kStageBytes / row_stride;                 // tile-rows per stage (row_stride <= 4096)
-    const int n_stages = args.stages / KI;                     // this group's ring stages
-    const uint8_t* slice = wbase + ((size_t)cb * (KB * 8) + (size_t)g_kb0 * 8) * row_stride;
-
-    const Smem L = smem_layout(EPI, KI, args.stages);
-    float* red = reinterpret_cast<float*>(smem + L.red_off);
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off) + grp * n_stages;
-    uint64_t* empty = reinterpret_cast<uint64_t*>(smem + L.bar_off) + kMaxStages + grp * n_stages;
-    uint8_t* ring = smem + L.ring_off + (size_t)grp * n_stages * kStageBytes;
-
-    if (wig == 0 && lane == 0) {
-        for (int s = 0; s < n_stages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], NTG); }
-        fence_barrier_init();
-    }
-    __syncthreads();
-
-    if (wig == 0) {
-        // ---------------- producer: the slice, stage by stage ----------------
-        if (lane == 0) {
-            const int n_iter = (n_rows + rps - 1) / rps;
-            bool to = false;
-            int last_issue[kMaxStages];
-            for (int s = 0; s < kMaxStages; ++s) last_issue[s] = -1;
-            for (int it = 0; it < n_iter && !to; ++it) {
-                const int s = it % n_stages;
-                if (it >= n_stages && !mbar_wait(&empty[s], ((it / n_stages) - 1) & 1)) { to = true; break; }
-                const uint32_t bytes = (uint32_t)(min(rps, n_rows - it * rps) * row_stride);
-                mbar_expect_tx(&full[s], bytes);
-                bulk_g2s(ring + (size_t)s * kStageBytes, slice + (size_t)it * rps * row_stride, bytes, &full[s]);
-                last_issue[s] = it;
-            }
-            EXL3_TRACE_POINT(7);
-            if (to) report(args.status, EXL3_ERR_TIMEOUT);
-            // every issued copy has landed before the CTA can retire its shared memory
-            for (int s = 0; s < n_stages; ++s)
-                if (last_issue[s] >= 0 && !mbar_wait(&full[s], (last_issue[s] / n_stages) & 1))
-                    report(args.status, EXL3_ERR_TIMEOUT);
-        }
-    } else {
-        // ---------------- consumers ----------------
-        const int tg = wig - 1;
-        const int m = tg / TG_PER_MAT, tile0 = (tg % TG_PER_MAT) * TPW;
-        const int g = lane >> 2, q = lane & 3;
-        pdl_wait();                                           // activations come from the previous kernel
-        if (threadIdx.x == 32) EXL3_TRACE_POINT(1);
-        // xf rows: linear -> row m; gate|up -> pair position (s0 + row), matrix m; down -> pair position
-        const size_t row_elems = (size_t)NMAT * args.k;
-        const size_t row0 = (EPI == EPI_LINEAR) ? 0 : (size_t)s0;
-        const __half* xf_row = args.xf + row0 * row_elems + (size_t)m * args.k + (size_t)g_kb0 * 128;
-        float d[TPW][4];
-#pragma unroll
-        for (int t = 0; t < TPW; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) d[t][e] = 0.f;
-        bool to = false;
-        consume_k<TPW>(Kb[m], d, ring, n_stages, row_stride, mat_off[m], tile0, n_rows, rps, full, empty, xf_row,
-                       (int)row_elems, Mi, lane, to);
-        if (to) report(args.status, EXL3_ERR_TIMEOUT);
-        if (lane == 0 && warp == 1) EXL3_TRACE_POINT(3);
-        float* rm = red + ((size_t)grp * NMAT + m) * kMaxRows * 128;
-#pragma unroll
-        for (int t = 0; t < TPW; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int row = 2 * q + (e & 1);
-                const int col = (tile0 + t) * 16 + g + ((e >> 1) << 3);
-                rm[row * 128 + col] = d[t][e];
-            }
-    }
-
-    // ---- reduction over ki and the cluster's split-K CTAs (fixed order) + epilogue ----
-    __syncwarp();
-    if (P > 1) cluster_sync_all(); else __syncthreads();
-    if (threadIdx.x == 0) EXL3_TRACE_POINT(5);
-
-    const int nwarps = blockDim.x >> 5;
-    for (int row = p + warp * P; row < Mi; row += nwarps * P) {
+    for (int row = ew; row < ui.Mi; row += kEpilogueWarps) {
         float v[NMAT][4];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
-            v[m][0] = v[m][1] = v[m][2] = v[m][3] = 0.f;
-            for (int c = 0; c < P; ++c)
-                for (int k2 = 0; k2 < KI; ++k2) {
-                    const float* src = red + (((size_t)k2 * NMAT + m) * kMaxRows + row) * 128 + 4 * lane;
-                    float4 t;
-                    if (P > 1) t = ld_dsmem_f4(map_shared_rank(src, c));
-                    else t = *reinterpret_cast<const float4*>(src);
-                    v[m][0] += t.x; v[m][1] += t.y; v[m][2] += t.z; v[m][3] += t.w;
-                }
+            const float4 t = *reinterpret_cast<const float4*>(red + ((size_t)m * kMaxRows + row) * 128 + 4 * lane);
+            v[m][0] = t.x; v[m][1] = t.y; v[m][2] = t.z; v[m][3] = t.w;
             fwht128_warp(v[m], lane);
         }
-        const int col = cb * 128 + 4 * lane;
         if constexpr (EPI == EPI_LINEAR) {
             float o[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 const float sv = __half2float(svh[0][col + j]);
-                if (args.y_dtype == EXL3_F16)
+                if (a.y_dtype == EXL3_F16)
                     o[j] = __half2float(__float2half_rn(__half2float(__float2half_rn(v[0][j] * kRsqrt128)) * sv));
                 else
                     o[j] = v[0][j] * kRsqrt128 * sv;
             }
-            if (args.y_dtype == EXL3_F32) {
-                float* yp = reinterpret_cast<float*>(args.y) + (size_t)row * args.ldy + col;
+            if (a.y_dtype == EXL3_F32) {
+                float* yp = reinterpret_cast<float*>(a.y) + (size_t)row * a.ldy + col;
                 *reinterpret_cast<float4*>(yp) = make_float4(o[0], o[1], o[2], o[3]);
-            } else if (args.y_dtype == EXL3_F16) {
-                __half* yp = reinterpret_cast<__half*>(args.y) + (size_t)row * args.ldy + col;
+            } else if (a.y_dtype == EXL3_F16) {
+                __half* yp = reinterpret_cast<__half*>(a.y) + (size_t)row * a.ldy + col;
                 __half2 h01 = __floats2half2_rn(o[0], o[1]), h23 = __floats2half2_rn(o[2], o[3]);
                 uint2 u;
                 u.x = *reinterpret_cast<uint32_t*>(&h01);
                 u.y = *reinterpret_cast<uint32_t*>(&h23);
                 *reinterpret_cast<uint2*>(yp) = u;
             } else {
-                __nv_bfloat16* yp = reinterpret_cast<__nv_bfloat16*>(args.y) + (size_t)row * args.ldy + col;
+                __nv_bfloat16* yp = reinterpret_cast<__nv_bfloat16*>(a.y) + (size_t)row * a.ldy + col;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) yp[j] = __float2bfloat16_rn(o[j]);
             }
         } else if constexpr (EPI == EPI_GATEUP) {
-            const ExpertDesc& ed = args.experts[expert];
-            const float Lc = args.act_limit;
-            float a[4];
+            const ExpertDesc& ed = a.experts[ui.expert];
+            const float Lc = a.act_limit;
+            float h[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 // gate/up outputs rounded to fp16 as the fp16 linear does: fp16(fp16(H(acc)*r) * svh)
@@ -417,68 +355,261 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) k_gemv(const GemvArgs args)
                 float sg = silu_f(gg);
                 if (Lc != 0.f) { sg = fminf(sg, Lc); uu = fminf(fmaxf(uu, -Lc), Lc); }
                 const float act = __half2float(__float2half_rn(sg * uu));
-                a[j] = __half2float(__float2half_rn(act * __half2float(ed.suh[2][col + j])));
+                h[j] = __half2float(__float2half_rn(act * __half2float(ed.suh[2][col + j])));
             }
-            fwht128_warp(a, lane);
+            fwht128_warp(h, lane);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) a[j] = a[j] * kRsqrt128;
+            for (int j = 0; j < 4; ++j) h[j] = h[j] * kRsqrt128;
             // the down projection's input block cb, straight into xf order
-            store_xf_block(a, lane, args.xf_out + (size_t)(s0 + row) * args.n + (size_t)cb * 128);
+            store_xf_block(h, lane, a.xf_out + (size_t)(ui.s0 + row) * a.n + (size_t)ui.cb * 128);
         } else {
-            const float w = args.items.pair_w[s0 + row];
+            const float w = __ldcg(a.items.pair_w + ui.s0 + row);
             float o[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) o[j] = w * (v[0][j] * kRsqrt128 * __half2float(svh[0][col + j]));
-            float* dst = args.ybuf + (size_t)(s0 + row) * args.n + col;
+            float* dst = a.ybuf + (size_t)(ui.s0 + row) * a.n + col;
             *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
         }
     }
-    __syncwarp();
-    if (P > 1) cluster_sync_all();
-    if (threadIdx.x == 0) EXL3_TRACE_POINT(6);
+}
+
+// First k-block of CTA c's range, and the CTA that owns k-block x (the last CTA whose range starts at or before x;
+// CTAs with empty ranges own nothing).
+__device__ __forceinline__ long long range_start(long long c, long long T, long long G) { return c * T / G; }
+__device__ __forceinline__ long long owner_of(long long x, long long T, long long G) { return ((x + 1) * G - 1) / T; }
+// The CTA owning the first k-block after CTA c's range (contributors of one unit, in order).
+__device__ __forceinline__ long long next_owner(long long c, long long T, long long G) {
+    return owner_of(range_start(c + 1, T, G), T, G);
+}
+
+// Grid: persistent, at most one CTA per SM, each a contiguous range of the launch's k-blocks; block: 1 producer warp,
+// kConsumerWarps consumer warps, kEpilogueWarps epilogue warps.
+template <int EPI>
+__global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
+    constexpr int NMAT = nmat_of(EPI);
+    constexpr int TPW = tiles_per_warp(EPI);
+    constexpr int UF = unit_floats(EPI);
+    extern __shared__ __align__(128) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) EXL3_TRACE_POINT(0);
+    pdl_trigger();
+    const int NB = args.n / 128, KB = args.k / 128;
+    const long long G = gridDim.x;
+    const long long ci = blockIdx.x;
+    // units: the linear's column blocks, or (expert item, column block) pairs of the alignment step's table
+    const int U = (EPI == EPI_LINEAR) ? NB : __ldcg(args.items.n_items) * NB;
+    const long long T = (long long)U * KB;
+    const long long r0 = range_start(ci, T, G), r1 = range_start(ci + 1, T, G);
+
+    const Smem L = smem_layout(EPI);
+    float* red = reinterpret_cast<float*>(smem + L.red_off);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+    uint64_t* empty = full + kStages;
+    uint64_t* acc_full = empty + kStages;                      // [2]: a segment's accumulators are in red[buf]
+    uint64_t* acc_empty = acc_full + 2;                        // [2]: red[buf] may be overwritten
+    volatile int* flag = reinterpret_cast<volatile int*>(smem + L.flag_off);
+    uint8_t* ring = smem + L.ring_off;
+    static_assert(sizeof(UnitInfo<EPI>) <= kDescBytes, "descriptor slot");
+    UnitInfo<EPI>* descs = reinterpret_cast<UnitInfo<EPI>*>(smem + L.desc_off);
+
+    // segments: the units the range touches; segment i = unit u0 + i, k-blocks [lo, hi). Their descriptors (dependent
+    // table loads) are resolved once, one thread per segment, while the previous kernel may still be running.
+    const long long u0 = r0 / KB;
+    const int n_seg = r1 > r0 ? (int)((r1 - 1) / KB - u0 + 1) : 0;
+    for (int i = threadIdx.x; i < n_seg && i < kMaxSeg; i += blockDim.x)
+        descs[i] = unit_info<EPI>(args, (int)(u0 + i), NB, KB);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], kConsumers); }
+        for (int b = 0; b < 2; ++b) { mbar_init(&acc_full[b], kConsumerWarps); mbar_init(&acc_empty[b], kEpilogueWarps); }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == 0) {
+        // ---------------- producer: the range, segment by segment, stage by stage ----------------
+        if (lane == 0) {
+            bool to = false;
+            int it = 0;
+            for (int i = 0; i < n_seg && !to; ++i) {
+                const long long u = u0 + i;
+                const int lo = i == 0 ? (int)(r0 - u * KB) : 0;
+                const int hi = (int)min((long long)KB, r1 - u * KB);
+                const UnitInfo<EPI> ui = i < kMaxSeg ? descs[i] : unit_info<EPI>(args, (int)u, NB, KB);
+                const uint8_t* src = ui.w + (size_t)lo * 8 * ui.row_stride;
+                const int n_rows = (hi - lo) * 8, rps = kStageBytes / ui.row_stride;
+                for (int r = 0; r < n_rows; r += rps, ++it) {
+                    const int s = it % kStages;
+                    if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1)) { to = true; break; }
+                    const uint32_t bytes = (uint32_t)(min(rps, n_rows - r) * ui.row_stride);
+                    mbar_expect_tx(&full[s], bytes);
+                    bulk_g2s(ring + (size_t)s * kStageBytes, src + (size_t)r * ui.row_stride, bytes, &full[s]);
+                }
+            }
+            EXL3_TRACE_POINT(7);
+            if (to) report(args.status, EXL3_ERR_TIMEOUT);
+            // every issued copy has landed before the CTA can retire its shared memory: stage s last held sequence
+            // number s + kStages * floor((it - 1 - s) / kStages)
+            for (int s = 0; s < kStages && s < it; ++s) {
+                const int last = s + ((it - 1 - s) / kStages) * kStages;
+                if (!mbar_wait(&full[s], (last / kStages) & 1)) report(args.status, EXL3_ERR_TIMEOUT);
+            }
+        }
+        return;
+    }
+
+    if (warp <= kConsumerWarps) {
+        // ---------------- consumers: decode + MMA, accumulators handed to the epilogue warps ----------------
+        const int cw = warp - 1;
+        const int sub = cw / kConsumers, cq = cw % kConsumers;
+        const int m = (cq * TPW) / kTilesPerMat, tile0 = (cq * TPW) % kTilesPerMat;
+        const int g = lane >> 2, q = lane & 3;
+        pdl_wait();                                           // activations come from earlier kernels
+        if (threadIdx.x == 32) EXL3_TRACE_POINT(1);
+        bool to = false;
+        int it = 0;
+        for (int i = 0; i < n_seg; ++i) {
+            const long long u = u0 + i;
+            const int lo = i == 0 ? (int)(r0 - u * KB) : 0;
+            const int hi = (int)min((long long)KB, r1 - u * KB);
+            const UnitInfo<EPI> ui = i < kMaxSeg ? descs[i] : unit_info<EPI>(args, (int)u, NB, KB);
+            const bool has_row = g < ui.Mi;
+            const __half* xf_row =
+                args.xf + (size_t)ui.xrow[g] * NMAT * args.k + (size_t)m * args.k + (size_t)lo * 128;
+            int mat_off = 0;
+#pragma unroll
+            for (int mm = 0; mm < NMAT; ++mm)
+                if (mm < m) mat_off += kTilesPerMat * 32 * ui.K[mm];
+            float d[TPW][4];
+#pragma unroll
+            for (int t = 0; t < TPW; ++t)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) d[t][e] = 0.f;
+            consume_k<TPW>(ui.K[m], d, ring, ui.row_stride, mat_off, tile0, (hi - lo) * 8,
+                           kStageBytes / ui.row_stride, sub, full, empty, xf_row, has_row, lane, it, to);
+            // hand the accumulators over: red[i & 1][sub], once the epilogue released segment i - 2's
+            const int buf = i & 1;
+            if (i >= 2 && !to && !mbar_wait(&acc_empty[buf], ((i >> 1) - 1) & 1)) to = true;
+            float* rs = red + ((size_t)buf * kSub + sub) * UF;
+#pragma unroll
+            for (int t = 0; t < TPW; ++t)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int row = 2 * q + (e & 1);
+                    const int col = (tile0 + t) * 16 + g + ((e >> 1) << 3);
+                    rs[((size_t)m * kMaxRows + row) * 128 + col] = d[t][e];
+                }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_full[buf]);
+        }
+        if (to) report(args.status, EXL3_ERR_TIMEOUT);
+        if (threadIdx.x == 32) EXL3_TRACE_POINT(6);
+        return;
+    }
+
+    // ---------------- epilogue warps: sum the sub-groups, reduce split units, finish units ----------------
+    const int ew = warp - 1 - kConsumerWarps;
+    const int et = ew * 32 + lane;
+    pdl_wait();                                               // tickets and outputs belong to this launch from here
+    bool to = false;
+    for (int i = 0; i < n_seg; ++i) {
+        const long long u = u0 + i;
+        const int lo = i == 0 ? (int)(r0 - u * KB) : 0;
+        const int hi = (int)min((long long)KB, r1 - u * KB);
+        const UnitInfo<EPI> ui = i < kMaxSeg ? descs[i] : unit_info<EPI>(args, (int)u, NB, KB);
+        const int buf = i & 1;
+        if (!to && !mbar_wait(&acc_full[buf], (i >> 1) & 1)) to = true;
+        float* rb = red + (size_t)buf * kSub * UF;
+        const bool whole = lo == 0 && hi == KB;
+        float4* slot = reinterpret_cast<float4*>(args.partial + (size_t)(i == 0 ? 2 * ci : 2 * ci + 1) * UF);
+        // sub-group sums in sub-group order: into rb[0] (whole unit) or this CTA's partial slot
+        for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
+            if ((e / 32) % kMaxRows >= ui.Mi) continue;       // rows beyond the unit's
+            float4 acc = reinterpret_cast<const float4*>(rb)[e];
+#pragma unroll
+            for (int j = 1; j < kSub; ++j) {
+                const float4 v = reinterpret_cast<const float4*>(rb + (size_t)j * UF)[e];
+                acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+            }
+            if (whole) reinterpret_cast<float4*>(rb)[e] = acc;
+            else slot[e] = acc;
+        }
+        bool finish = whole;
+        if (!whole) {
+            // ticket: the last contributor of unit u sums every partial in CTA order
+            __threadfence();
+            epilogue_sync();
+            const long long a0 = u * KB, a1 = a0 + KB;        // the unit's k-blocks [a0, a1)
+            if (et == 0) {
+                int nseg = 1;
+                for (long long c = owner_of(a0, T, G); range_start(c + 1, T, G) < a1; c = next_owner(c, T, G)) ++nseg;
+                const int old = atomicAdd(args.counters + u, 1);
+                const int last = old == nseg - 1;
+                if (last) {
+                    args.counters[u] = 0;                     // left zero for the next launch
+                    __threadfence();
+                }
+                *flag = last;
+            }
+            epilogue_sync();
+            finish = *flag != 0;
+            if (finish) {
+                // contributors in order: the owner of a0, then the owner after each range, up to the unit's end; a
+                // contributor that started before a0 keeps this unit's partial in its second slot
+                for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
+                    if ((e / 32) % kMaxRows >= ui.Mi) continue;
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    for (long long c = owner_of(a0, T, G);; c = next_owner(c, T, G)) {
+                        const long long sl = range_start(c, T, G) < a0 ? 2 * c + 1 : 2 * c;
+                        const float4 p = __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)sl * UF) + e);
+                        acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
+                        if (range_start(c + 1, T, G) >= a1) break;
+                    }
+                    reinterpret_cast<float4*>(rb)[e] = acc;
+                }
+            }
+        }
+        if (finish) {
+            epilogue_sync();
+            unit_epilogue<EPI>(args, ui, rb, ew, lane);
+        }
+        epilogue_sync();                                      // the flag and red[buf] are read: release them
+        if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+    if (to) report(args.status, EXL3_ERR_TIMEOUT);
 }
 
 // ------------------------------------------------------------------------------------------------ activation prep
 
-// xf of input rows: job = (row, matrix, 128-block), one warp each. x rows are fp16/bf16 at row stride ldx; row_tok
-// (optional) maps an xf row to its x row (MoE pair position -> token) and row_expert (optional) selects the suh of the
-// picked expert's matrix; otherwise suh0 is shared by all rows.
+// xf of the dense linear's input rows: job = (row, 128-block), one warp each; also zeroes the GEMV's tickets.
 struct PrepArgs {
     const void* x;
     int ldx;
     int x_bf16;
-    int rows, nmat, k;
-    const __half* suh0;
-    const int* row_tok;
-    const int* row_expert;
-    const ExpertDesc* experts;
-    const int* n_rows_dev;        // optional device count of valid rows (MoE: valid pair positions + shared rows)
-    __half* xf;                   // [rows][nmat][k] in xf order
+    int rows, k;
+    const __half* suh;
+    __half* xf;                   // [rows][k] in xf order
+    int* zero;                    // tickets of the following GEMV
+    int n_zero;
 };
 
 static __global__ void __launch_bounds__(256) k_prep(const PrepArgs a) {
     pdl_trigger();
     pdl_wait();
+    const int gt = blockIdx.x * blockDim.x + threadIdx.x;
+    for (int i = gt; i < a.n_zero; i += gridDim.x * blockDim.x) a.zero[i] = 0;
     const int KB = a.k / 128;
     const int lane = threadIdx.x & 31;
-    const int rows = a.n_rows_dev ? min(a.rows, *a.n_rows_dev) : a.rows;
-    const int jobs = rows * a.nmat * KB;
-    for (int j = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < jobs; j += (gridDim.x * blockDim.x) >> 5) {
-        const int row = j / (a.nmat * KB);
-        const int m = (j / KB) % a.nmat;
-        const int kb = j % KB;
-        const __half* suh = a.suh0;
-        size_t xrow = (size_t)row;
-        if (a.row_tok) xrow = (size_t)a.row_tok[row];
-        if (a.row_expert) suh = a.experts[a.row_expert[row]].suh[m];
+    const int jobs = a.rows * KB;
+    for (int j = gt >> 5; j < jobs; j += (gridDim.x * blockDim.x) >> 5) {
+        const int row = j / KB, kb = j % KB;
         float v[4];
-        const __half* su = suh ? suh + kb * 128 : nullptr;
+        const __half* su = a.suh ? a.suh + kb * 128 : nullptr;
         if (a.x_bf16)
-            rotated_block<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(a.x) + xrow * a.ldx + kb * 128, su,
-                                         lane, v);
+            rotated_block<__nv_bfloat16>(reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)row * a.ldx + kb * 128,
+                                         su, lane, v);
         else
-            rotated_block<__half>(reinterpret_cast<const __half*>(a.x) + xrow * a.ldx + kb * 128, su, lane, v);
-        store_xf_block(v, lane, a.xf + ((size_t)row * a.nmat + m) * a.k + (size_t)kb * 128);
+            rotated_block<__half>(reinterpret_cast<const __half*>(a.x) + (size_t)row * a.ldx + kb * 128, su, lane, v);
+        store_xf_block(v, lane, a.xf + (size_t)row * a.k + (size_t)kb * 128);
     }
 }
 
@@ -487,68 +618,40 @@ static __global__ void __launch_bounds__(256) k_prep(const PrepArgs a) {
 // Launch with programmatic stream serialization (the kernel may start while the previous one finishes).
 template <typename... KArgs, typename... Args>
 inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                              int cluster, Args... args) {
+                              Args... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    int na = 0;
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    ++na;
-    if (cluster > 1) {
-        attr[na].id = cudaLaunchAttributeClusterDimension;
-        attr[na].val.clusterDim.x = cluster;
-        attr[na].val.clusterDim.y = 1;
-        attr[na].val.clusterDim.z = 1;
-        ++na;
-    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = na;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
-// Work decomposition: units = work items x column blocks. Grids with fewer units than SMs split k over a cluster;
-// they and single-wave grids run KI = 3 consumer warps per tile group (one big CTA per SM, deep ring); larger grids
-// run KI = 1 (several smaller CTAs per SM).
+// Split-unit partial slots of a GEMV launch on the current device (workspace sizing): two per CTA.
+inline int max_ctas() { return num_sms(); }
+inline size_t partial_bytes(int epi) { return (size_t)2 * max_ctas() * unit_floats(epi) * 4; }
+
+// Work decomposition: one CTA per SM, or fewer when the launch has fewer k-blocks; `ctas` > 0 overrides the count
+// (tests, tuning).
 struct GemvPlan {
-    int split, KI, stages, threads, smem;
+    int ctas, smem;
 };
-inline GemvPlan plan_gemv(int epi, int units, int k, int row_stride_hint, int requested_split) {
+inline GemvPlan plan_gemv(int epi, long long work_upper, int ctas) {
     GemvPlan pl;
-    const int sms = num_sms();
-    const int KB = k / 128;
-    const int cap = KB < kMaxCluster ? KB : kMaxCluster;
-    int P = requested_split;
-    if (P <= 0) {
-        P = 1;
-        while (P < cap && units * (P + 1) <= sms) ++P;
-    }
-    if (P > cap) P = cap;
-    pl.split = P;
-    // MoE grids are sized from an upper bound on items (the surplus CTAs exit at once), so up to 1.25 x SMs still
-    // means about one working CTA per SM
-    pl.KI = units * P * 4 > sms * 5 ? 1 : max_ki(epi);
-    const int n_rows = klen_alloc_of(k, P) / 16;
-    const long slice = (long)n_rows * row_stride_hint;
-    int stages = (int)((slice + kStageBytes - 1) / kStageBytes);     // enough to hold the whole slice
-    const int max_st = pl.KI == 1 ? 6 : kMaxStages;
-    stages = stages > max_st ? max_st : stages;
-    stages = (stages + pl.KI - 1) / pl.KI;                           // per group
-    stages = stages < 2 ? 2 : stages;
-    while (stages * pl.KI > kMaxStages) --stages;
-    pl.stages = stages * pl.KI;
-    pl.threads = pl.KI * (tile_groups(epi) + 1) * 32;
-    pl.smem = smem_layout(epi, pl.KI, pl.stages).total;
+    const int sms = max_ctas();
+    if (ctas <= 0) ctas = work_upper < sms ? (int)(work_upper < 1 ? 1 : work_upper) : sms;
+    pl.ctas = ctas > sms ? sms : ctas;
+    pl.smem = smem_layout(epi).total;
     return pl;
 }
 
 template <int EPI>
-int launch_gemv(GemvArgs a, int units, const GemvPlan& pl, cudaStream_t st, const char* what) {
-    a.split = pl.split;
-    a.stages = pl.stages;
+int launch_gemv(GemvArgs a, const GemvPlan& pl, cudaStream_t st, const char* what) {
     EXL3_REQUIRE(pl.smem <= 227 * 1024, EXL3_ERR_UNSUPPORTED, "%s: shared memory plan too large", what);
     auto kern = k_gemv<EPI>;
     static int configured[64] = {0};
@@ -561,7 +664,7 @@ int launch_gemv(GemvArgs a, int units, const GemvPlan& pl, cudaStream_t st, cons
         }
         configured[dev] = 1;
     }
-    cudaError_t e = launch_pdl(kern, dim3(units * pl.split), dim3(pl.threads), pl.smem, st, pl.split, a);
+    cudaError_t e = launch_pdl(kern, dim3(pl.ctas), dim3(kGemvThreads), pl.smem, st, a);
     if (e != cudaSuccess) {
         set_error("%s: launch failed: %s", what, cudaGetErrorString(e));
         return EXL3_ERR_CUDA;
@@ -569,21 +672,14 @@ int launch_gemv(GemvArgs a, int units, const GemvPlan& pl, cudaStream_t st, cons
     return EXL3_OK;
 }
 
-// pdl: overlap the prep kernel with its predecessor. The MoE path launches it without (pdl = 0): the GEMV that follows
-// reads the alignment tables before its own griddepcontrol.wait, which is safe only if prep started after the
-// alignment kernel completed.
-inline int launch_prep(const PrepArgs& a, cudaStream_t st, const char* what, bool pdl) {
-    const long jobs = (long)a.rows * a.nmat * (a.k / 128);
+inline int launch_prep(const PrepArgs& a, cudaStream_t st, const char* what) {
+    const long jobs = (long)a.rows * (a.k / 128);
     long blocks = (jobs + 7) / 8;
+    const long zb = (a.n_zero + 255) / 256;
+    if (blocks < zb) blocks = zb;
     if (blocks > 4 * num_sms()) blocks = 4 * num_sms();
     if (blocks < 1) blocks = 1;
-    cudaError_t e;
-    if (pdl) {
-        e = launch_pdl(k_prep, dim3((unsigned)blocks), dim3(256), 0, st, 1, a);
-    } else {
-        k_prep<<<(unsigned)blocks, 256, 0, st>>>(a);
-        e = cudaGetLastError();
-    }
+    cudaError_t e = launch_pdl(k_prep, dim3((unsigned)blocks), dim3(256), 0, st, a);
     if (e != cudaSuccess) {
         set_error("%s: prep launch failed: %s", what, cudaGetErrorString(e));
         return EXL3_ERR_CUDA;

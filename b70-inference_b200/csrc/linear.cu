@@ -143,9 +143,22 @@ int exl3_pack_gateup(const void* gate, const void* up, int H, int I, int Kg, int
     return EXL3_OK;
 }
 
-size_t exl3_gemv_workspace_size(int M, int k) {
-    if (M <= 0 || k <= 0) return 0;
-    return (size_t)M * k * 2 + 256;
+// Workspace of exl3_gemv: rotated input rows [M][k] fp16 | tickets [n/128] int32 | split-unit partial slots.
+struct GemvWs {
+    size_t xf, tickets, partial, total;
+};
+static GemvWs gemv_ws(int M, int k, int n) {
+    GemvWs w;
+    w.xf = 0;
+    w.tickets = align_up((size_t)M * k * 2, 256);
+    w.partial = align_up(w.tickets + (size_t)(n / 128) * 4, 256);
+    w.total = w.partial + partial_bytes(EPI_LINEAR);
+    return w;
+}
+
+size_t exl3_gemv_workspace_size(int M, int k, int n) {
+    if (M <= 0 || k <= 0 || n <= 0) return 0;
+    return gemv_ws(M, k, n).total;
 }
 
 int exl3_dequant(const void* trellis, int k, int n, int K, int cb, int n0, int n_slice, void* w, int ldw,
@@ -209,7 +222,7 @@ int exl3_silu_mul(const void* g, const void* u, void* z, int64_t count, float ac
 
 int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* packed, const void* suh, const void* svh,
               int k, int n, int K, int cb, void* y, int y_dtype, int ldy, void* workspace, size_t ws_bytes,
-              int split_k, void* stream) {
+              int n_ctas, void* stream) {
     EXL3_REQUIRE(cb == 2, EXL3_ERR_UNSUPPORTED, "exl3_gemv: only the mul1 codebook (cb=2) is supported");
     EXL3_REQUIRE(K >= 1 && K <= 8, EXL3_ERR_UNSUPPORTED, "exl3_gemv: K=%d not in 1..8", K);
     EXL3_REQUIRE(M >= 0 && M <= kMaxRows, EXL3_ERR_ARG, "exl3_gemv: M=%d rows (1..8 per call)", M);
@@ -224,24 +237,27 @@ int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* packed, co
                  "exl3_gemv: row strides ldx=%d ldy=%d", ldx, ldy);
     EXL3_REQUIRE((reinterpret_cast<uintptr_t>(x) & 7) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0,
                  EXL3_ERR_ARG, "exl3_gemv: x must be 8-byte and y 16-byte aligned");
-    EXL3_REQUIRE(split_k >= 0 && split_k <= kMaxCluster, EXL3_ERR_ARG, "exl3_gemv: split_k=%d (0..8)", split_k);
+    EXL3_REQUIRE(n_ctas >= 0, EXL3_ERR_ARG, "exl3_gemv: n_ctas=%d", n_ctas);
     if (M == 0) return EXL3_OK;
-    const size_t need = exl3_gemv_workspace_size(M, k);
-    EXL3_REQUIRE(workspace && ws_bytes >= need && aligned16(workspace), EXL3_ERR_WORKSPACE,
-                 "exl3_gemv: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, need);
+    const GemvWs W = gemv_ws(M, k, n);
+    EXL3_REQUIRE(workspace && ws_bytes >= W.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
+                 "exl3_gemv: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, W.total);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    __half* xf = static_cast<__half*>(workspace);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    __half* xf = reinterpret_cast<__half*>(ws + W.xf);
+    int* tickets = reinterpret_cast<int*>(ws + W.tickets);
 
     PrepArgs pa = {};
     pa.x = x;
     pa.ldx = ldx;
     pa.x_bf16 = x_dtype == EXL3_BF16;
     pa.rows = M;
-    pa.nmat = 1;
     pa.k = k;
-    pa.suh0 = static_cast<const __half*>(suh);
+    pa.suh = static_cast<const __half*>(suh);
     pa.xf = xf;
-    int rc = launch_prep(pa, st, "exl3_gemv", true);
+    pa.zero = tickets;
+    pa.n_zero = n / 128;
+    int rc = launch_prep(pa, st, "exl3_gemv");
     if (rc) return rc;
 
     GemvArgs a = {};
@@ -255,10 +271,11 @@ int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* packed, co
     a.xf = xf;
     a.k = k;
     a.n = n;
+    a.partial = reinterpret_cast<float*>(ws + W.partial);
+    a.counters = tickets;
     a.status = device_status_ptr();
-    const int units = n / 128;
-    const GemvPlan pl = plan_gemv(EPI_LINEAR, units, k, 256 * K, split_k);
-    return launch_gemv<EPI_LINEAR>(a, units, pl, st, "exl3_gemv");
+    const GemvPlan pl = plan_gemv(EPI_LINEAR, (long long)(n / 128) * (k / 128), n_ctas);
+    return launch_gemv<EPI_LINEAR>(a, pl, st, "exl3_gemv");
 }
 
 }  // extern "C"

@@ -1,33 +1,35 @@
-// MoE decode path: top-k router with residency bias, token/expert alignment, grouped gate|up and down GEMVs
-// (gemv.cuh), and the fixed-order combine.
+// MoE decode path: top-k router with residency bias, the prepare step (token/expert alignment + rotated activation
+// rows), grouped gate|up and down GEMVs (gemv.cuh), and the fixed-order combine.
 //
-// Workspace layout of exl3_moe_align / exl3_moe_decode (int32 words unless noted; P_max = pairs + shared rows):
-//   [0] n_items  [1] n_pairs_valid  [2] positions in use (valid pairs + shared rows)  [3..7] reserved
+// Workspace layout of exl3_moe_decode and its phases (int32 words unless noted; P = pairs + shared rows):
+//   [0] n_items  [1] n_valid (routed pair positions)  [2] positions in use (+ shared rows)  [3..7] reserved
 //   item_expert[max_items] item_start[max_items] item_cnt[max_items]
-//   pair_tok[P_max] pair_expert[P_max] pair_of[npairs] pair_w[P_max] (fp32)
-//   then (decode only, 256-byte aligned): gate|up input rows in xf order fp16 [P_max][2][H], down input rows in xf
-//   order fp16 [P_max][I], ybuf fp32 [P_max][H]
+//   pair_tok[P] pair_expert[P] pair_of[pairs] pair_w[P] (fp32) pair_src[P]
+//   tickets[max_items * max(H, I) / 128] (GEMV split-unit counters)
+//   then, 256-byte aligned: gate|up input rows in xf order fp16 [P][2][H] (row = routed pair index, or pairs + m for
+//   the shared expert's row of token m), down input rows in xf order fp16 [P][I] (by position), ybuf fp32 [P][H],
+//   GEMV split-unit partial slots.
 #include "gemv.cuh"
 
 namespace exl3 {
 
-// Rows per GEMV work item: the MMA's N (8), or fewer when the batch is smaller (an item never holds more rows than
-// the launch's activation buffer, which is sized for min(8, M) rows).
+// Rows per GEMV work item: the MMA's N (8), or fewer when the batch is smaller.
 inline int item_rows(int M) { return M < 8 ? (M > 0 ? M : 1) : 8; }
 
 struct WsLayout {
-    size_t item_expert, item_start, item_cnt, pair_tok, pair_expert, pair_of, pair_w, xf_gu, xf_dn, ybuf, total;
-    int max_items, p_max;
+    size_t item_expert, item_start, item_cnt, pair_tok, pair_expert, pair_of, pair_w, pair_src, tickets, xf_gu,
+        xf_dn, ybuf, partial, total;
+    int max_items, p_max, n_tickets;
 };
-
-__host__ __device__ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 inline WsLayout ws_layout(int M, int topk, int E, int H, int I, int shared, int chunk) {
     WsLayout L;
     const int npairs = M * topk;
     const int active = npairs < E ? npairs : E;
-    L.max_items = active + (npairs + chunk - 1) / chunk + (shared ? (M + chunk - 1) / chunk : 0);
+    // sum over active experts of ceil(count / chunk) <= (pairs + active (chunk - 1)) / chunk
+    L.max_items = (npairs + active * (chunk - 1)) / chunk + (shared ? (M + chunk - 1) / chunk : 0);
     L.p_max = npairs + (shared ? M : 0);
+    L.n_tickets = L.max_items * ((H > I ? H : I) / 128);
     size_t o = 8 * 4;
     L.item_expert = o; o += (size_t)L.max_items * 4;
     L.item_start = o; o += (size_t)L.max_items * 4;
@@ -36,10 +38,13 @@ inline WsLayout ws_layout(int M, int topk, int E, int H, int I, int shared, int 
     L.pair_expert = o; o += (size_t)L.p_max * 4;
     L.pair_of = o; o += (size_t)npairs * 4;
     L.pair_w = o; o += (size_t)L.p_max * 4;
+    L.pair_src = o; o += (size_t)L.p_max * 4;
+    L.tickets = o; o += (size_t)L.n_tickets * 4;
     o = align_up(o, 256);
     L.xf_gu = o; o += align_up((size_t)L.p_max * 2 * H * 2, 256);
     L.xf_dn = o; o += align_up((size_t)L.p_max * I * 2, 256);
-    L.ybuf = o; o += (size_t)L.p_max * H * 4;
+    L.ybuf = o; o += align_up((size_t)L.p_max * H * 4, 256);
+    L.partial = o; o += partial_bytes(EPI_GATEUP);
     L.total = o;
     return L;
 }
@@ -78,6 +83,7 @@ __global__ void __launch_bounds__(kRouteThreads) k_route(const float* __restrict
     __shared__ uint64_t s_red[kRouteThreads / 32];
     __shared__ int s_pick[kRouteMaxK];
     __shared__ double s_dred[kRouteThreads / 32];
+    pdl_wait();                                               // logits may come from the previous kernel
     const int row = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const float* l = logits + (size_t)row * ld;
 
@@ -209,16 +215,25 @@ __device__ __forceinline__ int block_excl_scan(int v, int* scan, int* total) {
     return incl - v;
 }
 
+struct AlignOut {
+    int* ws_i;
+    int* item_expert;
+    int* item_start;
+    int* item_cnt;
+    int* pair_tok;
+    int* pair_expert;
+    int* pair_of;
+    float* pair_w;
+    int* pair_src;
+};
+
 // One CTA. Pairs are split into 32 contiguous warp segments; per-(warp, expert) counts give every pair a stable
 // position (experts ascending, pair index ascending within an expert): deterministic, unlike an atomic fill
 // (glm/xpu/csrc/exl3_moe.n128.sycl:693-734 fills positions in atomic order). Items: ceil(count / chunk) per active
 // expert in expert order, then the shared expert's rows (expert id E, weight 1) at positions n_valid + m.
-__global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restrict__ ids, const float* __restrict__ w,
-                                                         int npairs, int topk, int E, int M, int shared, int chunk,
-                                                         int* ws_i, int* item_expert, int* item_start, int* item_cnt,
-                                                         int* pair_tok, int* pair_expert, int* pair_of,
-                                                         float* pair_w) {
-    extern __shared__ int sm[];
+// pair_src[position] = the routed pair index (the gate|up activation row), npairs + m for shared rows.
+__device__ void align_cta(const int32_t* __restrict__ ids, const float* __restrict__ w, int npairs, int topk, int E,
+                          int M, int shared, int chunk, const AlignOut& o, int* sm) {
     int* cnt = sm;                             // [kAlignWarps][E]
     int* scan = sm + kAlignWarps * E;          // [kAlignThreads]
     const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -248,9 +263,9 @@ __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restri
     const int ibase = block_excl_scan(nch, scan, &n_routed_items);
     const int shared_items = shared ? (M + chunk - 1) / chunk : 0;
     if (t == 0) {
-        ws_i[0] = n_routed_items + shared_items;
-        ws_i[1] = n_valid;
-        ws_i[2] = n_valid + (shared ? M : 0);
+        o.ws_i[0] = n_routed_items + shared_items;
+        o.ws_i[1] = n_valid;
+        o.ws_i[2] = n_valid + (shared ? M : 0);
     }
     __syncthreads();
     // stable placement: each warp walks its segment in order, 32 pairs at a time
@@ -265,12 +280,13 @@ __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restri
             const unsigned before = peers & ((1u << lane) - 1u);
             if (valid) {
                 const int pos = cnt[warp * E + e] + __popc(before);
-                pair_tok[pos] = i / topk;
-                pair_expert[pos] = e;
-                pair_w[pos] = w[i];
-                pair_of[i] = pos;
+                o.pair_tok[pos] = i / topk;
+                o.pair_expert[pos] = e;
+                o.pair_w[pos] = w[i];
+                o.pair_src[pos] = i;
+                o.pair_of[i] = pos;
             } else {
-                pair_of[i] = -1;
+                o.pair_of[i] = -1;
             }
             __syncwarp(amask);
             if (valid && before == 0) cnt[warp * E + e] += __popc(peers);
@@ -279,21 +295,90 @@ __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restri
     }
     if (t < E)
         for (int c = 0; c < nch; ++c) {
-            item_expert[ibase + c] = t;
-            item_start[ibase + c] = start + c * chunk;
-            item_cnt[ibase + c] = min(chunk, total - c * chunk);
+            o.item_expert[ibase + c] = t;
+            o.item_start[ibase + c] = start + c * chunk;
+            o.item_cnt[ibase + c] = min(chunk, total - c * chunk);
         }
     if (shared) {
         for (int m = t; m < M; m += kAlignThreads) {
-            pair_tok[n_valid + m] = m;
-            pair_expert[n_valid + m] = E;
-            pair_w[n_valid + m] = 1.0f;
+            o.pair_tok[n_valid + m] = m;
+            o.pair_expert[n_valid + m] = E;
+            o.pair_w[n_valid + m] = 1.0f;
+            o.pair_src[n_valid + m] = npairs + m;
         }
         for (int c = t; c < shared_items; c += kAlignThreads) {
-            item_expert[n_routed_items + c] = E;
-            item_start[n_routed_items + c] = n_valid + c * chunk;
-            item_cnt[n_routed_items + c] = min(chunk, M - c * chunk);
+            o.item_expert[n_routed_items + c] = E;
+            o.item_start[n_routed_items + c] = n_valid + c * chunk;
+            o.item_cnt[n_routed_items + c] = min(chunk, M - c * chunk);
         }
+    }
+}
+
+__global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restrict__ ids, const float* __restrict__ w,
+                                                         int npairs, int topk, int E, int M, int shared, int chunk,
+                                                         const AlignOut o) {
+    extern __shared__ int sm[];
+    pdl_wait();
+    align_cta(ids, w, npairs, topk, E, M, shared, chunk, o, sm);
+}
+
+// ------------------------------------------------------------------------------------------------ prepare
+
+// CTA 0 aligns (tables, tickets zeroed) and only then lets the gate|up GEMV launch: that kernel's producers read the
+// item table before their own griddepcontrol.wait. The other CTAs rotate the activation rows of every routed pair
+// (row = pair index: token i / topk, the picked expert's gate and up input signs) and of the shared expert's rows,
+// one warp per (row, matrix, 128-block); they need only ids, so they run beside the alignment.
+struct PrepareArgs {
+    const void* x;
+    int ldx, x_bf16;
+    const int32_t* ids;
+    const float* w;
+    int M, topk, E, shared, H, chunk;
+    const ExpertDesc* experts;
+    AlignOut o;
+    int* tickets;
+    int n_tickets;
+    __half* xf;                  // [P][2][H]
+};
+
+__global__ void __launch_bounds__(kAlignThreads) k_prepare(const PrepareArgs a) {
+    extern __shared__ int sm[];
+    pdl_wait();                                               // ids (router) and x come from earlier kernels
+    const int npairs = a.M * a.topk;
+    if (blockIdx.x == 0) {
+        for (int i = threadIdx.x; i < a.n_tickets; i += kAlignThreads) a.tickets[i] = 0;
+        align_cta(a.ids, a.w, npairs, a.topk, a.E, a.M, a.shared, a.chunk, a.o, sm);
+        __threadfence();
+        __syncthreads();
+        pdl_trigger();
+        return;
+    }
+    pdl_trigger();
+    const int KB = a.H / 128;
+    const int lane = threadIdx.x & 31;
+    const int rows = npairs + (a.shared ? a.M : 0);
+    const int jobs = rows * 2 * KB;
+    const int nw = (gridDim.x - 1) * (kAlignThreads / 32);
+    for (int j = (blockIdx.x - 1) * (kAlignThreads / 32) + (threadIdx.x >> 5); j < jobs; j += nw) {
+        const int row = j / (2 * KB), mat = (j / KB) % 2, kb = j % KB;
+        int tok, e;
+        if (row < npairs) {
+            e = a.ids[row];
+            if (e < 0 || e >= a.E) continue;                  // never read: the pair has no position
+            tok = row / a.topk;
+        } else {
+            tok = row - npairs;
+            e = a.E;
+        }
+        const __half* suh = a.experts[e].suh[mat];
+        const __half* su = suh ? suh + kb * 128 : nullptr;
+        float v[4];
+        if (a.x_bf16)
+            rotated_block<__nv_bfloat16>(
+                reinterpret_cast<const __nv_bfloat16*>(a.x) + (size_t)tok * a.ldx + kb * 128, su, lane, v);
+        else
+            rotated_block<__half>(reinterpret_cast<const __half*>(a.x) + (size_t)tok * a.ldx + kb * 128, su, lane, v);
+        store_xf_block(v, lane, a.xf + ((size_t)row * 2 + mat) * a.H + (size_t)kb * 128);
     }
 }
 
@@ -303,7 +388,7 @@ __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restri
 template <typename TOut>
 __global__ void k_combine(const float* __restrict__ ybuf, const int* __restrict__ pair_of, const int* ws_i, int M,
                           int H, int topk, int shared, TOut* out) {
-    asm volatile("griddepcontrol.wait;" ::: "memory");       // ybuf comes from the down kernel
+    pdl_wait();                                               // ybuf comes from the down kernel
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;     // one float4 of one row
     const int per_row = H / 4;
     if (idx >= M * per_row) return;
@@ -328,30 +413,183 @@ __global__ void k_combine(const float* __restrict__ ybuf, const int* __restrict_
     }
 }
 
-static int launch_align(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
-                        uint8_t* ws, const WsLayout& L, cudaStream_t st) {
-    const size_t smem = (size_t)(kAlignWarps * E + kAlignThreads) * 4;
-    EXL3_REQUIRE(smem <= 227 * 1024, EXL3_ERR_UNSUPPORTED, "moe align: E=%d too large", E);
-    static int configured[64] = {0};
+// ------------------------------------------------------------------------------------------------ host side
+
+static AlignOut align_out(uint8_t* ws, const WsLayout& L) {
+    AlignOut o;
+    o.ws_i = reinterpret_cast<int*>(ws);
+    o.item_expert = reinterpret_cast<int*>(ws + L.item_expert);
+    o.item_start = reinterpret_cast<int*>(ws + L.item_start);
+    o.item_cnt = reinterpret_cast<int*>(ws + L.item_cnt);
+    o.pair_tok = reinterpret_cast<int*>(ws + L.pair_tok);
+    o.pair_expert = reinterpret_cast<int*>(ws + L.pair_expert);
+    o.pair_of = reinterpret_cast<int*>(ws + L.pair_of);
+    o.pair_w = reinterpret_cast<float*>(ws + L.pair_w);
+    o.pair_src = reinterpret_cast<int*>(ws + L.pair_src);
+    return o;
+}
+
+template <typename Kern>
+static int set_max_smem_once(Kern kern, int* configured, const char* what) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        if (cudaFuncSetAttribute(k_align, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
-            set_error("moe align: cudaFuncSetAttribute: %s", cudaGetErrorString(cudaGetLastError()));
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) != cudaSuccess) {
+            set_error("%s: cudaFuncSetAttribute: %s", what, cudaGetErrorString(cudaGetLastError()));
             return EXL3_ERR_CUDA;
         }
         configured[dev] = 1;
     }
-    int* wi = reinterpret_cast<int*>(ws);
-    k_align<<<1, kAlignThreads, smem, st>>>(ids, w, M * topk, topk, E, M, shared, chunk, wi,
-                                            reinterpret_cast<int*>(ws + L.item_expert),
-                                            reinterpret_cast<int*>(ws + L.item_start),
-                                            reinterpret_cast<int*>(ws + L.item_cnt),
-                                            reinterpret_cast<int*>(ws + L.pair_tok),
-                                            reinterpret_cast<int*>(ws + L.pair_expert),
-                                            reinterpret_cast<int*>(ws + L.pair_of),
-                                            reinterpret_cast<float*>(ws + L.pair_w));
-    EXL3_LAUNCH_CHECK("moe align");
+    return EXL3_OK;
+}
+
+static size_t align_smem(int E) { return (size_t)(kAlignWarps * E + kAlignThreads) * 4; }
+
+static int launch_align(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
+                        uint8_t* ws, const WsLayout& L, cudaStream_t st) {
+    const size_t smem = align_smem(E);
+    EXL3_REQUIRE(smem <= 227 * 1024, EXL3_ERR_UNSUPPORTED, "moe align: E=%d too large", E);
+    static int configured[64] = {0};
+    int rc = set_max_smem_once(k_align, configured, "moe align");
+    if (rc) return rc;
+    cudaError_t e = launch_pdl(k_align, dim3(1), dim3(kAlignThreads), smem, st, ids, w, M * topk, topk, E, M, shared,
+                               chunk, align_out(ws, L));
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "moe align: launch failed: %s", cudaGetErrorString(e));
+    return EXL3_OK;
+}
+
+static int moe_check(int M, int topk, const exl3_expert* experts, int E, int H, int I, int n_ctas,
+                     const char* what) {
+    EXL3_REQUIRE(experts && M >= 0 && topk > 0 && E > 0, EXL3_ERR_ARG, "%s: bad arguments", what);
+    EXL3_REQUIRE(E <= 1024, EXL3_ERR_UNSUPPORTED, "%s: E=%d > 1024", what, E);
+    EXL3_REQUIRE(H % 128 == 0 && I % 128 == 0 && H > 0 && I > 0, EXL3_ERR_ARG,
+                 "%s: H=%d, I=%d must be multiples of 128", what, H, I);
+    EXL3_REQUIRE(n_ctas >= 0, EXL3_ERR_ARG, "%s: n_ctas=%d", what, n_ctas);
+    return EXL3_OK;
+}
+
+static int ws_check(void* workspace, size_t ws_bytes, const WsLayout& L, const char* what) {
+    EXL3_REQUIRE(workspace && ws_bytes >= L.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
+                 "%s: workspace %zu < %zu bytes (or not 16-byte aligned)", what, ws_bytes, L.total);
+    return EXL3_OK;
+}
+
+static int run_prepare(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w, int topk,
+                       const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
+                       size_t ws_bytes, cudaStream_t st) {
+    int rc = moe_check(M, topk, experts, E, H, I, 0, "exl3_moe_prepare");
+    if (rc || M == 0) return rc;
+    EXL3_REQUIRE(x && ids && w, EXL3_ERR_ARG, "exl3_moe_prepare: null pointer");
+    EXL3_REQUIRE(x_dtype == EXL3_F16 || x_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "exl3_moe_prepare: x dtype");
+    EXL3_REQUIRE(ldx >= H && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 7) == 0, EXL3_ERR_ARG,
+                 "exl3_moe_prepare: x rows must be 8-byte aligned (ldx=%d)", ldx);
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
+    rc = ws_check(workspace, ws_bytes, L, "exl3_moe_prepare");
+    if (rc) return rc;
+    const size_t smem = align_smem(E);
+    EXL3_REQUIRE(smem <= 227 * 1024, EXL3_ERR_UNSUPPORTED, "exl3_moe_prepare: E=%d too large", E);
+    static int configured[64] = {0};
+    rc = set_max_smem_once(k_prepare, configured, "exl3_moe_prepare");
+    if (rc) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    PrepareArgs a = {};
+    a.x = x;
+    a.ldx = ldx;
+    a.x_bf16 = x_dtype == EXL3_BF16;
+    a.ids = ids;
+    a.w = w;
+    a.M = M;
+    a.topk = topk;
+    a.E = E;
+    a.shared = shared;
+    a.H = H;
+    a.chunk = item_rows(M);
+    a.experts = reinterpret_cast<const ExpertDesc*>(experts);
+    a.o = align_out(ws, L);
+    a.tickets = reinterpret_cast<int*>(ws + L.tickets);
+    a.n_tickets = L.n_tickets;
+    a.xf = reinterpret_cast<__half*>(ws + L.xf_gu);
+    const long jobs = (long)L.p_max * 2 * (H / 128);
+    long ctas = (jobs + kAlignWarps - 1) / kAlignWarps;
+    if (ctas > 2 * num_sms()) ctas = 2 * num_sms();
+    cudaError_t e = launch_pdl(k_prepare, dim3((unsigned)(1 + ctas)), dim3(kAlignThreads), smem, st, a);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_moe_prepare: launch failed: %s", cudaGetErrorString(e));
+    return EXL3_OK;
+}
+
+static GemvArgs moe_args(const exl3_expert* experts, float act_limit, uint8_t* ws, const WsLayout& L) {
+    GemvArgs a = {};
+    a.experts = reinterpret_cast<const ExpertDesc*>(experts);
+    a.items.n_items = reinterpret_cast<const int*>(ws);
+    a.items.item_expert = reinterpret_cast<const int*>(ws + L.item_expert);
+    a.items.item_start = reinterpret_cast<const int*>(ws + L.item_start);
+    a.items.item_cnt = reinterpret_cast<const int*>(ws + L.item_cnt);
+    a.items.pair_src = reinterpret_cast<const int*>(ws + L.pair_src);
+    a.items.pair_w = reinterpret_cast<const float*>(ws + L.pair_w);
+    a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
+    a.act_limit = act_limit;
+    a.partial = reinterpret_cast<float*>(ws + L.partial);
+    a.counters = reinterpret_cast<int*>(ws + L.tickets);
+    a.status = device_status_ptr();
+    return a;
+}
+
+static int run_gateup(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I,
+                      float act_limit, void* workspace, size_t ws_bytes, int n_ctas, cudaStream_t st) {
+    int rc = moe_check(M, topk, experts, E, H, I, n_ctas, "exl3_moe_gateup");
+    if (rc || M == 0) return rc;
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
+    rc = ws_check(workspace, ws_bytes, L, "exl3_moe_gateup");
+    if (rc) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    GemvArgs a = moe_args(experts, act_limit, ws, L);
+    a.xf = reinterpret_cast<const __half*>(ws + L.xf_gu);
+    a.xf_out = reinterpret_cast<__half*>(ws + L.xf_dn);
+    a.k = H;
+    a.n = I;
+    const GemvPlan pl = plan_gemv(EPI_GATEUP, (long long)L.max_items * (I / 128) * (H / 128), n_ctas);
+    return launch_gemv<EPI_GATEUP>(a, pl, st, "exl3_moe_gateup");
+}
+
+static int run_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
+                    size_t ws_bytes, int n_ctas, cudaStream_t st) {
+    int rc = moe_check(M, topk, experts, E, H, I, n_ctas, "exl3_moe_down");
+    if (rc || M == 0) return rc;
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
+    rc = ws_check(workspace, ws_bytes, L, "exl3_moe_down");
+    if (rc) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    GemvArgs a = moe_args(experts, 0.f, ws, L);
+    a.xf = reinterpret_cast<const __half*>(ws + L.xf_dn);
+    a.k = I;
+    a.n = H;
+    const GemvPlan pl = plan_gemv(EPI_DOWN, (long long)L.max_items * (H / 128) * (I / 128), n_ctas);
+    return launch_gemv<EPI_DOWN>(a, pl, st, "exl3_moe_down");
+}
+
+static int run_combine(int M, int topk, int E, int shared, int H, int I, void* out, int out_dtype, void* workspace,
+                       size_t ws_bytes, cudaStream_t st) {
+    EXL3_REQUIRE(out && M >= 0 && topk > 0 && E > 0 && H % 128 == 0 && I % 128 == 0, EXL3_ERR_ARG,
+                 "exl3_moe_combine: bad arguments");
+    EXL3_REQUIRE(out_dtype == EXL3_F16 || out_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED, "exl3_moe_combine: out dtype");
+    if (M == 0) return EXL3_OK;
+    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
+    int rc = ws_check(workspace, ws_bytes, L, "exl3_moe_combine");
+    if (rc) return rc;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const float* ybuf = reinterpret_cast<const float*>(ws + L.ybuf);
+    const int* pair_of = reinterpret_cast<const int*>(ws + L.pair_of);
+    const int* wi = reinterpret_cast<const int*>(ws);
+    const int n4 = M * (H / 4);
+    const dim3 grid((n4 + 255) / 256);
+    cudaError_t e;
+    if (out_dtype == EXL3_F32)
+        e = launch_pdl(k_combine<float>, grid, dim3(256), 0, st, ybuf, pair_of, wi, M, H, topk, shared,
+                       static_cast<float*>(out));
+    else
+        e = launch_pdl(k_combine<__half>, grid, dim3(256), 0, st, ybuf, pair_of, wi, M, H, topk, shared,
+                       static_cast<__half*>(out));
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_moe_combine: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }
 
@@ -369,14 +607,14 @@ int exl3_route(const float* logits, int ld, int R, int E, int kind, int k, const
     EXL3_REQUIRE(k >= 1 && k <= kRouteMaxK && k <= E, EXL3_ERR_ARG, "exl3_route: k=%d", k);
     EXL3_REQUIRE(kind >= 0 && kind <= 2, EXL3_ERR_ARG, "exl3_route: kind=%d", kind);
     if (R == 0) return EXL3_OK;
-    k_route<<<R, kRouteThreads, 0, static_cast<cudaStream_t>(stream)>>>(logits, ld, E, kind, k, bias, res, mul, scale,
-                                                                        renorm, ids, ids64, w, want);
-    EXL3_LAUNCH_CHECK("exl3_route");
+    cudaError_t e = launch_pdl(k_route, dim3(R), dim3(kRouteThreads), 0, static_cast<cudaStream_t>(stream), logits,
+                               ld, E, kind, k, bias, res, mul, scale, renorm, ids, ids64, w, want);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_route: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }
 
 size_t exl3_moe_workspace_size(int M, int topk, int E, int H, int I, int shared) {
-    if (M <= 0 || topk <= 0 || E <= 0) return 0;
+    if (M <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
     return ws_layout(M, topk, E, H, I, shared, item_rows(M)).total;
 }
 
@@ -391,124 +629,22 @@ int exl3_moe_align(const int32_t* ids, const float* w, int M, int topk, int E, i
                         static_cast<cudaStream_t>(stream));
 }
 
-static int moe_check(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
-                     int H, int I, int split_k, const char* what) {
-    EXL3_REQUIRE(experts && M >= 0 && topk > 0 && E > 0, EXL3_ERR_ARG, "%s: bad arguments", what);
-    EXL3_REQUIRE(E <= 1024, EXL3_ERR_UNSUPPORTED, "%s: E=%d > 1024", what, E);
-    EXL3_REQUIRE(H % 128 == 0 && I % 128 == 0 && H > 0 && I > 0, EXL3_ERR_ARG,
-                 "%s: H=%d, I=%d must be multiples of 128", what, H, I);
-    if (x) {
-        EXL3_REQUIRE(x_dtype == EXL3_F16 || x_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "%s: x dtype", what);
-        EXL3_REQUIRE(ldx >= H && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 7) == 0, EXL3_ERR_ARG,
-                     "%s: x rows must be 8-byte aligned (ldx=%d)", what, ldx);
-    }
-    EXL3_REQUIRE(split_k >= 0 && split_k <= kMaxCluster, EXL3_ERR_ARG, "%s: split_k=%d", what, split_k);
-    return EXL3_OK;
+int exl3_moe_prepare(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w, int topk,
+                     const exl3_expert* experts, int E, int shared, int H, int I, void* workspace, size_t ws_bytes,
+                     void* stream) {
+    return run_prepare(x, x_dtype, ldx, M, ids, w, topk, experts, E, shared, H, I, workspace, ws_bytes,
+                       static_cast<cudaStream_t>(stream));
 }
 
-static GemvArgs moe_args(const exl3_expert* experts, float act_limit, uint8_t* ws, const WsLayout& L) {
-    GemvArgs a = {};
-    a.experts = reinterpret_cast<const ExpertDesc*>(experts);
-    a.items.n_items = reinterpret_cast<const int*>(ws);
-    a.items.item_expert = reinterpret_cast<const int*>(ws + L.item_expert);
-    a.items.item_start = reinterpret_cast<const int*>(ws + L.item_start);
-    a.items.item_cnt = reinterpret_cast<const int*>(ws + L.item_cnt);
-    a.items.pair_tok = reinterpret_cast<const int*>(ws + L.pair_tok);
-    a.items.pair_w = reinterpret_cast<const float*>(ws + L.pair_w);
-    a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
-    a.act_limit = act_limit;
-    a.status = device_status_ptr();
-    return a;
-}
-
-static int bits_hint(int max_bits) { return max_bits >= 1 && max_bits <= 8 ? max_bits : 8; }
-
-static int run_gateup(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
-                      int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes, int max_bits,
-                      int split_k, cudaStream_t st) {
-    int rc = moe_check(x, x_dtype, ldx, M, topk, experts, E, H, I, split_k, "exl3_moe_gateup");
-    if (rc || M == 0) return rc;
-    EXL3_REQUIRE(x, EXL3_ERR_ARG, "exl3_moe_gateup: null x");
-    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
-    EXL3_REQUIRE(workspace && ws_bytes >= L.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
-                 "exl3_moe_gateup: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, L.total);
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    // rotated, quantised input rows of every pair position (gate and up signs of the position's expert)
-    PrepArgs pa = {};
-    pa.x = x;
-    pa.ldx = ldx;
-    pa.x_bf16 = x_dtype == EXL3_BF16;
-    pa.rows = L.p_max;
-    pa.nmat = 2;
-    pa.k = H;
-    pa.row_tok = reinterpret_cast<const int*>(ws + L.pair_tok);
-    pa.row_expert = reinterpret_cast<const int*>(ws + L.pair_expert);
-    pa.experts = reinterpret_cast<const ExpertDesc*>(experts);
-    pa.n_rows_dev = reinterpret_cast<const int*>(ws) + 2;
-    pa.xf = reinterpret_cast<__half*>(ws + L.xf_gu);
-    rc = launch_prep(pa, st, "exl3_moe_gateup", false);
-    if (rc) return rc;
-    GemvArgs a = moe_args(experts, act_limit, ws, L);
-    a.xf = pa.xf;
-    a.xf_out = reinterpret_cast<__half*>(ws + L.xf_dn);
-    a.k = H;
-    a.n = I;
-    const int units = L.max_items * (I / 128);
-    const GemvPlan pl = plan_gemv(EPI_GATEUP, units, H, 512 * bits_hint(max_bits), split_k);
-    return launch_gemv<EPI_GATEUP>(a, units, pl, st, "exl3_moe_gateup");
-}
-
-static int run_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
-                    size_t ws_bytes, int max_bits, int split_k, cudaStream_t st) {
-    int rc = moe_check(nullptr, 0, 0, M, topk, experts, E, H, I, split_k, "exl3_moe_down");
-    if (rc || M == 0) return rc;
-    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
-    EXL3_REQUIRE(workspace && ws_bytes >= L.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
-                 "exl3_moe_down: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, L.total);
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    GemvArgs a = moe_args(experts, 0.f, ws, L);
-    a.xf = reinterpret_cast<const __half*>(ws + L.xf_dn);
-    a.k = I;
-    a.n = H;
-    const int units = L.max_items * (H / 128);
-    const GemvPlan pl = plan_gemv(EPI_DOWN, units, I, 256 * bits_hint(max_bits), split_k);
-    return launch_gemv<EPI_DOWN>(a, units, pl, st, "exl3_moe_down");
-}
-
-static int run_combine(int M, int topk, int E, int shared, int H, int I, void* out, int out_dtype, void* workspace,
-                       size_t ws_bytes, cudaStream_t st) {
-    EXL3_REQUIRE(out && M >= 0 && topk > 0 && H % 128 == 0, EXL3_ERR_ARG, "exl3_moe_combine: bad arguments");
-    EXL3_REQUIRE(out_dtype == EXL3_F16 || out_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED, "exl3_moe_combine: out dtype");
-    if (M == 0) return EXL3_OK;
-    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
-    EXL3_REQUIRE(workspace && ws_bytes >= L.total, EXL3_ERR_WORKSPACE, "exl3_moe_combine: workspace too small");
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
-    const float* ybuf = reinterpret_cast<const float*>(ws + L.ybuf);
-    const int* pair_of = reinterpret_cast<const int*>(ws + L.pair_of);
-    const int* wi = reinterpret_cast<const int*>(ws);
-    const int n4 = M * (H / 4);
-    const dim3 grid((n4 + 255) / 256);
-    cudaError_t e;
-    if (out_dtype == EXL3_F32)
-        e = launch_pdl(k_combine<float>, grid, dim3(256), 0, st, 1, ybuf, pair_of, wi, M, H, topk, shared,
-                       static_cast<float*>(out));
-    else
-        e = launch_pdl(k_combine<__half>, grid, dim3(256), 0, st, 1, ybuf, pair_of, wi, M, H, topk, shared,
-                       static_cast<__half*>(out));
-    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_moe_combine: launch failed: %s", cudaGetErrorString(e));
-    return EXL3_OK;
-}
-
-int exl3_moe_gateup(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
-                    int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes, int max_bits,
-                    int split_k, void* stream) {
-    return run_gateup(x, x_dtype, ldx, M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, max_bits,
-                      split_k, static_cast<cudaStream_t>(stream));
+int exl3_moe_gateup(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I, float act_limit,
+                    void* workspace, size_t ws_bytes, int n_ctas, void* stream) {
+    return run_gateup(M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, n_ctas,
+                      static_cast<cudaStream_t>(stream));
 }
 
 int exl3_moe_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
-                  size_t ws_bytes, int max_bits, int split_k, void* stream) {
-    return run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, max_bits, split_k,
+                  size_t ws_bytes, int n_ctas, void* stream) {
+    return run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, n_ctas,
                     static_cast<cudaStream_t>(stream));
 }
 
@@ -520,22 +656,18 @@ int exl3_moe_combine(int M, int topk, int E, int shared, int H, int I, void* out
 
 int exl3_moe_decode(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w, int topk,
                     const exl3_expert* experts, int E, int shared, int H, int I, float act_limit, void* out,
-                    int out_dtype, void* workspace, size_t ws_bytes, int max_bits, int split_k, void* stream) {
-    int rc = moe_check(x, x_dtype, ldx, M, topk, experts, E, H, I, split_k, "exl3_moe_decode");
+                    int out_dtype, void* workspace, size_t ws_bytes, int n_ctas, void* stream) {
+    int rc = moe_check(M, topk, experts, E, H, I, n_ctas, "exl3_moe_decode");
     if (rc) return rc;
-    EXL3_REQUIRE(x && ids && w && out, EXL3_ERR_ARG, "exl3_moe_decode: null pointer");
+    EXL3_REQUIRE(out, EXL3_ERR_ARG, "exl3_moe_decode: null out");
     EXL3_REQUIRE(out_dtype == EXL3_F16 || out_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED, "exl3_moe_decode: out dtype");
     if (M == 0) return EXL3_OK;
-    const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
-    EXL3_REQUIRE(workspace && ws_bytes >= L.total && aligned16(workspace), EXL3_ERR_WORKSPACE,
-                 "exl3_moe_decode: workspace %zu < %zu bytes (or not 16-byte aligned)", ws_bytes, L.total);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    rc = launch_align(ids, w, M, topk, E, shared, item_rows(M), static_cast<uint8_t*>(workspace), L, st);
+    rc = run_prepare(x, x_dtype, ldx, M, ids, w, topk, experts, E, shared, H, I, workspace, ws_bytes, st);
     if (rc) return rc;
-    rc = run_gateup(x, x_dtype, ldx, M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, max_bits,
-                    split_k, st);
+    rc = run_gateup(M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, n_ctas, st);
     if (rc) return rc;
-    rc = run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, max_bits, split_k, st);
+    rc = run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, n_ctas, st);
     if (rc) return rc;
     return run_combine(M, topk, E, shared, H, I, out, out_dtype, workspace, ws_bytes, st);
 }

@@ -106,7 +106,7 @@ class ExpertTable:
 
 def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, table: ExpertTable,
                 act_limit: float = 0.0, out_dtype=torch.float32, out: torch.Tensor | None = None,
-                workspace: torch.Tensor | None = None, split_k: int = 0, events: dict | None = None) -> torch.Tensor:
+                workspace: torch.Tensor | None = None, n_ctas: int = 0, events: dict | None = None) -> torch.Tensor:
     """Routed MoE sum (+ the table's shared expert, weight 1) for x [M, H] fp16/bf16:
     out[m] = sum_j topk_w[m, j] * expert_{topk_ids[m, j]}(x[m]) + shared(x[m]), fp32 (or fp16) [M, H].
     topk_ids int32 [M, k] (other int types converted; ids < 0 or >= E skipped), topk_w fp32 [M, k].
@@ -138,23 +138,22 @@ def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, t
         rc = lib.exl3_moe_decode(x2.data_ptr(), L.dtype_code(x2.dtype), x2.stride(0), M, ids.data_ptr(),
                                  w.data_ptr(), k, table.table.data_ptr(), table.E, shared, H, table.I,
                                  float(act_limit), out.data_ptr(), L.dtype_code(out.dtype), ws.data_ptr(), ws.numel(),
-                                 table.max_bits, int(split_k), st)
+                                 int(n_ctas), st)
         L.check(rc, "moe_forward")
         return out
     # the same launches one phase at a time, with CUDA events around the two GEMV kernels
-    L.check(lib.exl3_moe_align(ids.data_ptr(), w.data_ptr(), M, k, table.E, shared, min(8, M), ws.data_ptr(),
-                                ws.numel(), st),
-            "moe_forward align")
+    L.check(lib.exl3_moe_prepare(x2.data_ptr(), L.dtype_code(x2.dtype), x2.stride(0), M, ids.data_ptr(),
+                                 w.data_ptr(), k, table.table.data_ptr(), table.E, shared, H, table.I, ws.data_ptr(),
+                                 ws.numel(), st), "moe_forward prepare")
     ext = bool(events.get("external", False))      # event record nodes when captured in a CUDA graph
     e0, e1, e2, e3 = (torch.cuda.Event(enable_timing=True, external=ext) for _ in range(4))
     e0.record()
-    L.check(lib.exl3_moe_gateup(x2.data_ptr(), L.dtype_code(x2.dtype), x2.stride(0), M, k, table.table.data_ptr(),
-                                table.E, shared, H, table.I, float(act_limit), ws.data_ptr(), ws.numel(),
-                                table.max_bits, int(split_k), st), "moe_forward gate|up")
+    L.check(lib.exl3_moe_gateup(M, k, table.table.data_ptr(), table.E, shared, H, table.I, float(act_limit),
+                                ws.data_ptr(), ws.numel(), int(n_ctas), st), "moe_forward gate|up")
     e1.record()
     e2.record()
     L.check(lib.exl3_moe_down(M, k, table.table.data_ptr(), table.E, shared, H, table.I, ws.data_ptr(), ws.numel(),
-                              table.max_bits, int(split_k), st), "moe_forward down")
+                              int(n_ctas), st), "moe_forward down")
     e3.record()
     L.check(lib.exl3_moe_combine(M, k, table.E, shared, H, table.I, out.data_ptr(), L.dtype_code(out.dtype),
                                  ws.data_ptr(), ws.numel(), st), "moe_forward combine")
@@ -165,15 +164,16 @@ def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, t
 
 def moe_align(topk_ids: torch.Tensor, topk_w: torch.Tensor, E: int, shared: bool = False, chunk: int = 8):
     """Alignment tables as tensors (the reference's debug moe_align, glm/xpu/csrc/exl3_moe.n128.sycl:1442-1450):
-    dict of n_items, n_valid, item_expert/start/cnt, pair_tok, pair_of, pair_w."""
+    dict of n_items, n_valid, item_expert/start/cnt, pair_tok, pair_expert, pair_of, pair_w, pair_src."""
     ids = topk_ids.to(torch.int32).contiguous()
     w = topk_w.to(torch.float32).contiguous()
     M, k = ids.shape
     npairs = M * k
     active = min(npairs, E)
-    max_items = active + (npairs + chunk - 1) // chunk + ((M + chunk - 1) // chunk if shared else 0)
+    shared_items = (M + chunk - 1) // chunk if shared else 0
+    max_items = (npairs + active * (chunk - 1)) // chunk + shared_items
     p_max = npairs + (M if shared else 0)
-    nbytes = 32 + 4 * (3 * max_items + 3 * p_max + npairs) + 256
+    nbytes = 32 + 4 * (3 * max_items + 4 * p_max + npairs + max_items)     # tables + tickets (moe.cu layout)
     ws = torch.zeros(nbytes + 4096, dtype=torch.uint8, device=ids.device)
     rc = L.lib().exl3_moe_align(ids.data_ptr(), w.data_ptr(), M, k, E, int(shared), chunk, ws.data_ptr(), ws.numel(),
                                 L.stream_of(ids))
@@ -186,7 +186,8 @@ def moe_align(topk_ids: torch.Tensor, topk_w: torch.Tensor, E: int, shared: bool
     pair_tok = wi[o:o + p_max]; o += p_max
     pair_expert = wi[o:o + p_max]; o += p_max
     pair_of = wi[o:o + npairs]; o += npairs
-    pair_w = wi[o:o + p_max].view(torch.float32)
+    pair_w = wi[o:o + p_max].view(torch.float32); o += p_max
+    pair_src = wi[o:o + p_max]; o += p_max
     n_items = int(wi[0])
     n_valid = int(wi[1])
     n_pos = n_valid + (M if shared else 0)
@@ -194,7 +195,7 @@ def moe_align(topk_ids: torch.Tensor, topk_w: torch.Tensor, E: int, shared: bool
                 item_expert=item_expert[:n_items].clone(),
                 item_start=item_start[:n_items].clone(), item_cnt=item_cnt[:n_items].clone(),
                 pair_tok=pair_tok[:n_valid + (M if shared else 0)].clone(), pair_of=pair_of.clone(),
-                pair_w=pair_w[:n_valid + (M if shared else 0)].clone())
+                pair_w=pair_w[:n_valid + (M if shared else 0)].clone(), pair_src=pair_src[:n_pos].clone())
 
 
 class BlockSparseMLP:

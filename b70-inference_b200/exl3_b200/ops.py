@@ -47,18 +47,18 @@ def pack_gateup(gate: torch.Tensor, up: torch.Tensor, Kg: int, Ku: int) -> torch
 
 
 def exl3_gemv(x: torch.Tensor, packed: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
-              y: torch.Tensor, split_k: int = 0, workspace: torch.Tensor | None = None) -> None:
+              y: torch.Tensor, n_ctas: int = 0, workspace: torch.Tensor | None = None) -> None:
     """y[M, n] = Had(Had(x * suh) @ W_hat) * svh for M <= 8 rows; packed = pack(trellis, K); y fp16/bf16/fp32
-    preallocated (C ABI exl3_gemv)."""
+    preallocated (C ABI exl3_gemv). n_ctas: CTAs of the persistent launch (0 = one per SM)."""
     L.require_cuda(x, packed, y)
     M, k = x.shape
     n = svh.shape[0]
     lib = L.lib()
-    need = lib.exl3_gemv_workspace_size(M, k)
+    need = lib.exl3_gemv_workspace_size(M, k, n)
     ws = workspace if workspace is not None else L.workspace(x.device, need, "gemv")
     rc = lib.exl3_gemv(x.data_ptr(), L.dtype_code(x.dtype), x.stride(0), M, packed.data_ptr(), L.ptr(suh),
                        svh.data_ptr(), k, n, int(K), 2, y.data_ptr(), L.dtype_code(y.dtype), y.stride(0),
-                       ws.data_ptr(), ws.numel(), int(split_k), L.stream_of(x))
+                       ws.data_ptr(), ws.numel(), int(n_ctas), L.stream_of(x))
     L.check(rc, "exl3_gemv")
 
 

@@ -93,15 +93,16 @@ EXL3_API int exl3_pack_gateup(const void* gate, const void* up, int H, int I, in
  * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for M <= 8 rows (larger M: call per 8-row chunk, or use the
  * reconstruct + GEMM path); x fp16 or bf16 (x_dtype), y fp16/bf16/fp32 (y_dtype) with row strides ldx, ldy.
  * packed = the weights in the packed layout (exl3_pack). k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2.
- * workspace >= exl3_gemv_workspace_size(M, k) bytes (the rotated input rows). split_k = CTAs per cluster along k
- * (0 = auto). Weights are decoded to the reference's fp16 values bit for bit and multiplied with fp32
- * accumulation; results differ from the reference only by summation order.
+ * workspace >= exl3_gemv_workspace_size(M, k, n) bytes (rotated input rows, split-unit reduction state; calls that
+ * share a workspace must be ordered on one stream). n_ctas = CTAs of the persistent launch (0 = one per SM).
+ * Weights are decoded to the reference's fp16 values bit for bit and multiplied with fp32 accumulation; results
+ * differ from the reference only by summation order, and are identical from call to call for one n_ctas.
  * Replaces exl3_gemm_small (glm/xpu/csrc/exl3_ops.sycl:258-321) / exllamav3 exl3_gemm
  * (glm/docs/ext-op-inventory.md:498-557) as called by BC_LinearEXL3.run (glm/xpu/glm_xpu/ops.py:60-80). */
-EXL3_API size_t exl3_gemv_workspace_size(int M, int k);
+EXL3_API size_t exl3_gemv_workspace_size(int M, int k, int n);
 EXL3_API int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* packed, const void* suh,
                        const void* svh, int k, int n, int K, int cb, void* y, int y_dtype, int ldy, void* workspace,
-                       size_t ws_bytes, int split_k, void* stream);
+                       size_t ws_bytes, int n_ctas, void* stream);
 
 /* ---- activation ----
  * z = fp16(min(silu(g), L) * clamp(u, -L, L)), L = act_limit (0 disables the clamps); fp32 math.
@@ -130,31 +131,32 @@ EXL3_API int exl3_route(const float* logits, int ld, int R, int E, int kind, int
  * x fp16/bf16 [M][H] (row stride ldx); ids int32 [M][topk] (ids < 0 or >= E skipped); w fp32 [M][topk];
  * experts: device array of E (+1 shared) exl3_expert. H % 128 == 0, I % 128 == 0.
  * Each expert is read once per call whatever number of rows picked it (rows grouped 8 per work item).
- * max_bits = the largest K of any expert matrix (sizes the launch; 0 = assume 8).
+ * n_ctas = CTAs of the persistent GEMV launches (0 = one per SM).
  * Replaces exl3xpu_moe::moe_forward (glm/xpu/csrc/exl3_moe.n128.sycl:1338-1439) and exllamav3
  * BC_BlockSparseMLP::run_bszN (glm/docs/ext-op-inventory.md:1030-1041). */
 EXL3_API size_t exl3_moe_workspace_size(int M, int topk, int E, int H, int I, int shared);
 EXL3_API int exl3_moe_decode(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w, int topk,
                     const exl3_expert* experts, int E, int shared, int H, int I, float act_limit, void* out,
-                    int out_dtype, void* workspace, size_t ws_bytes, int max_bits, int split_k, void* stream);
+                    int out_dtype, void* workspace, size_t ws_bytes, int n_ctas, void* stream);
 
-/* The phases of exl3_moe_decode as separate launches on one workspace, in order: exl3_moe_align (below),
- * exl3_moe_gateup (gate|up GEMVs + activation + down-input rotation -> activation rows in the workspace),
- * exl3_moe_down (down GEMVs x routing weight -> per-pair rows), exl3_moe_combine (fixed-order sum into out).
- * Same arguments and constraints as exl3_moe_decode; exl3_moe_align must use chunk = min(8, M).
- * Replace the reference's GateUpKernel / DownKernel / CombineKernel launches
+/* The phases of exl3_moe_decode as separate launches on one workspace, in order: exl3_moe_prepare (alignment of
+ * pairs into per-expert items + the rotated gate/up input rows), exl3_moe_gateup (gate|up GEMVs + activation +
+ * down-input rotation -> activation rows in the workspace), exl3_moe_down (down GEMVs x routing weight -> per-pair
+ * rows), exl3_moe_combine (fixed-order sum into out). Same arguments and constraints as exl3_moe_decode.
+ * Replace the reference's moe_align / GateUpKernel / DownKernel / CombineKernel launches
  * (glm/xpu/csrc/exl3_moe.n128.sycl:736-790,1418-1438). */
-EXL3_API int exl3_moe_gateup(const void* x, int x_dtype, int ldx, int M, int topk, const exl3_expert* experts, int E,
-                             int shared, int H, int I, float act_limit, void* workspace, size_t ws_bytes,
-                             int max_bits, int split_k, void* stream);
+EXL3_API int exl3_moe_prepare(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w,
+                              int topk, const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
+                              size_t ws_bytes, void* stream);
+EXL3_API int exl3_moe_gateup(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I,
+                             float act_limit, void* workspace, size_t ws_bytes, int n_ctas, void* stream);
 EXL3_API int exl3_moe_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I,
-                           void* workspace, size_t ws_bytes, int max_bits, int split_k, void* stream);
+                           void* workspace, size_t ws_bytes, int n_ctas, void* stream);
 EXL3_API int exl3_moe_combine(int M, int topk, int E, int shared, int H, int I, void* out, int out_dtype,
                               void* workspace, size_t ws_bytes, void* stream);
 
-/* Alignment step of exl3_moe_decode on its own (debug / reuse): writes into the workspace the item table and the
- * pair permutation, in the layout documented in moe.cu. Replaces moe_align
- * (glm/xpu/csrc/exl3_moe.n128.sycl:1442-1450). */
+/* Alignment step on its own (debug / reuse): writes into the workspace the item table and the pair permutation, in
+ * the layout documented in moe.cu. Replaces moe_align (glm/xpu/csrc/exl3_moe.n128.sycl:1442-1450). */
 EXL3_API int exl3_moe_align(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
                    void* workspace, size_t ws_bytes, void* stream);
 

@@ -30,6 +30,11 @@ def rand_linear(rng, k, n, K):
     return tr, suh, svh
 
 
+def poisoned_workspace(nbytes):
+    """A workspace of 0xFF bytes (NaN as fp32, -1 as int32): nothing may depend on its previous contents."""
+    return torch.full((nbytes,), 255, dtype=torch.uint8, device=DEV)
+
+
 @pytest.fixture(autouse=True)
 def _status_clean():
     L.lib().exl3_device_status(1)
@@ -108,25 +113,28 @@ def test_gemv_matches_oracle(K, M):
     tr, suh, svh = rand_linear(rng, k, n, K)
     x = rng.standard_normal((M, k)).astype(np.float16)
     for y_dt, np_dt in ((torch.float32, np.float32), (torch.float16, np.float16)):
-        y = torch.empty((M, n), dtype=y_dt, device=DEV)
+        y = torch.full((M, n), float("nan"), dtype=y_dt, device=DEV)
         ops.exl3_gemv(to_dev(x), ops.pack(to_dev(tr), K), to_dev(suh), to_dev(svh), K, y)
         ref = O.exl3_linear(x, tr, suh, svh, K, np_dt)
         assert_close(y.float().cpu().numpy(), ref.astype(np.float32), what=f"gemv K={K} M={M} {y_dt}")
 
 
-@pytest.mark.parametrize("split", [1, 2, 3, 4, 8])
-def test_gemv_split_k_is_consistent(split):
+@pytest.mark.parametrize("groups", [1, 2, 3, 7, 64, 0])
+def test_gemv_cta_counts_are_consistent(groups):
+    """Any CTA count (1 = every unit whole in one CTA; many = units split over CTAs and reduced through the tickets)
+    gives the oracle's result, bit-identically from call to call."""
     rng = np.random.default_rng(77)
     k, n, K, M = 1024, 256, 3, 4
     tr, suh, svh = rand_linear(rng, k, n, K)
     x = rng.standard_normal((M, k)).astype(np.float16)
-    y = torch.empty((M, n), dtype=torch.float32, device=DEV)
+    y = torch.full((M, n), float("nan"), dtype=torch.float32, device=DEV)
     pk = ops.pack(to_dev(tr), K)
-    ops.exl3_gemv(to_dev(x), pk, to_dev(suh), to_dev(svh), K, y, split_k=split)
-    assert_close(y.cpu().numpy(), O.exl3_linear(x, tr, suh, svh, K, np.float32), what=f"split {split}")
-    y2 = torch.empty_like(y)
-    ops.exl3_gemv(to_dev(x), pk, to_dev(suh), to_dev(svh), K, y2, split_k=split)
-    assert torch.equal(y, y2), "fixed-order split-K reduction must be deterministic"
+    ws = poisoned_workspace(L.lib().exl3_gemv_workspace_size(M, k, n))
+    ops.exl3_gemv(to_dev(x), pk, to_dev(suh), to_dev(svh), K, y, n_ctas=groups, workspace=ws)
+    assert_close(y.cpu().numpy(), O.exl3_linear(x, tr, suh, svh, K, np.float32), what=f"groups {groups}")
+    y2 = torch.full_like(y, float("nan"))
+    ops.exl3_gemv(to_dev(x), pk, to_dev(suh), to_dev(svh), K, y2, n_ctas=groups, workspace=ws)
+    assert torch.equal(y, y2), "fixed-order split-unit reduction must be deterministic"
 
 
 def test_gemv_bf16_input_and_output():
@@ -185,7 +193,7 @@ def test_gemv_full_size_against_torch(k, n, K):
     suh = (torch.randint(0, 2, (k,), device=DEV, generator=g) * 2 - 1).half()
     svh = (torch.randint(0, 2, (n,), device=DEV, generator=g) * 2 - 1).half()
     x = torch.randn((4, k), device=DEV, generator=g).half()
-    y = torch.empty((4, n), dtype=torch.float32, device=DEV)
+    y = torch.full((4, n), float("nan"), dtype=torch.float32, device=DEV)
     ops.exl3_gemv(x, ops.pack(tr, K), suh, svh, K, y)
     W = torch.empty((k, n), dtype=torch.half, device=DEV)
     ops.exl3_reconstruct(tr, W, 0, K)

@@ -23,6 +23,11 @@ def to_dev(a):
     return t.to(DEV)
 
 
+def poisoned(nbytes):
+    """A workspace of 0xFF bytes (NaN as fp32, -1 as int32): nothing may depend on its previous contents."""
+    return torch.full((nbytes,), 255, dtype=torch.uint8, device=DEV)
+
+
 @pytest.fixture(autouse=True)
 def _status_clean():
     L.lib().exl3_device_status(1)
@@ -114,6 +119,9 @@ def test_align_matches_oracle(M, k, E, shared):
     assert np.array_equal(a["pair_of"].cpu().numpy(), ref["pair_of"])
     assert np.array_equal(a["pair_tok"].cpu().numpy()[:nv], ref["pair_tok"])
     assert np.array_equal(a["pair_w"].cpu().numpy()[:nv], w.reshape(-1)[ref["pair_src"]])
+    assert np.array_equal(a["pair_src"].cpu().numpy()[:nv], ref["pair_src"])
+    if shared:
+        assert np.array_equal(a["pair_src"].cpu().numpy()[nv:], M * k + np.arange(M))
     # items: ceil(count / 8) per active expert, in expert order
     exp_items = []
     for e, s0, c in zip(ref["act_expert"], ref["act_start"], ref["act_cnt"]):
@@ -172,6 +180,13 @@ def test_moe_decode_matches_oracle(M, shared):
     assert_close(out.cpu().numpy(), ref, what=f"moe M={M} shared={shared}")
     out2 = moe.moe_forward(to_dev(x), to_dev(ids), to_dev(w), table, Lc)
     assert torch.equal(out, out2), "MoE decode must be deterministic"
+    # the phase-by-phase launches compute the same thing; any k-group count matches the oracle
+    need = L.lib().exl3_moe_workspace_size(M, topk, E, H, I, int(shared))
+    out3 = moe.moe_forward(to_dev(x), to_dev(ids), to_dev(w), table, Lc, events={}, workspace=poisoned(need))
+    assert torch.equal(out, out3)
+    for groups in (1, 3, 11):
+        og = moe.moe_forward(to_dev(x), to_dev(ids), to_dev(w), table, Lc, n_ctas=groups, workspace=poisoned(need))
+        assert_close(og.cpu().numpy(), ref, what=f"moe M={M} ctas={groups}")
 
 
 def test_moe_decode_no_clamp_and_bf16_input():
@@ -185,6 +200,22 @@ def test_moe_decode_no_clamp_and_bf16_input():
     out = moe.moe_forward(xb.to(DEV), to_dev(ids), to_dev(w), table, 0.0)
     ref = O.moe_forward(xb.float().numpy(), ids, w, np_exp, 0.0)
     assert_close(out.cpu().numpy(), ref, what="bf16 no clamp")
+
+
+def test_moe_decode_benchmark_shape():
+    """The benchmark's layer shape (H 2048, I 512, top-10 of many experts, 4 tokens): every GEMV unit is split over
+    several CTAs, so the ticketed reduction carries the whole result."""
+    rng = np.random.default_rng(123)
+    E, H, I, topk, M = 48, 2048, 512, 10, 4
+    np_exp, dev_exp, _, _ = make_experts(rng, E, H, I, [(3, 3, 3)] * E)
+    table = moe.ExpertTable(dev_exp)
+    x = rng.standard_normal((M, H)).astype(np.float16)
+    ids = np.stack([rng.permutation(E)[:topk] for _ in range(M)]).astype(np.int32)
+    w = rng.random((M, topk)).astype(np.float32)
+    need = L.lib().exl3_moe_workspace_size(M, topk, E, H, I, 0)
+    out = moe.moe_forward(to_dev(x), to_dev(ids), to_dev(w), table, 0.0, workspace=poisoned(need))
+    ref = O.moe_forward(x, ids, w, np_exp, 0.0)
+    assert_close(out.cpu().numpy(), ref, what="moe benchmark shape")
 
 
 def test_moe_golden_expert_math():

@@ -33,8 +33,8 @@ def test_version_and_error_text():
 def test_argument_validation_returns_status_codes():
     lib = L.lib()
 
-    def gemv(x=16, M=1, packed=16, k=128, n=128, K=3, cb=2, ws=16, ws_bytes=1 << 20, split=0):
-        return lib.exl3_gemv(x, 0, k, M, packed, 16, 16, k, n, K, cb, 16, 0, n, ws, ws_bytes, split, None)
+    def gemv(x=16, M=1, packed=16, k=128, n=128, K=3, cb=2, ws=16, ws_bytes=1 << 30, groups=0):
+        return lib.exl3_gemv(x, 0, k, M, packed, 16, 16, k, n, K, cb, 16, 0, n, ws, ws_bytes, groups, None)
 
     # codebook other than mul1
     assert gemv(cb=1) == L.EXL3_ERR_UNSUPPORTED
@@ -61,15 +61,18 @@ def test_argument_validation_returns_status_codes():
         L.EXL3_ERR_UNSUPPORTED
     assert lib.exl3_route(16, 4, 1, 4, 0, 8, None, None, None, 1.0, 1, 16, 0, 16, None, None) == L.EXL3_ERR_ARG
     # MoE: missing workspace
-    assert lib.exl3_moe_decode(16, 0, 128, 1, 16, 16, 2, 16, 4, 0, 128, 128, 0.0, 16, 2, None, 0, 0, 0, None) == \
+    assert lib.exl3_moe_decode(16, 0, 128, 1, 16, 16, 2, 16, 4, 0, 128, 128, 0.0, 16, 2, None, 0, 0, None) == \
         L.EXL3_ERR_WORKSPACE
+    assert lib.exl3_moe_gateup(1, 2, 16, 4, 0, 128, 128, 0.0, None, 0, 0, None) == L.EXL3_ERR_WORKSPACE
+    # negative group count
+    assert gemv(groups=-1) == L.EXL3_ERR_ARG
     # zero rows is a no-op
     assert gemv(M=0) == L.EXL3_OK
 
 
 def test_workspace_size_grows_with_batch():
     lib = L.lib()
-    assert 0 < lib.exl3_gemv_workspace_size(1, 4096) < lib.exl3_gemv_workspace_size(8, 4096)
+    assert 0 < lib.exl3_gemv_workspace_size(1, 4096, 4096) < lib.exl3_gemv_workspace_size(8, 4096, 4096)
     a = lib.exl3_moe_workspace_size(1, 10, 512, 2048, 512, 0)
     b = lib.exl3_moe_workspace_size(4, 10, 512, 2048, 512, 1)
     assert 0 < a < b
