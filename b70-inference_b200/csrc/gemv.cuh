@@ -555,14 +555,31 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
             if (finish) {
                 // contributors in order: the owner of a0, then the owner after each range, up to the unit's end; a
                 // contributor that started before a0 keeps this unit's partial in its second slot
+                int slots[4];                                 // partial slots of the first contributors, in order
+                int n_c = 0;
+                for (long long c = owner_of(a0, T, G); n_c < 4; c = next_owner(c, T, G)) {
+                    slots[n_c++] = (int)(range_start(c, T, G) < a0 ? 2 * c + 1 : 2 * c);
+                    if (range_start(c + 1, T, G) >= a1) break;
+                }
                 for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
                     if ((e / 32) % kMaxRows >= ui.Mi) continue;
+                    float4 p[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+                        p[j] = j < n_c ? __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)slots[j] * UF) + e)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-                    for (long long c = owner_of(a0, T, G);; c = next_owner(c, T, G)) {
-                        const long long sl = range_start(c, T, G) < a0 ? 2 * c + 1 : 2 * c;
-                        const float4 p = __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)sl * UF) + e);
-                        acc.x += p.x; acc.y += p.y; acc.z += p.z; acc.w += p.w;
-                        if (range_start(c + 1, T, G) >= a1) break;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) { acc.x += p[j].x; acc.y += p[j].y; acc.z += p[j].z; acc.w += p[j].w; }
+                    if (n_c == 4) {                           // units split over more than 4 CTAs: the rest in order
+                        long long c = owner_of(a0, T, G);
+                        for (int j = 0; j < 4; ++j) c = next_owner(c, T, G);
+                        for (;; c = next_owner(c, T, G)) {
+                            if (range_start(c, T, G) >= a1) break;
+                            const long long sl = range_start(c, T, G) < a0 ? 2 * c + 1 : 2 * c;
+                            const float4 q = __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)sl * UF) + e);
+                            acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
+                        }
                     }
                     reinterpret_cast<float4*>(rb)[e] = acc;
                 }

@@ -60,6 +60,11 @@ __device__ __forceinline__ uint64_t pack_key(float key, int e) {
     if (isnan(key)) key = -INFINITY;
     return ((uint64_t)ordered_bits(key) << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)e);
 }
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+    return v;
+}
 __device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
 #pragma unroll
     for (int m = 16; m > 0; m >>= 1) {
@@ -69,127 +74,100 @@ __device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
     return v;
 }
 
-constexpr int kRouteThreads = 256;
+constexpr int kRouteWarps = 4;                        // rows per CTA, one warp each
 constexpr int kRouteMaxE = 1024;
-constexpr int kRoutePer = kRouteMaxE / kRouteThreads;   // experts per thread
 constexpr int kRouteMaxK = 32;
 
-// One CTA per row. score in fp64 rounded once to fp32; selection by k argmax passes (ties -> lowest index).
-__global__ void __launch_bounds__(kRouteThreads) k_route(const float* __restrict__ logits, int ld, int E, int kind,
-                                                         int k, const float* bias, const float* res,
-                                                         const float* mul, float scale, int renorm, void* ids,
-                                                         int ids64, float* w, void* want) {
-    __shared__ float s_score[kRouteMaxE];
-    __shared__ uint64_t s_red[kRouteThreads / 32];
-    __shared__ int s_pick[kRouteMaxK];
-    __shared__ double s_dred[kRouteThreads / 32];
-    pdl_wait();                                               // logits may come from the previous kernel
-    const int row = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    const float* l = logits + (size_t)row * ld;
-
-    // scores
-    float lmax = -INFINITY;
-    for (int j = 0; j < kRoutePer; ++j) {
-        const int e = t + j * kRouteThreads;
-        if (e >= E) break;
-        const float v = l[e];
-        float s;
-        if (kind == EXL3_ROUTE_SIGMOID) {
-            s = (float)(1.0 / (1.0 + exp(-(double)v)));
-        } else if (kind == EXL3_ROUTE_SQRT_SOFTPLUS) {
-            const double d = (double)v;
-            s = (float)sqrt(d > 20.0 ? d : log1p(exp(d)));
-        } else {
-            s = v;
-            lmax = fmaxf(lmax, v);
-        }
-        s_score[e] = s;
+__device__ __forceinline__ float route_score(float v, int kind) {
+    if (kind == EXL3_ROUTE_SIGMOID) return (float)(1.0 / (1.0 + exp(-(double)v)));
+    if (kind == EXL3_ROUTE_SQRT_SOFTPLUS) {
+        const double d = (double)v;
+        return (float)sqrt(d > 20.0 ? d : log1p(exp(d)));
     }
-    // softmax denominator (fp64), only for the weights
-    double denom = 1.0, dmax = 0.0;
-    if (kind == EXL3_ROUTE_SOFTMAX) {
-        float m = lmax;
+    return v;
+}
+
+// One warp per row: scores in fp64 rounded once to fp32 and 64-bit selection keys in shared memory; k argmax passes
+// (lane-local scan + warp reduction, ties -> lowest index) with no block-wide barriers; the picks' weights are
+// evaluated in parallel, one lane per pick, and summed in slot order.
+__global__ void __launch_bounds__(kRouteWarps * 32) k_route(const float* __restrict__ logits, int ld, int R, int E,
+                                                            int kind, int k, const float* bias, const float* res,
+                                                            const float* mul, float scale, int renorm, void* ids,
+                                                            int ids64, float* w, void* want) {
+    __shared__ float s_score[kRouteWarps][kRouteMaxE];
+    __shared__ uint64_t s_key[kRouteWarps][kRouteMaxE];
+    pdl_wait();                                               // logits may come from the previous kernel
+    const int lane = threadIdx.x & 31, wr = threadIdx.x >> 5;
+    const int row = blockIdx.x * kRouteWarps + wr;
+    if (row >= R) return;
+    const float* l = logits + (size_t)row * ld;
+    float* sc = s_score[wr];
+    uint64_t* key = s_key[wr];
+
+    // logits: every load of the row issued before any is used (one memory round trip), then the scores
+    float lmax = -INFINITY;
+    {
+        float v[kRouteMaxE / 32];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-        if (lane == 0) s_dred[warp] = m;
-        __syncthreads();
-        double mm = -INFINITY;
-        for (int i = 0; i < kRouteThreads / 32; ++i) mm = fmax(mm, s_dred[i]);
-        dmax = mm;
-        __syncthreads();
-        double part = 0.0;
-        for (int j = 0; j < kRoutePer; ++j) {
-            const int e = t + j * kRouteThreads;
-            if (e >= E) break;
-            part += exp((double)l[e] - dmax);
+        for (int j = 0; j < kRouteMaxE / 32; ++j) v[j] = (lane + 32 * j < E) ? l[lane + 32 * j] : -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kRouteMaxE / 32; ++j) {
+            lmax = fmaxf(lmax, v[j]);
+            sc[lane + 32 * j] = v[j];
         }
+    }
+    __syncwarp();
+    if (kind != EXL3_ROUTE_SOFTMAX)
+        for (int e = lane; e < E; e += 32) sc[e] = route_score(sc[e], kind);
+    double denom = 1.0, dmax = 0.0;
+    if (kind == EXL3_ROUTE_SOFTMAX) {                         // softmax statistics (fp64), only for the weights
+        dmax = (double)warp_max(lmax);
+        double part = 0.0;
+        for (int e = lane; e < E; e += 32) part += exp((double)sc[e] - dmax);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, o);
-        if (lane == 0) s_dred[warp] = part;
-        __syncthreads();
-        denom = 0.0;
-        for (int i = 0; i < kRouteThreads / 32; ++i) denom += s_dred[i];
+        denom = part;
     }
-    __syncthreads();
 
     for (int pass = 0; pass < 2; ++pass) {
         if (pass == 1 && !want) break;
-        uint64_t key[kRoutePer];
-#pragma unroll
-        for (int j = 0; j < kRoutePer; ++j) {
-            const int e = t + j * kRouteThreads;
-            key[j] = 0;
-            if (e < E) {
-                float kv = s_score[e];
-                if (pass == 0 && mul) kv = kv * mul[e];
-                if (bias) kv = kv + bias[e];
-                if (pass == 0 && res) kv = kv + res[e];
-                key[j] = pack_key(kv, e);
-            }
+        for (int e = lane; e < E; e += 32) {
+            float kv = sc[e];
+            if (pass == 0 && mul) kv = kv * mul[e];
+            if (bias) kv = kv + bias[e];
+            if (pass == 0 && res) kv = kv + res[e];
+            key[e] = pack_key(kv, e);
         }
+        __syncwarp();
+        int pick = -1;                                        // lane j < k ends up holding pick j
         for (int j = 0; j < k; ++j) {
             uint64_t best = 0;
-#pragma unroll
-            for (int i = 0; i < kRoutePer; ++i) best = key[i] > best ? key[i] : best;
+            for (int e = lane; e < E; e += 32) best = key[e] > best ? key[e] : best;
             best = warp_max_u64(best);
-            if (lane == 0) s_red[warp] = best;
-            __syncthreads();
-            uint64_t all = 0;
-#pragma unroll
-            for (int i = 0; i < kRouteThreads / 32; ++i) all = s_red[i] > all ? s_red[i] : all;
-            const int e = (int)(0xFFFFFFFFu - (uint32_t)(all & 0xFFFFFFFFu));
-#pragma unroll
-            for (int i = 0; i < kRoutePer; ++i)
-                if (key[i] == all) key[i] = 0;
-            if (t == 0) s_pick[j] = e;
-            __syncthreads();
+            const int e = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
+            if ((e & 31) == lane) key[e] = 0;                 // the owner lane clears the picked key
+            if (lane == j) pick = e;
+            __syncwarp();
         }
-        if (t == 0) {
-            if (pass == 0) {
-                // weights from the unbiased score, summed over the picks in slot order
-                float wv[kRouteMaxK];
-                float tot = 0.f;
-                for (int j = 0; j < k; ++j) {
-                    const int e = s_pick[j];
-                    wv[j] = kind == EXL3_ROUTE_SOFTMAX ? (float)(exp((double)l[e] - dmax) / denom) : s_score[e];
-                    tot += wv[j];
-                }
-                for (int j = 0; j < k; ++j) {
-                    float o;
-                    if (kind == EXL3_ROUTE_SOFTMAX) o = renorm ? wv[j] / (tot + 1e-20f) : wv[j];
-                    else o = wv[j] * scale / (tot + 1e-20f);
-                    w[(size_t)row * k + j] = o;
-                    if (ids64) static_cast<int64_t*>(ids)[(size_t)row * k + j] = s_pick[j];
-                    else static_cast<int32_t*>(ids)[(size_t)row * k + j] = s_pick[j];
-                }
-            } else {
-                for (int j = 0; j < k; ++j) {
-                    if (ids64) static_cast<int64_t*>(want)[(size_t)row * k + j] = s_pick[j];
-                    else static_cast<int32_t*>(want)[(size_t)row * k + j] = s_pick[j];
-                }
+        if (pass == 0) {
+            // weights from the unbiased score, summed over the picks in slot order
+            float wv = 0.f;
+            if (lane < k) wv = kind == EXL3_ROUTE_SOFTMAX ? (float)(exp((double)l[pick] - dmax) / denom) : sc[pick];
+            float tot = 0.f;
+            for (int j = 0; j < k; ++j) tot += __shfl_sync(0xFFFFFFFFu, wv, j);
+            if (lane < k) {
+                float o;
+                if (kind == EXL3_ROUTE_SOFTMAX) o = renorm ? wv / (tot + 1e-20f) : wv;
+                else o = wv * scale / (tot + 1e-20f);
+                w[(size_t)row * k + lane] = o;
+                if (ids64) static_cast<int64_t*>(ids)[(size_t)row * k + lane] = pick;
+                else static_cast<int32_t*>(ids)[(size_t)row * k + lane] = pick;
             }
+        } else if (lane < k) {
+            if (ids64) static_cast<int64_t*>(want)[(size_t)row * k + lane] = pick;
+            else static_cast<int32_t*>(want)[(size_t)row * k + lane] = pick;
         }
-        __syncthreads();
+        __syncwarp();
     }
 }
 
@@ -607,8 +585,9 @@ int exl3_route(const float* logits, int ld, int R, int E, int kind, int k, const
     EXL3_REQUIRE(k >= 1 && k <= kRouteMaxK && k <= E, EXL3_ERR_ARG, "exl3_route: k=%d", k);
     EXL3_REQUIRE(kind >= 0 && kind <= 2, EXL3_ERR_ARG, "exl3_route: kind=%d", kind);
     if (R == 0) return EXL3_OK;
-    cudaError_t e = launch_pdl(k_route, dim3(R), dim3(kRouteThreads), 0, static_cast<cudaStream_t>(stream), logits,
-                               ld, E, kind, k, bias, res, mul, scale, renorm, ids, ids64, w, want);
+    cudaError_t e = launch_pdl(k_route, dim3((R + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), 0,
+                               static_cast<cudaStream_t>(stream), logits, ld, R, E, kind, k, bias, res, mul, scale,
+                               renorm, ids, ids64, w, want);
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_route: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }

@@ -3,8 +3,9 @@
 
 Workload (the metric's "MoE-layer decode"): Qwen-Next-like MoE decode, hidden 2048, 512 routed
 experts of intermediate 512, top-10 softmax router (renormalised), K = 3 bits per weight, 48 layers, 4 tokens per
-GPU. A step is one decode step of the batch through all 48 MoE layers: router -> align -> gate|up GEMV -> down GEMV
--> combine per layer, captured once in a CUDA graph and replayed. With N GPUs the experts are sharded expert-parallel
+GPU. A step is one decode step of the batch through all 48 MoE layers: router -> prepare (alignment + rotated
+activation rows) -> gate|up GEMV -> down GEMV -> fixed-order combine per layer, captured once in a CUDA graph and
+replayed. With N GPUs the experts are sharded expert-parallel
 (512/N per GPU) and tokens are data-parallel (4 per GPU): NCCL all-to-all dispatch/combine per layer.
 Synthetic data: uniform random trellis bitstreams, +-1 sign vectors, activations ~N(0,1) fp16, router logits
 ~N(0,1) fp32, all seeded; weights are created on the device.
@@ -133,7 +134,19 @@ def config_of(args, cfg):
             "topk": cfg["topk"], "K": list(cfg["Ks"]), "layers": cfg["layers"], "router": cfg["router"],
             "batch_per_gpu": cfg["batch"], "global_batch": cfg["batch"] * N,
             "parallelism": f"ep{N}" if N > 1 else "single",
-            "l2": "inputs larger than L2 (each step reads every layer's picked experts; >1 GB of weights per step)"}
+            "l2": l2_note(cfg)}
+
+
+def l2_note(cfg) -> str:
+    """Whether a step's weight reads exceed the 126 MB L2 (picked experts of every layer; upper bound: all picks
+    distinct)."""
+    per_expert = 3 * cfg["H"] * cfg["I"] * max(cfg["Ks"]) / 8
+    picks = min(cfg["E"], cfg["batch"] * cfg["topk"]) + (1 if cfg["shared_K"] else 0)
+    lo = min(cfg["Ks"]) / max(cfg["Ks"]) * per_expert * min(cfg["E"], cfg["topk"]) * cfg["layers"]
+    if lo > 126e6:
+        return (f"inputs larger than L2: each step reads every layer's picked experts "
+                f"(>= {lo / 1e9:.2f} GB of weights per step)")
+    return f"inputs may fit in L2 ({per_expert * picks * cfg['layers'] / 1e6:.0f} MB of weights per step at most)"
 
 
 # ------------------------------------------------------------------------------------------------ clocks

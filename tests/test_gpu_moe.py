@@ -218,6 +218,25 @@ def test_moe_decode_benchmark_shape():
     assert_close(out.cpu().numpy(), ref, what="moe benchmark shape")
 
 
+@pytest.mark.parametrize("shared", [False, True])
+def test_moe_decode_token_without_picks(shared):
+    """A token whose picks are all dropped gets zeros (or only the shared expert), from a poisoned workspace."""
+    rng = np.random.default_rng(31)
+    E, H, I, topk, M = 8, 256, 128, 3, 3
+    np_exp, dev_exp, sh_np, sh_dev = make_experts(rng, E, H, I, [(3, 3, 3)] * E, 3 if shared else None)
+    table = moe.ExpertTable(dev_exp, sh_dev)
+    x = rng.standard_normal((M, H)).astype(np.float16)
+    ids = np.array([[1, 4, 6], [-1, -1, -1], [6, 1, 2]], dtype=np.int32)
+    w = rng.random((M, topk)).astype(np.float32)
+    need = L.lib().exl3_moe_workspace_size(M, topk, E, H, I, int(shared))
+    out = torch.full((M, H), float("nan"), device=DEV)
+    moe.moe_forward(to_dev(x), to_dev(ids), to_dev(w), table, 0.0, out=out, workspace=poisoned(need))
+    ref = O.moe_forward(x, ids, w, np_exp, 0.0, sh_np)
+    assert_close(out.cpu().numpy(), ref, what=f"dropped token shared={shared}")
+    if not shared:
+        assert (out[1] == 0).all()
+
+
 def test_moe_golden_expert_math():
     d = np.load(os.path.join(G, "moe_expert.npz"))
     H, I, Lc = int(d["H"]), int(d["I"]), float(d["act_limit"])
