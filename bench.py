@@ -438,8 +438,9 @@ def run_ours(args, cfg):
         dist.destroy_process_group()
 
 
-# DRAM bytes per gate|up launch from the committed ncu capture (profiles/), per workload; None until captured.
-TRAFFIC_PER_LAUNCH: dict = {}
+# DRAM bytes (read + write) per gate|up launch from the committed ncu capture
+# (profiles/k_gemv_moe_qwen_next_full.md), per workload; None where no capture was made.
+TRAFFIC_PER_LAUNCH: dict = {"qwen_next_decode": 31220224 + 33024}
 
 
 def main():
