@@ -62,6 +62,19 @@ def exl3_gemv(x: torch.Tensor, packed: torch.Tensor, suh: torch.Tensor, svh: tor
     L.check(rc, "exl3_gemv")
 
 
+def exl3_gemv_noalloc(x: torch.Tensor, packed: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
+                      y: torch.Tensor) -> None:
+    """exl3_gemv with the library's static device scratch instead of a workspace (C ABI exl3_gemv_noalloc):
+    M <= 8, k <= 32768, n <= 65536; calls on one device must not overlap."""
+    L.require_cuda(x, packed, y)
+    M, k = x.shape
+    n = svh.shape[0]
+    rc = L.lib().exl3_gemv_noalloc(x.data_ptr(), L.dtype_code(x.dtype), x.stride(0), M, packed.data_ptr(),
+                                   L.ptr(suh), svh.data_ptr(), k, n, int(K), 2, y.data_ptr(), L.dtype_code(y.dtype),
+                                   y.stride(0), L.stream_of(x))
+    L.check(rc, "exl3_gemv_noalloc")
+
+
 def exl3_reconstruct(trellis: torch.Tensor, w: torch.Tensor, n0: int, K: int, cb: int = 2) -> None:
     """w[k, n_slice] (fp16, written) = W_hat[:, n0 : n0 + n_slice] (glm/xpu/csrc/exl3_ops.sycl:539-555)."""
     L.require_cuda(trellis, w)

@@ -104,6 +104,16 @@ EXL3_API int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* p
                        const void* svh, int k, int n, int K, int cb, void* y, int y_dtype, int ldy, void* workspace,
                        size_t ws_bytes, int n_ctas, void* stream);
 
+/* No-allocation variant of exl3_gemv: same arguments minus the workspace and n_ctas; its scratch is a fixed
+ * file-scope device array (about 2.3 MB per device), for callers that cannot allocate device memory. Limits: M <= 8,
+ * k <= 32768, n <= 65536 (larger shapes return EXL3_ERR_UNSUPPORTED). Calls on one device that may overlap race on
+ * the shared scratch: order them on one stream. Make the first call on each device outside stream capture (it looks
+ * up the scratch's address). No reference counterpart: the reference allocates its scratch per call
+ * (glm/xpu/csrc/exl3_ops.sycl:286-300). */
+EXL3_API int exl3_gemv_noalloc(const void* x, int x_dtype, int ldx, int M, const void* packed, const void* suh,
+                               const void* svh, int k, int n, int K, int cb, void* y, int y_dtype, int ldy,
+                               void* stream);
+
 /* ---- activation ----
  * z = fp16(min(silu(g), L) * clamp(u, -L, L)), L = act_limit (0 disables the clamps); fp32 math.
  * g, u, z fp16 [count]; z may alias u. Replaces silu_mul (glm/xpu/glm_xpu/ops.py:147-154). */
