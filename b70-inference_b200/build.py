@@ -58,7 +58,7 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     with cf.ThreadPoolExecutor(max_workers=min(8, len(srcs))) as ex:
         objs = list(ex.map(lambda s: compile_one(s, force, verbose, extra or []), srcs))
     if force or not os.path.exists(OUT) or os.path.getmtime(OUT) < max(os.path.getmtime(o) for o in objs):
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", OUT, *objs, "-lcuda"]
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", OUT, *objs]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)

@@ -62,6 +62,22 @@ def exl3_gemv(x: torch.Tensor, packed: torch.Tensor, suh: torch.Tensor, svh: tor
     L.check(rc, "exl3_gemv")
 
 
+def exl3_gemm_tc(x: torch.Tensor, packed: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
+                 y: torch.Tensor, workspace: torch.Tensor | None = None) -> None:
+    """y[M, n] = Had(Had(x * suh) @ W_hat) * svh for any M on tcgen05 (C ABI exl3_gemm_tc); packed = pack(trellis,
+    K); n % 256 == 0; y fp16/bf16/fp32 preallocated."""
+    L.require_cuda(x, packed, y)
+    M, k = x.shape
+    n = svh.shape[0]
+    lib = L.lib()
+    need = lib.exl3_gemm_tc_workspace_size(M, k)
+    ws = workspace if workspace is not None else L.workspace(x.device, need, "gemm_tc")
+    rc = lib.exl3_gemm_tc(x.data_ptr(), L.dtype_code(x.dtype), x.stride(0), M, packed.data_ptr(), L.ptr(suh),
+                          svh.data_ptr(), k, n, int(K), 2, y.data_ptr(), L.dtype_code(y.dtype), y.stride(0),
+                          ws.data_ptr(), ws.numel(), L.stream_of(x))
+    L.check(rc, "exl3_gemm_tc")
+
+
 def exl3_gemv_noalloc(x: torch.Tensor, packed: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
                       y: torch.Tensor) -> None:
     """exl3_gemv with the library's static device scratch instead of a workspace (C ABI exl3_gemv_noalloc):

@@ -104,6 +104,18 @@ EXL3_API int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* p
                        const void* svh, int k, int n, int K, int cb, void* y, int y_dtype, int ldy, void* workspace,
                        size_t ws_bytes, int n_ctas, void* stream);
 
+/* ---- EXL3 linear, prefill sizes (tcgen05) ----
+ * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for any M, on the 5th-generation tensor cores: trellis tiles decoded to
+ * the reference's fp16 weights bit for bit into shared memory, tcgen05.mma kind::f16 with fp32 accumulation in
+ * tensor memory, 256 x 256 output tiles. k % 128 == 0, n % 256 == 0, 1 <= K <= 8, cb == 2; packed = exl3_pack.
+ * workspace >= exl3_gemm_tc_workspace_size(M, k) bytes, 256-byte aligned (the rotated input rows).
+ * Replaces the reconstruct + GEMM linear for M > 128 (glm/xpu/csrc/exl3_ops.sycl:539-555,651-757) and exllamav3
+ * exl3_gemm's large-M shapes (glm/docs/ext-op-inventory.md:498-557). */
+EXL3_API size_t exl3_gemm_tc_workspace_size(int M, int k);
+EXL3_API int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed, const void* suh,
+                          const void* svh, int k, int n, int K, int cb, void* y, int y_dtype, int ldy,
+                          void* workspace, size_t ws_bytes, void* stream);
+
 /* No-allocation variant of exl3_gemv: same arguments minus the workspace and n_ctas; its scratch is a fixed
  * file-scope device array (about 2.3 MB per device), for callers that cannot allocate device memory. Limits: M <= 8,
  * k <= 32768, n <= 65536 (larger shapes return EXL3_ERR_UNSUPPORTED). Calls on one device that may overlap race on
