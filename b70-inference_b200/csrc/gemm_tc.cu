@@ -3,14 +3,14 @@
 // y[M][n] = Had(Had(x * suh) @ W_hat) * svh, W_hat decoded from the packed trellis (exl3_pack layout) to the
 // reference's fp16 weights bit for bit, multiplied on tcgen05 kind::f16 with fp32 accumulation in tensor memory.
 //
-// One CTA computes a 256-row x 256-column tile (two 128-row accumulators of 256 fp32 columns = all 512 TMEM
+// One CTA computes a TC_BM x TC_BN output tile (TC_BM / 128 accumulators of TC_BN fp32 columns = all 512 TMEM
 // columns) over the whole k range, in k-chunks of 64:
-//   warp 0        TMA: the chunk's rotated activation tile [256 rows][64] fp16, 128-byte swizzle, into a 2-stage ring;
-//   warp 1        allocates TMEM, then one elected lane issues 2 x 4 tcgen05.mma (M 128, N 256, K 16) per chunk and
-//                 commits each stage's release and, after the last chunk, the accumulators;
-//   warp 2        bulk-copies the chunk's trellis tiles (2 column blocks x 4 tile-rows x 8 tiles) into a ring;
+//   warp 0        TMA: the chunk's rotated activation tile [TC_BM rows][64] fp16, 128-byte swizzle, into a ring;
+//   warp 1        allocates TMEM, then one elected lane issues (TC_BM / 128) x 4 tcgen05.mma (M 128, N TC_BN, K 16)
+//                 per chunk and commits each stage's release and, after the last chunk, the accumulators;
+//   warp 2        bulk-copies the chunk's trellis tiles (TC_BN / 128 column blocks x 4 tile-rows x 8 tiles);
 //   warps 3..18   decode the trellis tiles (same register decode as the GEMV: one lane, eight positions of a tile)
-//                 into the B stage [256 columns][64] fp16 in the canonical K-major 128-byte-swizzled layout; after
+//                 into the B stage [TC_BN columns][64] fp16 in the canonical K-major 128-byte-swizzled layout; after
 //                 the main loop the same warps run the epilogue: TMEM -> registers -> shared memory (XOR-swizzled
 //                 rows) -> output Hadamard per 128-column block with warp shuffles -> x svh -> y.
 // All waits are bounded (EXL3_ERR_TIMEOUT in the device status word). No multicast, no clusters.
@@ -21,23 +21,33 @@
 
 namespace exl3 {
 
-constexpr int TC_BM = 256, TC_BN = 256, TC_BK = 64;
+#ifndef EXL3_TC_BM
+#define EXL3_TC_BM 256
+#define EXL3_TC_BN 256
+#define EXL3_TC_ASTAGES 4
+#define EXL3_TC_BSTAGES 2
+#endif
+constexpr int TC_BM = EXL3_TC_BM, TC_BN = EXL3_TC_BN, TC_BK = 64;
+constexpr int TC_ACC = TC_BM / 128;                            // 128-row accumulators (TMEM: TC_ACC x TC_BN columns)
+constexpr int TC_NB = TC_BN / 128;                             // 128-column blocks per tile
+static_assert(TC_ACC * TC_BN == 512, "the accumulators fill the 512 TMEM columns");
 constexpr int TC_DEC_WARPS = 16;
 constexpr int TC_WARPS = 3 + TC_DEC_WARPS;
 constexpr int TC_THREADS = TC_WARPS * 32;
-constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;                 // 32 KB
-constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;                 // 32 KB
-constexpr int TC_T_RING = 64 * 1024;                          // trellis ring bytes
+constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;
+constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;
+constexpr int TC_A_STAGES = EXL3_TC_ASTAGES, TC_B_STAGES = EXL3_TC_BSTAGES;
+constexpr int TC_T_RING = 32 * 1024;                          // trellis ring bytes
 constexpr int TC_MAX_TSTAGES = 8;
-constexpr int TC_TILES = (TC_BN / 16) * (TC_BK / 16);         // trellis tiles per chunk: 16 x 4 = 64
+constexpr int TC_TILES = (TC_BN / 16) * (TC_BK / 16);         // trellis tiles per chunk
 
 struct TcSmem {
-    static constexpr int a0 = 0;                               // A[2] (1024-aligned)
-    static constexpr int b0 = 2 * TC_A_BYTES;                  // B[2]
-    static constexpr int t0 = b0 + 2 * TC_B_BYTES;             // trellis ring
+    static constexpr int a0 = 0;                               // A[3] (1024-aligned)
+    static constexpr int b0 = TC_A_STAGES * TC_A_BYTES;        // B[2]
+    static constexpr int t0 = b0 + TC_B_STAGES * TC_B_BYTES;   // trellis ring
     static constexpr int bars = t0 + TC_T_RING;
-    // a_full[2], b_full[2], ab_empty[2], t_full[8], t_empty[8], acc_full
-    static constexpr int n_bars = 2 + 2 + 2 + 2 * TC_MAX_TSTAGES + 1;
+    // a_full[3], a_empty[3], b_full[2], b_empty[2], t_full[8], t_empty[8], acc_full
+    static constexpr int n_bars = 2 * TC_A_STAGES + 2 * TC_B_STAGES + 2 * TC_MAX_TSTAGES + 1;
     static constexpr int tmem_slot = bars + n_bars * 8;
     static constexpr int total = tmem_slot + 16 + 1024;        // + slack for 1024-byte alignment of the base
 };
@@ -103,36 +113,58 @@ struct TcArgs {
     int* status;
 };
 
-// Decode one chunk's 64 trellis tiles (warp dw takes tiles 4dw .. 4dw+3) into the swizzled B stage.
+// Per-thread constant addressing of the decode: for each of the warp's tiles in a chunk, the tile's byte
+// offset in a trellis stage and the four swizzled byte offsets in a B stage that receive the lane's fragment
+// registers {n, k..k+1}, {n + 8, k..}, {n, k + 8..}, {n + 8, k + 8..} (n = tile column + g, k = tile row + 2q).
+constexpr int TC_TPW = TC_TILES / TC_DEC_WARPS;
+struct TcDecodeMap {
+    uint32_t tile[TC_TPW];
+    uint32_t st[TC_TPW][4];
+};
+
 template <int K>
-__device__ __forceinline__ void tc_decode_chunk(const uint8_t* tst, uint8_t* bst, int dw, int lane) {
-    const LaneWords lw = lane_words<K>(lane);
+__device__ __forceinline__ TcDecodeMap tc_decode_map(int dw, int lane) {
+    TcDecodeMap mp;
     const int g = lane >> 2, q = lane & 3;
 #pragma unroll
-    for (int j = 0; j < TC_TILES / TC_DEC_WARPS; ++j) {
-        const int ti = dw * (TC_TILES / TC_DEC_WARPS) + j;     // 0..63
-        const int cb = ti >> 5, tr = (ti >> 3) & 3, t = ti & 7;
-        const uint32_t* tile = reinterpret_cast<const uint32_t*>(tst + (((cb * 4 + tr) * 8 + t) * 32 * K));
-        uint32_t a[4];
-        decode_frag<K>(tile, lw, a);
+    for (int j = 0; j < TC_TPW; ++j) {
+        const int ti = dw * TC_TPW + j;
+        const int cb = ti >> 5, tr = (ti >> 3) & 3, t = ti & 7;   // column block, tile-row, tile
+        mp.tile[j] = (uint32_t)(((cb * 4 + tr) * 8 + t) * 32 * K);
         const int n0 = cb * 128 + t * 16 + g, k0 = tr * 16 + 2 * q;
-        *reinterpret_cast<uint32_t*>(bst + sw128_off(n0, k0)) = a[0];
-        *reinterpret_cast<uint32_t*>(bst + sw128_off(n0 + 8, k0)) = a[1];
-        *reinterpret_cast<uint32_t*>(bst + sw128_off(n0, k0 + 8)) = a[2];
-        *reinterpret_cast<uint32_t*>(bst + sw128_off(n0 + 8, k0 + 8)) = a[3];
+        mp.st[j][0] = sw128_off(n0, k0);
+        mp.st[j][1] = sw128_off(n0 + 8, k0);
+        mp.st[j][2] = sw128_off(n0, k0 + 8);
+        mp.st[j][3] = sw128_off(n0 + 8, k0 + 8);
+    }
+    return mp;
+}
+
+// Decode one chunk's trellis tiles of this warp into the swizzled B stage.
+template <int K>
+__device__ __forceinline__ void tc_decode_chunk(const uint8_t* tst, uint8_t* bst, const TcDecodeMap& mp,
+                                                const LaneWords& lw) {
+#pragma unroll
+    for (int j = 0; j < TC_TPW; ++j) {
+        uint32_t a[4];
+        decode_frag<K>(reinterpret_cast<const uint32_t*>(tst + mp.tile[j]), lw, a);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) *reinterpret_cast<uint32_t*>(bst + mp.st[j][r]) = a[r];
     }
 }
 
 template <int K>
 __device__ void tc_decoder_loop(const TcArgs& p, uint8_t* smem, uint64_t* t_full, uint64_t* t_empty,
-                                uint64_t* b_full, uint64_t* ab_empty, int nk, int dw, int lane, bool& to) {
+                                uint64_t* b_full, uint64_t* b_empty, int nk, int dw, int lane, bool& to) {
+    const TcDecodeMap mp = tc_decode_map<K>(dw, lane);
+    const LaneWords lw = lane_words<K>(lane);
     for (int kc = 0; kc < nk; ++kc) {
-        const int ts = kc % p.t_stages, s = kc & 1;
+        const int ts = kc % p.t_stages, s = kc % TC_B_STAGES;
         if (!to && !mbar_wait(&t_full[ts], (kc / p.t_stages) & 1)) to = true;
-        if (kc >= 2 && !to && !mbar_wait(&ab_empty[s], ((kc >> 1) - 1) & 1)) to = true;
+        if (kc >= TC_B_STAGES && !to && !mbar_wait(&b_empty[s], ((kc / TC_B_STAGES) - 1) & 1)) to = true;
         if (!to)
             tc_decode_chunk<K>(smem + TcSmem::t0 + (size_t)ts * p.t_stage_bytes, smem + TcSmem::b0 + s * TC_B_BYTES,
-                               dw, lane);
+                               mp, lw);
         fence_proxy_async();                                  // generic-proxy writes -> the tensor core's reads
         __syncwarp();
         if (lane == 0) {
@@ -149,9 +181,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::bars);
     uint64_t* a_full = bars;
-    uint64_t* b_full = bars + 2;
-    uint64_t* ab_empty = bars + 4;
-    uint64_t* t_full = bars + 6;
+    uint64_t* a_empty = a_full + TC_A_STAGES;
+    uint64_t* b_full = a_empty + TC_A_STAGES;
+    uint64_t* b_empty = b_full + TC_B_STAGES;
+    uint64_t* t_full = b_empty + TC_B_STAGES;
     uint64_t* t_empty = t_full + TC_MAX_TSTAGES;
     uint64_t* acc_full = t_empty + TC_MAX_TSTAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::tmem_slot);
@@ -160,10 +193,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     pdl_trigger();
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < TC_A_STAGES; ++s) {
             mbar_init(&a_full[s], 1);
+            mbar_init(&a_empty[s], 1);
+        }
+        for (int s = 0; s < TC_B_STAGES; ++s) {
             mbar_init(&b_full[s], TC_DEC_WARPS);
-            mbar_init(&ab_empty[s], 1);
+            mbar_init(&b_empty[s], 1);
         }
         for (int s = 0; s < p.t_stages; ++s) {
             mbar_init(&t_full[s], 1);
@@ -172,7 +208,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         mbar_init(acc_full, 1);
         fence_barrier_init();
     }
-    if (warp == 1) {                                          // TMEM: 512 columns = two 128 x 256 fp32 accumulators
+    if (warp == 1) {                                          // TMEM: 512 columns = four 128 x 128 fp32 accumulators
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -187,37 +223,42 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         // ---------------- activation tiles (TMA) ----------------
         pdl_wait();                                           // the rotated activations come from the previous kernel
         if (lane == 0) {
-            int last_s[2] = {-1, -1};
+            int last_s[TC_A_STAGES];
+            for (int s = 0; s < TC_A_STAGES; ++s) last_s[s] = -1;
             for (int kc = 0; kc < nk && !to; ++kc) {
-                const int s = kc & 1;
-                if (kc >= 2 && !mbar_wait(&ab_empty[s], ((kc >> 1) - 1) & 1)) { to = true; break; }
+                const int s = kc % TC_A_STAGES;
+                if (kc >= TC_A_STAGES && !mbar_wait(&a_empty[s], ((kc / TC_A_STAGES) - 1) & 1)) { to = true; break; }
                 mbar_expect_tx(&a_full[s], TC_A_BYTES);
-                tma_load_2d(smem + TcSmem::a0 + s * TC_A_BYTES, &amap, kc * TC_BK, m0, &a_full[s]);
+#pragma unroll
+                for (int h = 0; h < (TC_BM + 255) / 256; ++h)  // boxes of 256 rows
+                    tma_load_2d(smem + TcSmem::a0 + s * TC_A_BYTES + h * (TC_A_BYTES * 256 / TC_BM), &amap,
+                                kc * TC_BK, m0 + h * 256, &a_full[s]);
                 last_s[s] = kc;
             }
-            for (int s = 0; s < 2; ++s)                       // copies landed before the CTA may exit
-                if (last_s[s] >= 0 && !mbar_wait(&a_full[s], (last_s[s] >> 1) & 1)) to = true;
+            for (int s = 0; s < TC_A_STAGES; ++s)             // copies landed before the CTA may exit
+                if (last_s[s] >= 0 && !mbar_wait(&a_full[s], (last_s[s] / TC_A_STAGES) & 1)) to = true;
         }
     } else if (warp == 1) {
         // ---------------- MMA issue (one lane) ----------------
         if (lane == 0) {
             constexpr uint32_t idesc = tc_idesc_f16(128, TC_BN);
             for (int kc = 0; kc < nk; ++kc) {
-                const int s = kc & 1;
-                if (!to && !mbar_wait(&a_full[s], (kc >> 1) & 1)) to = true;
-                if (!to && !mbar_wait(&b_full[s], (kc >> 1) & 1)) to = true;
+                const int sa = kc % TC_A_STAGES, sb = kc % TC_B_STAGES;
+                if (!to && !mbar_wait(&a_full[sa], (kc / TC_A_STAGES) & 1)) to = true;
+                if (!to && !mbar_wait(&b_full[sb], (kc / TC_B_STAGES) & 1)) to = true;
                 tc_fence_after();
                 if (!to) {
-                    const uint32_t a_base = smem_u32(smem + TcSmem::a0 + s * TC_A_BYTES);
-                    const uint32_t b_base = smem_u32(smem + TcSmem::b0 + s * TC_B_BYTES);
+                    const uint32_t a_base = smem_u32(smem + TcSmem::a0 + sa * TC_A_BYTES);
+                    const uint32_t b_base = smem_u32(smem + TcSmem::b0 + sb * TC_B_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 16; ++kk)
 #pragma unroll
-                        for (int j = 0; j < 2; ++j)
-                            tc_mma_f16(tmem + j * TC_BN, sw128_desc(a_base + j * (TC_A_BYTES / 2) + kk * 32),
+                        for (int j = 0; j < TC_ACC; ++j)
+                            tc_mma_f16(tmem + j * TC_BN, sw128_desc(a_base + j * (TC_A_BYTES / TC_ACC) + kk * 32),
                                        sw128_desc(b_base + kk * 32), idesc, (kc | kk) != 0);
                 }
-                tc_commit(&ab_empty[s]);                      // the stage is free once these MMAs completed
+                tc_commit(&a_empty[sa]);                      // the stages are free once these MMAs completed
+                tc_commit(&b_empty[sb]);
             }
             tc_commit(acc_full);
         }
@@ -225,18 +266,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         // ---------------- trellis tiles (bulk copies) ----------------
         if (lane == 0) {
             const size_t block_bytes = (size_t)(p.k / 16) * 8 * 32 * p.K;       // one 128-column block, all k
-            const uint32_t half = (uint32_t)(p.t_stage_bytes / 2);             // one block's 4 tile-rows
             int last[TC_MAX_TSTAGES];
             for (int s = 0; s < TC_MAX_TSTAGES; ++s) last[s] = -1;
             for (int kc = 0; kc < nk && !to; ++kc) {
                 const int ts = kc % p.t_stages;
                 if (kc >= p.t_stages && !mbar_wait(&t_empty[ts], ((kc / p.t_stages) - 1) & 1)) { to = true; break; }
-                mbar_expect_tx(&t_full[ts], (uint32_t)p.t_stage_bytes);
+                const uint32_t blk = (uint32_t)(p.t_stage_bytes / TC_NB);           // a block's 4 tile-rows
+                const int nbv = min(TC_NB, (p.n - n0) / 128);    // column blocks present (last tile may be partial)
+                mbar_expect_tx(&t_full[ts], blk * (uint32_t)nbv);
                 uint8_t* dst = smem + TcSmem::t0 + (size_t)ts * p.t_stage_bytes;
-#pragma unroll
-                for (int b = 0; b < 2; ++b) {
-                    const uint8_t* src = p.packed + (size_t)(n0 / 128 + b) * block_bytes + (size_t)kc * half;
-                    bulk_g2s(dst + b * half, src, half, &t_full[ts]);
+                for (int b = 0; b < nbv; ++b) {
+                    const uint8_t* src = p.packed + (size_t)(n0 / 128 + b) * block_bytes + (size_t)kc * blk;
+                    bulk_g2s(dst + b * blk, src, blk, &t_full[ts]);
                 }
                 last[ts] = kc;
             }
@@ -247,50 +288,52 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         // ---------------- decoders, then the epilogue ----------------
         const int dw = warp - 3;
         switch (p.K) {
-            case 1: tc_decoder_loop<1>(p, smem, t_full, t_empty, b_full, ab_empty, nk, dw, lane, to); break;
-            case 2: tc_decoder_loop<2>(p, smem, t_full, t_empty, b_full, ab_empty, nk, dw, lane, to); break;
-            case 3: tc_decoder_loop<3>(p, smem, t_full, t_empty, b_full, ab_empty, nk, dw, lane, to); break;
-            case 4: tc_decoder_loop<4>(p, smem, t_full, t_empty, b_full, ab_empty, nk, dw, lane, to); break;
-            case 5: tc_decoder_loop<5>(p, smem, t_full, t_empty, b_full, ab_empty, nk, dw, lane, to); break;
-            case 6: tc_decoder_loop<6>(p, smem, t_full, t_empty, b_full, ab_empty, nk, dw, lane, to); break;
-            case 7: tc_decoder_loop<7>(p, smem, t_full, t_empty, b_full, ab_empty, nk, dw, lane, to); break;
-            default: tc_decoder_loop<8>(p, smem, t_full, t_empty, b_full, ab_empty, nk, dw, lane, to); break;
+            case 1: tc_decoder_loop<1>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
+            case 2: tc_decoder_loop<2>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
+            case 3: tc_decoder_loop<3>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
+            case 4: tc_decoder_loop<4>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
+            case 5: tc_decoder_loop<5>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
+            case 6: tc_decoder_loop<6>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
+            case 7: tc_decoder_loop<7>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
+            default: tc_decoder_loop<8>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
         }
         pdl_wait();                                           // y may be in use by an earlier kernel until here
         if (!to && !mbar_wait(acc_full, 0)) to = true;
         tc_fence_after();
-        // TMEM lane quadrant of this warp; the four warps of a quadrant take (accumulator j, block b)
-        const int quad = warp & 3, iq = dw >> 2;               // warps 3..18: quad covers 0..3 four times
-        const int j = iq >> 1, b = iq & 1;
-        // staging: [2 blocks][128 rows][128 cols] fp32 in the A/B stages (free after the main loop), columns
-        // XOR-swizzled by the row; accumulator 0 then accumulator 1
+        // TMEM lane quadrant of this warp; the four warps of a quadrant take one 128 x 128 block each:
+        // block bi = accumulator bi / TC_NB, column block bi % TC_NB
+        const int quad = warp & 3, bi = dw >> 2;              // warps 3..18: quad covers 0..3 four times
+        static_assert(TC_ACC * TC_NB == 4, "four 128 x 128 blocks per tile");
+        // staging: [2][128 rows][128 cols] fp32 in the A stages (free after the main loop), columns XOR-swizzled
+        // by the row; blocks 0, 1 then 2, 3
         for (int pass = 0; pass < 2; ++pass) {
-            const bool mine = j == pass;
-            float* st = reinterpret_cast<float*>(smem + TcSmem::a0) + (size_t)b * 128 * 128;
-            if (mine) {
+            if ((bi >> 1) == pass) {
+                float* st = reinterpret_cast<float*>(smem + TcSmem::a0) + (size_t)(bi & 1) * 128 * 128;
                 const int row = quad * 32 + lane;             // accumulator row = TMEM lane
+                const uint32_t col0 = (uint32_t)((bi / TC_NB) * TC_BN + (bi % TC_NB) * 128);
 #pragma unroll
                 for (int c0 = 0; c0 < 128; c0 += 32) {
                     uint32_t r[32];
-                    tc_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(j * TC_BN + b * 128 + c0), r);
+                    tc_ld32(tmem + ((uint32_t)(quad * 32) << 16) + col0 + (uint32_t)c0, r);
 #pragma unroll
                     for (int c = 0; c < 32; ++c)
                         st[row * 128 + ((c0 + c) ^ (row & 31))] = __uint_as_float(r[c]);
                 }
             }
             asm volatile("bar.sync 1, %0;" ::"r"(TC_DEC_WARPS * 32) : "memory");
-            // rows of this pass: 2 blocks x 128 rows over 16 warps, one row-block per warp at a time
+            // 2 accumulators x 128 rows over 16 warps, one row at a time
             for (int rb = dw; rb < 2 * 128; rb += TC_DEC_WARPS) {
-                const int bb = rb >> 7, row = rb & 127;
-                const float* src = reinterpret_cast<const float*>(smem + TcSmem::a0) + (size_t)bb * 128 * 128 +
+                const int jj = rb >> 7, row = rb & 127;
+                const float* src = reinterpret_cast<const float*>(smem + TcSmem::a0) + (size_t)jj * 128 * 128 +
                                    row * 128;
                 float v[4];
 #pragma unroll
                 for (int e = 0; e < 4; ++e) v[e] = src[(4 * lane + e) ^ (row & 31)];
                 fwht128_warp(v, lane);
-                const int m = m0 + pass * 128 + row;
-                const int col = n0 + bb * 128 + 4 * lane;
-                if (m < p.M) {
+                const int blk = pass * 2 + jj;
+                const int m = m0 + (blk / TC_NB) * 128 + row;
+                const int col = n0 + (blk % TC_NB) * 128 + 4 * lane;
+                if (m < p.M && col < p.n) {
                     float o[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
@@ -372,8 +415,8 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
                  void* stream) {
     EXL3_REQUIRE(cb == 2, EXL3_ERR_UNSUPPORTED, "exl3_gemm_tc: only the mul1 codebook (cb=2) is supported");
     EXL3_REQUIRE(K >= 1 && K <= 8, EXL3_ERR_UNSUPPORTED, "exl3_gemm_tc: K=%d not in 1..8", K);
-    EXL3_REQUIRE(M >= 0 && k > 0 && n > 0 && k % 128 == 0 && n % TC_BN == 0, EXL3_ERR_ARG,
-                 "exl3_gemm_tc: k=%d must be a multiple of 128 and n=%d of %d", k, n, TC_BN);
+    EXL3_REQUIRE(M >= 0 && k > 0 && n > 0 && k % 128 == 0 && n % 128 == 0, EXL3_ERR_ARG,
+                 "exl3_gemm_tc: k=%d, n=%d must be multiples of 128", k, n);
     EXL3_REQUIRE(x && packed && svh && y, EXL3_ERR_ARG, "exl3_gemm_tc: null pointer");
     EXL3_REQUIRE(aligned16(packed) && aligned16(y), EXL3_ERR_ARG, "exl3_gemm_tc: packed and y must be 16-byte aligned");
     EXL3_REQUIRE(x_dtype == EXL3_F16 || x_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "exl3_gemm_tc: x dtype %d",
@@ -404,7 +447,7 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-    const cuuint32_t box[2] = {TC_BK, TC_BM};
+    const cuuint32_t box[2] = {TC_BK, TC_BM < 256 ? TC_BM : 256};  // TC_BM / 256 boxes per stage
     const cuuint32_t estr[2] = {1, 1};
     // the driver entry point through the runtime (no link-time dependency on libcuda)
     static PFN_encode_tiled encode = nullptr;
@@ -431,7 +474,7 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
     a.k = k;
     a.n = n;
     a.K = K;
-    a.t_stage_bytes = 2 * 4 * 8 * 32 * K;                    // 2 column blocks x 4 tile-rows x 8 tiles
+    a.t_stage_bytes = TC_NB * 4 * 8 * 32 * K;                // column blocks x 4 tile-rows x 8 tiles
     a.t_stages = TC_T_RING / a.t_stage_bytes;
     if (a.t_stages > TC_MAX_TSTAGES) a.t_stages = TC_MAX_TSTAGES;
     a.status = device_status_ptr();
@@ -446,7 +489,7 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
                      cudaGetErrorString(cudaGetLastError()));
         configured[dev] = 1;
     }
-    const dim3 grid(n / TC_BN, (M + TC_BM - 1) / TC_BM);
+    const dim3 grid((n + TC_BN - 1) / TC_BN, (M + TC_BM - 1) / TC_BM);
     cudaError_t e = launch_pdl(k_gemm_tc, grid, dim3(TC_THREADS), TcSmem::total, st, map, a);
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_gemm_tc: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;

@@ -65,7 +65,7 @@ def exl3_gemv(x: torch.Tensor, packed: torch.Tensor, suh: torch.Tensor, svh: tor
 def exl3_gemm_tc(x: torch.Tensor, packed: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
                  y: torch.Tensor, workspace: torch.Tensor | None = None) -> None:
     """y[M, n] = Had(Had(x * suh) @ W_hat) * svh for any M on tcgen05 (C ABI exl3_gemm_tc); packed = pack(trellis,
-    K); n % 256 == 0; y fp16/bf16/fp32 preallocated."""
+    K); n % 128 == 0; y fp16/bf16/fp32 preallocated."""
     L.require_cuda(x, packed, y)
     M, k = x.shape
     n = svh.shape[0]

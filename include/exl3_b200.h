@@ -107,7 +107,7 @@ EXL3_API int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* p
 /* ---- EXL3 linear, prefill sizes (tcgen05) ----
  * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for any M, on the 5th-generation tensor cores: trellis tiles decoded to
  * the reference's fp16 weights bit for bit into shared memory, tcgen05.mma kind::f16 with fp32 accumulation in
- * tensor memory, 256 x 256 output tiles. k % 128 == 0, n % 256 == 0, 1 <= K <= 8, cb == 2; packed = exl3_pack.
+ * tensor memory, 512 x 128 output tiles. k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2; packed = exl3_pack.
  * workspace >= exl3_gemm_tc_workspace_size(M, k) bytes, 256-byte aligned (the rotated input rows).
  * Replaces the reconstruct + GEMM linear for M > 128 (glm/xpu/csrc/exl3_ops.sycl:539-555,651-757) and exllamav3
  * exl3_gemm's large-M shapes (glm/docs/ext-op-inventory.md:498-557). */

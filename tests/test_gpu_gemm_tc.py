@@ -26,7 +26,7 @@ def _status_clean():
     assert L.lib().exl3_device_status(0) == 0, "a device-side wait timed out"
 
 
-@pytest.mark.parametrize("M,k,n,K", [(256, 512, 256, 3), (300, 1024, 512, 2), (77, 256, 256, 4), (520, 384, 768, 1),
+@pytest.mark.parametrize("M,k,n,K", [(256, 512, 256, 3), (300, 1024, 512, 2), (77, 256, 128, 4), (520, 384, 768, 1), (1100, 256, 384, 2),
                                      (256, 640, 256, 8), (1, 128, 256, 5)])
 def test_gemm_tc_matches_oracle(M, k, n, K):
     rng = np.random.default_rng(M * 7 + k + n + K)
@@ -60,7 +60,7 @@ def test_gemm_tc_bf16_input_and_repeatable():
     assert torch.equal(y, y2)
 
 
-@pytest.mark.parametrize("M,k,n,K", [(8192, 7168, 2048, 2), (2048, 2048, 7168, 1), (1000, 5120, 5120, 4)])
+@pytest.mark.parametrize("M,k,n,K", [(8192, 7168, 2048, 2), (2048, 2048, 7168, 1), (1000, 5120, 5120, 4), (700, 1024, 384, 3)])
 def test_gemm_tc_full_size_against_torch(M, k, n, K):
     g = torch.Generator(device=DEV).manual_seed(M + k + n + K)
     tr = torch.randint(-32768, 32767, (k // 16, n // 16, 16 * K), dtype=torch.int16, device=DEV, generator=g)
