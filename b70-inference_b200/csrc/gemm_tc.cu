@@ -1,53 +1,51 @@
-// EXL3 linear for prefill-sized batches on the 5th-generation tensor cores (tcgen05, TMEM accumulators).
+// EXL3 linears for prefill-sized batches on the 5th-generation tensor cores (tcgen05, TMEM accumulators): the dense
+// linear (any M) and the grouped MoE expert projections (rows grouped per expert by the alignment step).
 //
-// y[M][n] = Had(Had(x * suh) @ W_hat) * svh, W_hat decoded from the packed trellis (exl3_pack layout) to the
-// reference's fp16 weights bit for bit, multiplied on tcgen05 kind::f16 with fp32 accumulation in tensor memory.
-//
-// One CTA computes a TC_BM x TC_BN output tile (TC_BM / 128 accumulators of TC_BN fp32 columns = all 512 TMEM
-// columns) over the whole k range, in k-chunks of 64:
-//   warp 0        TMA: the chunk's rotated activation tile [TC_BM rows][64] fp16, 128-byte swizzle, into a ring;
-//   warp 1        allocates TMEM, then one elected lane issues (TC_BM / 128) x 4 tcgen05.mma (M 128, N TC_BN, K 16)
-//                 per chunk and commits each stage's release and, after the last chunk, the accumulators;
-//   warp 2        bulk-copies the chunk's trellis tiles (TC_BN / 128 column blocks x 4 tile-rows x 8 tiles);
-//   warps 3..18   decode the trellis tiles (same register decode as the GEMV: one lane, eight positions of a tile)
-//                 into the B stage [TC_BN columns][64] fp16 in the canonical K-major 128-byte-swizzled layout; after
-//                 the main loop the same warps run the epilogue: TMEM -> registers -> shared memory (XOR-swizzled
-//                 rows) -> output Hadamard per 128-column block with warp shuffles -> x svh -> y.
+// Weights are decoded from the packed trellis (exl3_pack / exl3_pack_gateup layouts) to the reference's fp16 values
+// bit for bit, written into shared memory in the canonical K-major 128-byte-swizzled layout and multiplied with
+// tcgen05.mma kind::f16, fp32 accumulation in tensor memory. One CTA computes a 256-row x 256-column tile over the
+// whole k range, in k-chunks of 64:
+//   warp 0        TMA: the chunk's rotated activation tile(s) [256 rows][64] fp16 (one per matrix), 128-byte swizzle;
+//   warp 1        allocates the 512 TMEM columns, then one elected lane issues the chunk's MMAs (M 128, K 16) and
+//                 commits each stage's release and, after the last chunk, the accumulators;
+//   warp 2        bulk-copies the chunk's trellis tiles into a ring;
+//   warps 3..18   decode the trellis tiles into the B stage [256 columns][64]; after the main loop they run the
+//                 epilogue: TMEM -> registers -> shared memory (XOR-swizzled rows) -> output Hadamard per 128-column
+//                 block with warp shuffles -> the epilogue of the projection.
+// Epilogues: linear (y = H(acc) * svh), MoE gate|up (the tile's 256 columns are the fused gate and up blocks of one
+// column block; two activation matrices, four 128 x 128 accumulators; SiLU * clamp, then the down input's
+// rotation, stored as the down projection's activation rows), MoE down (routing weight x H(acc) * svh, fp32 rows).
 // All waits are bounded (EXL3_ERR_TIMEOUT in the device status word). No multicast, no clusters.
 //
 // Reference semantics: exl3_linear / ReconstructKernel + GEMM for M > 128 (glm/xpu/csrc/exl3_ops.sycl:539-555,
-// 651-757; glm/docs/ext-op-inventory.md:597-612) and the DPAS small-batch kernel (glm/xpu/csrc/exl3_esimd.h:582-862).
+// 651-757; glm/docs/ext-op-inventory.md:597-612), the MoE prefill GateUpDpasKernel / DownDpasKernel
+// (glm/xpu/csrc/exl3_moe.n128.sycl:422-690,868-916) and the expert math (glm/docs/ext-op-inventory.md:923-942).
 #include "gemv.cuh"
+#include "tc.cuh"
 
 namespace exl3 {
 
-#ifndef EXL3_TC_BM
-#define EXL3_TC_BM 256
-#define EXL3_TC_BN 256
-#define EXL3_TC_ASTAGES 4
-#define EXL3_TC_BSTAGES 2
-#endif
-constexpr int TC_BM = EXL3_TC_BM, TC_BN = EXL3_TC_BN, TC_BK = 64;
-constexpr int TC_ACC = TC_BM / 128;                            // 128-row accumulators (TMEM: TC_ACC x TC_BN columns)
-constexpr int TC_NB = TC_BN / 128;                             // 128-column blocks per tile
-static_assert(TC_ACC * TC_BN == 512, "the accumulators fill the 512 TMEM columns");
+constexpr int TC_BM = 256, TC_BN = 256, TC_BK = 64;
 constexpr int TC_DEC_WARPS = 16;
 constexpr int TC_WARPS = 3 + TC_DEC_WARPS;
 constexpr int TC_THREADS = TC_WARPS * 32;
-constexpr int TC_A_BYTES = TC_BM * TC_BK * 2;
-constexpr int TC_B_BYTES = TC_BN * TC_BK * 2;
-constexpr int TC_A_STAGES = EXL3_TC_ASTAGES, TC_B_STAGES = EXL3_TC_BSTAGES;
+constexpr int TC_TILE_BYTES = TC_BM * TC_BK * 2;              // one activation tile (and the B stage): 32 KB
+constexpr int TC_A_REGION = 128 * 1024;                       // activation ring: 4 x 32 KB or 2 x 64 KB
+constexpr int TC_B_STAGES = 2;
 constexpr int TC_T_RING = 32 * 1024;                          // trellis ring bytes
 constexpr int TC_MAX_TSTAGES = 8;
-constexpr int TC_TILES = (TC_BN / 16) * (TC_BK / 16);         // trellis tiles per chunk
+constexpr int TC_TPW = 4;                                     // trellis tiles per decoder warp per chunk (64 / 16)
+
+__host__ __device__ constexpr int tc_nmat(int epi) { return epi == TC_GATEUP ? 2 : 1; }
+__host__ __device__ constexpr int tc_a_stages(int epi) { return TC_A_REGION / (tc_nmat(epi) * TC_TILE_BYTES); }
 
 struct TcSmem {
-    static constexpr int a0 = 0;                               // A[3] (1024-aligned)
-    static constexpr int b0 = TC_A_STAGES * TC_A_BYTES;        // B[2]
-    static constexpr int t0 = b0 + TC_B_STAGES * TC_B_BYTES;   // trellis ring
+    static constexpr int a0 = 0;                               // activation ring (1024-aligned)
+    static constexpr int b0 = TC_A_REGION;                     // B[2]
+    static constexpr int t0 = b0 + TC_B_STAGES * TC_TILE_BYTES;
     static constexpr int bars = t0 + TC_T_RING;
-    // a_full[3], a_empty[3], b_full[2], b_empty[2], t_full[8], t_empty[8], acc_full
-    static constexpr int n_bars = 2 * TC_A_STAGES + 2 * TC_B_STAGES + 2 * TC_MAX_TSTAGES + 1;
+    // a_full[4], a_empty[4], b_full[2], b_empty[2], t_full[8], t_empty[8], acc_full
+    static constexpr int n_bars = 4 + 4 + 2 + 2 + 2 * TC_MAX_TSTAGES + 1;
     static constexpr int tmem_slot = bars + n_bars * 8;
     static constexpr int total = tmem_slot + 16 + 1024;        // + slack for 1024-byte alignment of the base
 };
@@ -104,34 +102,59 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int k) {
 }
 
 struct TcArgs {
-    const uint8_t* packed;     // [n/128][k/16][8 tiles][8K words]
+    // linear: one packed matrix [n/128][k/16][8 tiles][8K words], its svh, y rows
+    const uint8_t* packed;
     const __half* svh;
+    int K;
     void* y;
     int ldy, y_dtype;
-    int M, k, n, K;
-    int t_stages, t_stage_bytes;
+    int M, k, n;                  // linear: M rows; grouped: k, n of the launch's projection
+    // grouped: alignment tables (items of <= 256 rows of one expert) and the expert table
+    const int* n_items;
+    const int* item_expert;
+    const int* item_start;
+    const int* item_cnt;
+    const float* pair_w;          // down: routing weight of a pair position
+    const ExpertDesc* experts;
+    float act_limit;
+    __half* a_dn;                 // gate|up: the down projection's activation rows [positions][I]
+    float* ybuf;                  // down: weighted rows [positions][H]
     int* status;
 };
 
-// Per-thread constant addressing of the decode: for each of the warp's tiles in a chunk, the tile's byte
-// offset in a trellis stage and the four swizzled byte offsets in a B stage that receive the lane's fragment
-// registers {n, k..k+1}, {n + 8, k..}, {n, k + 8..}, {n + 8, k + 8..} (n = tile column + g, k = tile row + 2q).
-constexpr int TC_TPW = TC_TILES / TC_DEC_WARPS;
+// ------------------------------------------------------------------------------------------------ decode
+
+// Per-thread constant addressing of the decode: for each of the warp's 4 tiles of a chunk, the tile's byte offset in
+// a trellis stage and the four swizzled byte offsets in a B stage that receive the lane's fragment registers
+// {n, k..k+1}, {n + 8, k..}, {n, k + 8..}, {n + 8, k + 8..} (n = tile column + g, k = tile row + 2q).
+// Linear / down: a stage holds two column blocks [cb][4 tile-rows][8 tiles][32K bytes] of one matrix; warp dw takes
+// tiles 4dw .. 4dw+3 of the 64. Gate|up: a stage holds 4 tile-rows of the fused block, each [8 gate tiles (Kg) |
+// 8 up tiles (Ku)]; warps 0-7 take the gate tiles, 8-15 the up tiles, and B rows 0-127 / 128-255 are gate / up.
 struct TcDecodeMap {
     uint32_t tile[TC_TPW];
     uint32_t st[TC_TPW][4];
 };
 
-template <int K>
-__device__ __forceinline__ TcDecodeMap tc_decode_map(int dw, int lane) {
+__device__ __forceinline__ TcDecodeMap tc_decode_map(int epi, int dw, int lane, int Kg, int Ku) {
     TcDecodeMap mp;
     const int g = lane >> 2, q = lane & 3;
 #pragma unroll
     for (int j = 0; j < TC_TPW; ++j) {
-        const int ti = dw * TC_TPW + j;
-        const int cb = ti >> 5, tr = (ti >> 3) & 3, t = ti & 7;   // column block, tile-row, tile
-        mp.tile[j] = (uint32_t)(((cb * 4 + tr) * 8 + t) * 32 * K);
-        const int n0 = cb * 128 + t * 16 + g, k0 = tr * 16 + 2 * q;
+        int n0, k0;
+        if (epi == TC_GATEUP) {
+            const int mat = dw >> 3, idx = (dw & 7) * TC_TPW + j;    // 0..31 within the matrix
+            const int tr = idx >> 3, t = idx & 7;
+            const int row_stride = 8 * 32 * Kg + 8 * 32 * Ku;
+            mp.tile[j] = (uint32_t)(tr * row_stride + (mat ? 8 * 32 * Kg : 0) + t * 32 * (mat ? Ku : Kg));
+            n0 = mat * 128 + t * 16 + g;
+            k0 = tr * 16 + 2 * q;
+        } else {
+            const int ti = dw * TC_TPW + j;
+            const int cb = ti >> 5, tr = (ti >> 3) & 3, t = ti & 7;
+            mp.tile[j] = (uint32_t)(((cb * 4 + tr) * 8 + t) * 32 * Ku);
+            n0 = cb * 128 + t * 16 + g;
+            k0 = tr * 16 + 2 * q;
+        }
         mp.st[j][0] = sw128_off(n0, k0);
         mp.st[j][1] = sw128_off(n0 + 8, k0);
         mp.st[j][2] = sw128_off(n0, k0 + 8);
@@ -140,7 +163,6 @@ __device__ __forceinline__ TcDecodeMap tc_decode_map(int dw, int lane) {
     return mp;
 }
 
-// Decode one chunk's trellis tiles of this warp into the swizzled B stage.
 template <int K>
 __device__ __forceinline__ void tc_decode_chunk(const uint8_t* tst, uint8_t* bst, const TcDecodeMap& mp,
                                                 const LaneWords& lw) {
@@ -154,16 +176,16 @@ __device__ __forceinline__ void tc_decode_chunk(const uint8_t* tst, uint8_t* bst
 }
 
 template <int K>
-__device__ void tc_decoder_loop(const TcArgs& p, uint8_t* smem, uint64_t* t_full, uint64_t* t_empty,
-                                uint64_t* b_full, uint64_t* b_empty, int nk, int dw, int lane, bool& to) {
-    const TcDecodeMap mp = tc_decode_map<K>(dw, lane);
+__device__ void tc_decoder_loop(const TcDecodeMap& mp, uint8_t* smem, int t_stages, int t_stage_bytes,
+                                uint64_t* t_full, uint64_t* t_empty, uint64_t* b_full, uint64_t* b_empty, int nk,
+                                int lane, bool& to) {
     const LaneWords lw = lane_words<K>(lane);
     for (int kc = 0; kc < nk; ++kc) {
-        const int ts = kc % p.t_stages, s = kc % TC_B_STAGES;
-        if (!to && !mbar_wait(&t_full[ts], (kc / p.t_stages) & 1)) to = true;
+        const int ts = kc % t_stages, s = kc % TC_B_STAGES;
+        if (!to && !mbar_wait(&t_full[ts], (kc / t_stages) & 1)) to = true;
         if (kc >= TC_B_STAGES && !to && !mbar_wait(&b_empty[s], ((kc / TC_B_STAGES) - 1) & 1)) to = true;
         if (!to)
-            tc_decode_chunk<K>(smem + TcSmem::t0 + (size_t)ts * p.t_stage_bytes, smem + TcSmem::b0 + s * TC_B_BYTES,
+            tc_decode_chunk<K>(smem + TcSmem::t0 + (size_t)ts * t_stage_bytes, smem + TcSmem::b0 + s * TC_TILE_BYTES,
                                mp, lw);
         fence_proxy_async();                                  // generic-proxy writes -> the tensor core's reads
         __syncwarp();
@@ -174,26 +196,94 @@ __device__ void tc_decoder_loop(const TcArgs& p, uint8_t* smem, uint64_t* t_full
     }
 }
 
-__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap amap,
+__device__ void tc_decoder_dispatch(int K, const TcDecodeMap& mp, uint8_t* smem, int t_stages, int t_stage_bytes,
+                                    uint64_t* t_full, uint64_t* t_empty, uint64_t* b_full, uint64_t* b_empty, int nk,
+                                    int lane, bool& to) {
+#define EXL3_TC_DEC(KK) \
+    tc_decoder_loop<KK>(mp, smem, t_stages, t_stage_bytes, t_full, t_empty, b_full, b_empty, nk, lane, to)
+    switch (K) {
+        case 1: EXL3_TC_DEC(1); break;
+        case 2: EXL3_TC_DEC(2); break;
+        case 3: EXL3_TC_DEC(3); break;
+        case 4: EXL3_TC_DEC(4); break;
+        case 5: EXL3_TC_DEC(5); break;
+        case 6: EXL3_TC_DEC(6); break;
+        case 7: EXL3_TC_DEC(7); break;
+        default: EXL3_TC_DEC(8); break;
+    }
+#undef EXL3_TC_DEC
+}
+
+// ------------------------------------------------------------------------------------------------ kernel
+
+template <int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap amap0,
+                                                           const __grid_constant__ CUtensorMap amap1,
                                                            const TcArgs p) {
+    constexpr int NMAT = tc_nmat(EPI);
+    constexpr int AST = tc_a_stages(EPI);
+    constexpr int A_STAGE = NMAT * TC_TILE_BYTES;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_trigger();
+
+    // ---- the tile: rows [m0, m0 + rows) of the activation matrices, output columns from n0 ----
+    int m0, rows, n0, Ku = p.K, Kg = p.K, expert = 0;
+    const uint8_t* wmat;                                      // packed weights of the tile's first column block
+    size_t cb_bytes;                                          // bytes of one column block (all k)
+    const __half* svh0;
+    const __half* svh1 = nullptr;
+    if constexpr (EPI == TC_LINEAR) {
+        m0 = blockIdx.y * TC_BM;
+        rows = min(TC_BM, p.M - m0);
+        n0 = blockIdx.x * TC_BN;
+        cb_bytes = (size_t)(p.k / 16) * 8 * 32 * Ku;
+        wmat = p.packed + (size_t)(n0 / 128) * cb_bytes;
+        svh0 = p.svh;
+    } else {
+        pdl_wait();                                           // the alignment tables come from an earlier kernel
+        const int item = blockIdx.y;
+        if (item >= __ldcg(p.n_items)) return;                // before any barrier or TMEM allocation
+        expert = __ldcg(p.item_expert + item);
+        m0 = __ldcg(p.item_start + item);
+        rows = __ldcg(p.item_cnt + item);
+        const ExpertDesc& ed = p.experts[expert];
+        if constexpr (EPI == TC_GATEUP) {
+            Kg = ed.K[0];
+            Ku = ed.K[1];
+            n0 = blockIdx.x * 128;                            // output column block of gate and up
+            cb_bytes = (size_t)(p.k / 16) * (8 * 32 * Kg + 8 * 32 * Ku);
+            wmat = reinterpret_cast<const uint8_t*>(ed.tr[0]) + (size_t)blockIdx.x * cb_bytes;
+            svh0 = ed.svh[0];
+            svh1 = ed.svh[1];
+        } else {
+            Ku = ed.K[2];
+            Kg = Ku;
+            n0 = blockIdx.x * TC_BN;
+            cb_bytes = (size_t)(p.k / 16) * 8 * 32 * Ku;
+            wmat = reinterpret_cast<const uint8_t*>(ed.tr[2]) + (size_t)(n0 / 128) * cb_bytes;
+            svh0 = ed.svh[2];
+        }
+    }
+    const int nk = p.k / TC_BK;
+    // trellis stage: linear / down two column blocks x 4 tile-rows x 8 tiles; gate|up 4 fused tile-rows
+    const int t_stage_bytes = EPI == TC_GATEUP ? 4 * (8 * 32 * Kg + 8 * 32 * Ku) : 2 * 4 * 8 * 32 * Ku;
+    int t_stages = TC_T_RING / t_stage_bytes;
+    if (t_stages > TC_MAX_TSTAGES) t_stages = TC_MAX_TSTAGES;
+
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::bars);
     uint64_t* a_full = bars;
-    uint64_t* a_empty = a_full + TC_A_STAGES;
-    uint64_t* b_full = a_empty + TC_A_STAGES;
+    uint64_t* a_empty = a_full + 4;
+    uint64_t* b_full = a_empty + 4;
     uint64_t* b_empty = b_full + TC_B_STAGES;
     uint64_t* t_full = b_empty + TC_B_STAGES;
     uint64_t* t_empty = t_full + TC_MAX_TSTAGES;
     uint64_t* acc_full = t_empty + TC_MAX_TSTAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::tmem_slot);
-    const int n0 = blockIdx.x * TC_BN, m0 = blockIdx.y * TC_BM;
-    const int nk = p.k / TC_BK;
-    pdl_trigger();
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < TC_A_STAGES; ++s) {
+        for (int s = 0; s < AST; ++s) {
             mbar_init(&a_full[s], 1);
             mbar_init(&a_empty[s], 1);
         }
@@ -201,14 +291,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             mbar_init(&b_full[s], TC_DEC_WARPS);
             mbar_init(&b_empty[s], 1);
         }
-        for (int s = 0; s < p.t_stages; ++s) {
+        for (int s = 0; s < t_stages; ++s) {
             mbar_init(&t_full[s], 1);
             mbar_init(&t_empty[s], TC_DEC_WARPS);
         }
         mbar_init(acc_full, 1);
         fence_barrier_init();
     }
-    if (warp == 1) {                                          // TMEM: 512 columns = four 128 x 128 fp32 accumulators
+    if (warp == 1) {                                          // TMEM: all 512 columns (four 128 x 128 fp32 blocks)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -221,41 +311,55 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
 
     if (warp == 0) {
         // ---------------- activation tiles (TMA) ----------------
-        pdl_wait();                                           // the rotated activations come from the previous kernel
+        pdl_wait();                                           // the rotated activations come from an earlier kernel
         if (lane == 0) {
-            int last_s[TC_A_STAGES];
-            for (int s = 0; s < TC_A_STAGES; ++s) last_s[s] = -1;
+            int last_s[4] = {-1, -1, -1, -1};
             for (int kc = 0; kc < nk && !to; ++kc) {
-                const int s = kc % TC_A_STAGES;
-                if (kc >= TC_A_STAGES && !mbar_wait(&a_empty[s], ((kc / TC_A_STAGES) - 1) & 1)) { to = true; break; }
-                mbar_expect_tx(&a_full[s], TC_A_BYTES);
-#pragma unroll
-                for (int h = 0; h < (TC_BM + 255) / 256; ++h)  // boxes of 256 rows
-                    tma_load_2d(smem + TcSmem::a0 + s * TC_A_BYTES + h * (TC_A_BYTES * 256 / TC_BM), &amap,
-                                kc * TC_BK, m0 + h * 256, &a_full[s]);
+                const int s = kc % AST;
+                if (kc >= AST && !mbar_wait(&a_empty[s], ((kc / AST) - 1) & 1)) { to = true; break; }
+                mbar_expect_tx(&a_full[s], A_STAGE);
+                uint8_t* dst = smem + TcSmem::a0 + s * A_STAGE;
+                tma_load_2d(dst, &amap0, kc * TC_BK, m0, &a_full[s]);
+                if constexpr (NMAT == 2) tma_load_2d(dst + TC_TILE_BYTES, &amap1, kc * TC_BK, m0, &a_full[s]);
                 last_s[s] = kc;
             }
-            for (int s = 0; s < TC_A_STAGES; ++s)             // copies landed before the CTA may exit
-                if (last_s[s] >= 0 && !mbar_wait(&a_full[s], (last_s[s] / TC_A_STAGES) & 1)) to = true;
+            for (int s = 0; s < AST; ++s)                     // copies landed before the CTA may exit
+                if (last_s[s] >= 0 && !mbar_wait(&a_full[s], (last_s[s] / AST) & 1)) to = true;
         }
     } else if (warp == 1) {
         // ---------------- MMA issue (one lane) ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = tc_idesc_f16(128, TC_BN);
             for (int kc = 0; kc < nk; ++kc) {
-                const int sa = kc % TC_A_STAGES, sb = kc % TC_B_STAGES;
-                if (!to && !mbar_wait(&a_full[sa], (kc / TC_A_STAGES) & 1)) to = true;
+                const int sa = kc % AST, sb = kc % TC_B_STAGES;
+                if (!to && !mbar_wait(&a_full[sa], (kc / AST) & 1)) to = true;
                 if (!to && !mbar_wait(&b_full[sb], (kc / TC_B_STAGES) & 1)) to = true;
                 tc_fence_after();
                 if (!to) {
-                    const uint32_t a_base = smem_u32(smem + TcSmem::a0 + sa * TC_A_BYTES);
-                    const uint32_t b_base = smem_u32(smem + TcSmem::b0 + sb * TC_B_BYTES);
+                    const uint32_t a_base = smem_u32(smem + TcSmem::a0 + sa * A_STAGE);
+                    const uint32_t b_base = smem_u32(smem + TcSmem::b0 + sb * TC_TILE_BYTES);
 #pragma unroll
-                    for (int kk = 0; kk < TC_BK / 16; ++kk)
+                    for (int kk = 0; kk < TC_BK / 16; ++kk) {
+                        const uint32_t acc = (kc | kk) != 0;
+                        if constexpr (EPI == TC_GATEUP) {
+                            // accumulator (mat, j) at TMEM column (2 mat + j) * 128: activation tile of the matrix,
+                            // row half j; B rows of the matrix (gate 0-127, up 128-255)
 #pragma unroll
-                        for (int j = 0; j < TC_ACC; ++j)
-                            tc_mma_f16(tmem + j * TC_BN, sw128_desc(a_base + j * (TC_A_BYTES / TC_ACC) + kk * 32),
-                                       sw128_desc(b_base + kk * 32), idesc, (kc | kk) != 0);
+                            for (int mat = 0; mat < 2; ++mat)
+#pragma unroll
+                                for (int j = 0; j < 2; ++j)
+                                    tc_mma_f16(tmem + (2 * mat + j) * 128,
+                                               sw128_desc(a_base + mat * TC_TILE_BYTES + j * (TC_TILE_BYTES / 2) +
+                                                          kk * 32),
+                                               sw128_desc(b_base + mat * (TC_TILE_BYTES / 2) + kk * 32),
+                                               tc_idesc_f16(128, 128), acc);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 2; ++j)
+                                tc_mma_f16(tmem + j * TC_BN,
+                                           sw128_desc(a_base + j * (TC_TILE_BYTES / 2) + kk * 32),
+                                           sw128_desc(b_base + kk * 32), tc_idesc_f16(128, TC_BN), acc);
+                        }
+                    }
                 }
                 tc_commit(&a_empty[sa]);                      // the stages are free once these MMAs completed
                 tc_commit(&b_empty[sb]);
@@ -265,97 +369,138 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     } else if (warp == 2) {
         // ---------------- trellis tiles (bulk copies) ----------------
         if (lane == 0) {
-            const size_t block_bytes = (size_t)(p.k / 16) * 8 * 32 * p.K;       // one 128-column block, all k
             int last[TC_MAX_TSTAGES];
             for (int s = 0; s < TC_MAX_TSTAGES; ++s) last[s] = -1;
+            // column blocks present (the last tile of a linear or down projection may have 1); gate|up: one fused block
+            const int nbv = EPI == TC_GATEUP ? 1 : min(2, (p.n - n0) / 128);
+            const uint32_t blk = (uint32_t)(t_stage_bytes / (EPI == TC_GATEUP ? 1 : 2));
             for (int kc = 0; kc < nk && !to; ++kc) {
-                const int ts = kc % p.t_stages;
-                if (kc >= p.t_stages && !mbar_wait(&t_empty[ts], ((kc / p.t_stages) - 1) & 1)) { to = true; break; }
-                const uint32_t blk = (uint32_t)(p.t_stage_bytes / TC_NB);           // a block's 4 tile-rows
-                const int nbv = min(TC_NB, (p.n - n0) / 128);    // column blocks present (last tile may be partial)
+                const int ts = kc % t_stages;
+                if (kc >= t_stages && !mbar_wait(&t_empty[ts], ((kc / t_stages) - 1) & 1)) { to = true; break; }
                 mbar_expect_tx(&t_full[ts], blk * (uint32_t)nbv);
-                uint8_t* dst = smem + TcSmem::t0 + (size_t)ts * p.t_stage_bytes;
-                for (int b = 0; b < nbv; ++b) {
-                    const uint8_t* src = p.packed + (size_t)(n0 / 128 + b) * block_bytes + (size_t)kc * blk;
-                    bulk_g2s(dst + b * blk, src, blk, &t_full[ts]);
-                }
+                uint8_t* dst = smem + TcSmem::t0 + (size_t)ts * t_stage_bytes;
+                for (int b = 0; b < nbv; ++b)
+                    bulk_g2s(dst + b * blk, wmat + (size_t)b * cb_bytes + (size_t)kc * blk, blk, &t_full[ts]);
                 last[ts] = kc;
             }
-            for (int s = 0; s < p.t_stages; ++s)
-                if (last[s] >= 0 && !mbar_wait(&t_full[s], (last[s] / p.t_stages) & 1)) to = true;
+            for (int s = 0; s < t_stages; ++s)
+                if (last[s] >= 0 && !mbar_wait(&t_full[s], (last[s] / t_stages) & 1)) to = true;
         }
     } else {
         // ---------------- decoders, then the epilogue ----------------
         const int dw = warp - 3;
-        switch (p.K) {
-            case 1: tc_decoder_loop<1>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
-            case 2: tc_decoder_loop<2>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
-            case 3: tc_decoder_loop<3>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
-            case 4: tc_decoder_loop<4>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
-            case 5: tc_decoder_loop<5>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
-            case 6: tc_decoder_loop<6>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
-            case 7: tc_decoder_loop<7>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
-            default: tc_decoder_loop<8>(p, smem, t_full, t_empty, b_full, b_empty, nk, dw, lane, to); break;
-        }
-        pdl_wait();                                           // y may be in use by an earlier kernel until here
+        const TcDecodeMap mp = tc_decode_map(EPI, dw, lane, Kg, Ku);
+        const int Kw = (EPI == TC_GATEUP && dw < 8) ? Kg : Ku;
+        tc_decoder_dispatch(Kw, mp, smem, t_stages, t_stage_bytes, t_full, t_empty, b_full, b_empty, nk, lane, to);
+
+        pdl_wait();                                           // outputs may be in use by an earlier kernel until here
         if (!to && !mbar_wait(acc_full, 0)) to = true;
         tc_fence_after();
-        // TMEM lane quadrant of this warp; the four warps of a quadrant take one 128 x 128 block each:
-        // block bi = accumulator bi / TC_NB, column block bi % TC_NB
+        // the four 128 x 128 accumulator blocks: block bi at TMEM column 128 bi. Linear / down: bi = 2 j + b
+        // (row half j, column block b); gate|up: bi = 2 mat + j. The four warps of a TMEM lane quadrant each load
+        // one block; staging [2][128 rows][128 cols] fp32 in the activation ring (free after the main loop), columns
+        // XOR-swizzled by the row. Pass 0: blocks of row half 0, pass 1: row half 1.
         const int quad = warp & 3, bi = dw >> 2;              // warps 3..18: quad covers 0..3 four times
-        static_assert(TC_ACC * TC_NB == 4, "four 128 x 128 blocks per tile");
-        // staging: [2][128 rows][128 cols] fp32 in the A stages (free after the main loop), columns XOR-swizzled
-        // by the row; blocks 0, 1 then 2, 3
+        const int bj = EPI == TC_GATEUP ? (bi & 1) : (bi >> 1);   // row half of block bi
+        const int bslot = EPI == TC_GATEUP ? (bi >> 1) : (bi & 1); // staging slot: column block, or gate / up
+        float* stage = reinterpret_cast<float*>(smem + TcSmem::a0);
         for (int pass = 0; pass < 2; ++pass) {
-            if ((bi >> 1) == pass) {
-                float* st = reinterpret_cast<float*>(smem + TcSmem::a0) + (size_t)(bi & 1) * 128 * 128;
+            if (bj == pass) {
+                float* st = stage + (size_t)bslot * 128 * 128;
                 const int row = quad * 32 + lane;             // accumulator row = TMEM lane
-                const uint32_t col0 = (uint32_t)((bi / TC_NB) * TC_BN + (bi % TC_NB) * 128);
 #pragma unroll
                 for (int c0 = 0; c0 < 128; c0 += 32) {
                     uint32_t r[32];
-                    tc_ld32(tmem + ((uint32_t)(quad * 32) << 16) + col0 + (uint32_t)c0, r);
+                    tc_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(bi * 128 + c0), r);
 #pragma unroll
                     for (int c = 0; c < 32; ++c)
                         st[row * 128 + ((c0 + c) ^ (row & 31))] = __uint_as_float(r[c]);
                 }
             }
             asm volatile("bar.sync 1, %0;" ::"r"(TC_DEC_WARPS * 32) : "memory");
-            // 2 accumulators x 128 rows over 16 warps, one row at a time
-            for (int rb = dw; rb < 2 * 128; rb += TC_DEC_WARPS) {
-                const int jj = rb >> 7, row = rb & 127;
-                const float* src = reinterpret_cast<const float*>(smem + TcSmem::a0) + (size_t)jj * 128 * 128 +
-                                   row * 128;
-                float v[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) v[e] = src[(4 * lane + e) ^ (row & 31)];
-                fwht128_warp(v, lane);
-                const int blk = pass * 2 + jj;
-                const int m = m0 + (blk / TC_NB) * 128 + row;
-                const int col = n0 + (blk % TC_NB) * 128 + 4 * lane;
-                if (m < p.M && col < p.n) {
-                    float o[4];
+            if constexpr (EPI == TC_GATEUP) {
+                // row r of this half: gate and up blocks -> act -> the down input's rotation, into a_dn
+                const __half* suh_d = p.experts[expert].suh[2];
+                for (int row = dw; row < 128; row += TC_DEC_WARPS) {
+                    const int rr = pass * 128 + row;
+                    if (rr >= rows) continue;
+                    float gv[4], uv[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float sv = __half2float(p.svh[col + e]);
-                        if (p.y_dtype == EXL3_F16)
-                            o[e] = __half2float(__float2half_rn(__half2float(__float2half_rn(v[e] * kRsqrt128)) * sv));
-                        else
-                            o[e] = v[e] * kRsqrt128 * sv;
+                        gv[e] = stage[row * 128 + ((4 * lane + e) ^ (row & 31))];
+                        uv[e] = stage[128 * 128 + row * 128 + ((4 * lane + e) ^ (row & 31))];
                     }
-                    if (p.y_dtype == EXL3_F32) {
-                        *reinterpret_cast<float4*>(static_cast<float*>(p.y) + (size_t)m * p.ldy + col) =
-                            make_float4(o[0], o[1], o[2], o[3]);
-                    } else if (p.y_dtype == EXL3_F16) {
-                        __half2 h01 = __floats2half2_rn(o[0], o[1]), h23 = __floats2half2_rn(o[2], o[3]);
-                        uint2 u;
-                        u.x = *reinterpret_cast<uint32_t*>(&h01);
-                        u.y = *reinterpret_cast<uint32_t*>(&h23);
-                        *reinterpret_cast<uint2*>(static_cast<__half*>(p.y) + (size_t)m * p.ldy + col) = u;
-                    } else {
-                        __nv_bfloat16* yp = static_cast<__nv_bfloat16*>(p.y) + (size_t)m * p.ldy + col;
+                    fwht128_warp(gv, lane);
+                    fwht128_warp(uv, lane);
+                    const int col = n0 + 4 * lane;            // column of I
+                    float h[4];
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) yp[e] = __float2bfloat16_rn(o[e]);
+                    for (int e = 0; e < 4; ++e) {
+                        const float gg = __half2float(__float2half_rn(
+                            __half2float(__float2half_rn(gv[e] * kRsqrt128)) * __half2float(svh0[col + e])));
+                        float uu = __half2float(__float2half_rn(
+                            __half2float(__float2half_rn(uv[e] * kRsqrt128)) * __half2float(svh1[col + e])));
+                        float sg = silu_f(gg);
+                        if (p.act_limit != 0.f) {
+                            sg = fminf(sg, p.act_limit);
+                            uu = fminf(fmaxf(uu, -p.act_limit), p.act_limit);
+                        }
+                        const float act = __half2float(__float2half_rn(sg * uu));
+                        h[e] = __half2float(__float2half_rn(act * __half2float(suh_d[col + e])));
+                    }
+                    fwht128_warp(h, lane);
+                    __half2 h01 = __floats2half2_rn(h[0] * kRsqrt128, h[1] * kRsqrt128);
+                    __half2 h23 = __floats2half2_rn(h[2] * kRsqrt128, h[3] * kRsqrt128);
+                    uint2 u;
+                    u.x = *reinterpret_cast<uint32_t*>(&h01);
+                    u.y = *reinterpret_cast<uint32_t*>(&h23);
+                    *reinterpret_cast<uint2*>(p.a_dn + (size_t)(m0 + rr) * p.n + col) = u;
+                }
+            } else {
+                // 2 column blocks x 128 rows over 16 warps, one row at a time
+                for (int rb = dw; rb < 2 * 128; rb += TC_DEC_WARPS) {
+                    const int b = rb >> 7, row = rb & 127;
+                    const int rr = pass * 128 + row;
+                    const int col = n0 + b * 128 + 4 * lane;
+                    if (rr >= rows || col >= p.n) continue;
+                    const float* src = stage + (size_t)b * 128 * 128 + row * 128;
+                    float v[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) v[e] = src[(4 * lane + e) ^ (row & 31)];
+                    fwht128_warp(v, lane);
+                    if constexpr (EPI == TC_DOWN) {
+                        const float wgt = __ldcg(p.pair_w + m0 + rr);
+                        float o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) o[e] = wgt * (v[e] * kRsqrt128 * __half2float(svh0[col + e]));
+                        *reinterpret_cast<float4*>(p.ybuf + (size_t)(m0 + rr) * p.n + col) =
+                            make_float4(o[0], o[1], o[2], o[3]);
+                    } else {
+                        const int m = m0 + rr;
+                        float o[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float sv = __half2float(svh0[col + e]);
+                            if (p.y_dtype == EXL3_F16)
+                                o[e] = __half2float(
+                                    __float2half_rn(__half2float(__float2half_rn(v[e] * kRsqrt128)) * sv));
+                            else
+                                o[e] = v[e] * kRsqrt128 * sv;
+                        }
+                        if (p.y_dtype == EXL3_F32) {
+                            *reinterpret_cast<float4*>(static_cast<float*>(p.y) + (size_t)m * p.ldy + col) =
+                                make_float4(o[0], o[1], o[2], o[3]);
+                        } else if (p.y_dtype == EXL3_F16) {
+                            __half2 h01 = __floats2half2_rn(o[0], o[1]), h23 = __floats2half2_rn(o[2], o[3]);
+                            uint2 u;
+                            u.x = *reinterpret_cast<uint32_t*>(&h01);
+                            u.y = *reinterpret_cast<uint32_t*>(&h23);
+                            *reinterpret_cast<uint2*>(static_cast<__half*>(p.y) + (size_t)m * p.ldy + col) = u;
+                        } else {
+                            __nv_bfloat16* yp = static_cast<__nv_bfloat16*>(p.y) + (size_t)m * p.ldy + col;
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) yp[e] = __float2bfloat16_rn(o[e]);
+                        }
                     }
                 }
             }
@@ -370,6 +515,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }
 }
+
+// ------------------------------------------------------------------------------------------------ activation rows
 
 // Rotated input rows in plain row-major order: xh[m][k] = fp16(H(fp16(x * suh)) / sqrt(128)) per 128-block.
 static __global__ void __launch_bounds__(256) k_rotate_rows(const void* x, int ldx, int x_bf16, int M, int k,
@@ -395,9 +542,116 @@ static __global__ void __launch_bounds__(256) k_rotate_rows(const void* x, int l
     }
 }
 
+// Rotated gate and up input rows of every pair position, row-major: a_gu[mat][pos][H] = rot(x[token] * suh of the
+// position's expert's matrix mat). Positions beyond the count in use are skipped.
+static __global__ void __launch_bounds__(256) k_rotate_pairs(const void* x, int ldx, int x_bf16, int H, int P,
+                                                             const int* n_pos, const int* pair_tok,
+                                                             const int* pair_expert, const ExpertDesc* experts,
+                                                             __half* a_gu) {
+    pdl_wait();
+    pdl_trigger();
+    const int KB = H / 128, lane = threadIdx.x & 31;
+    const int np = min(P, __ldcg(n_pos));
+    for (long j = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < (long)np * 2 * KB;
+         j += ((long)gridDim.x * blockDim.x) >> 5) {
+        const int pos = (int)(j / (2 * KB)), mat = (int)((j / KB) % 2), kb = (int)(j % KB);
+        const int tok = __ldcg(pair_tok + pos), e = __ldcg(pair_expert + pos);
+        const __half* suh = experts[e].suh[mat];
+        const __half* su = suh ? suh + kb * 128 : nullptr;
+        float v[4];
+        if (x_bf16)
+            rotated_block<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x) + (size_t)tok * ldx + kb * 128, su,
+                                         lane, v);
+        else
+            rotated_block<__half>(static_cast<const __half*>(x) + (size_t)tok * ldx + kb * 128, su, lane, v);
+        __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t*>(&h01);
+        u.y = *reinterpret_cast<uint32_t*>(&h23);
+        *reinterpret_cast<uint2*>(a_gu + ((size_t)mat * P + pos) * H + kb * 128 + 4 * lane) = u;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ host launch
+
 using PFN_encode_tiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                       const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Tensor map of a row-major [rows][cols] fp16 matrix: boxes of 64 columns x 256 rows, 128-byte swizzle, zero fill.
+static int make_row_map(CUtensorMap* map, const __half* base, long rows, int cols, const char* what) {
+    static PFN_encode_tiled encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        EXL3_REQUIRE(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+                         q == cudaDriverEntryPointSuccess && fn,
+                     EXL3_ERR_CUDA, "%s: cuTensorMapEncodeTiled is not available", what);
+        encode = reinterpret_cast<PFN_encode_tiled>(fn);
+    }
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {TC_BK, TC_BM};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult cr = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    EXL3_REQUIRE(cr == CUDA_SUCCESS, EXL3_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)cr);
+    return EXL3_OK;
+}
+
+template <int EPI>
+static int launch_tc(const CUtensorMap& m0, const CUtensorMap& m1, const TcArgs& a, dim3 grid, cudaStream_t st,
+                     const char* what) {
+    static int configured[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !configured[dev]) {
+        EXL3_REQUIRE(cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          TcSmem::total) == cudaSuccess,
+                     EXL3_ERR_CUDA, "%s: cudaFuncSetAttribute: %s", what, cudaGetErrorString(cudaGetLastError()));
+        configured[dev] = 1;
+    }
+    cudaError_t e = launch_pdl(k_gemm_tc<EPI>, grid, dim3(TC_THREADS), TcSmem::total, st, m0, m1, a);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
+    return EXL3_OK;
+}
+
+int tc_moe_prefill(const TcMoeArgs& m, cudaStream_t st) {
+    const char* what = "exl3_moe_prefill";
+    {
+        const long jobs = (long)m.P * 2 * (m.H / 128);
+        long blocks = (jobs + 7) / 8;
+        if (blocks > 8L * num_sms()) blocks = 8L * num_sms();
+        cudaError_t e = launch_pdl(k_rotate_pairs, dim3((unsigned)blocks), dim3(256), 0, st, m.x, m.ldx, m.x_bf16,
+                                   m.H, m.P, m.n_pos, m.pair_tok, m.pair_expert, m.experts, m.a_gu);
+        EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "%s: rotate launch failed: %s", what, cudaGetErrorString(e));
+    }
+    if (m.max_items == 0) return EXL3_OK;
+    TcArgs a = {};
+    a.n_items = m.n_items;
+    a.item_expert = m.item_expert;
+    a.item_start = m.item_start;
+    a.item_cnt = m.item_cnt;
+    a.pair_w = m.pair_w;
+    a.experts = m.experts;
+    a.act_limit = m.act_limit;
+    a.a_dn = m.a_dn;
+    a.ybuf = m.ybuf;
+    a.status = device_status_ptr();
+    CUtensorMap mg, mu, md;
+    int rc = make_row_map(&mg, m.a_gu, m.P, m.H, what);
+    if (!rc) rc = make_row_map(&mu, m.a_gu + (size_t)m.P * m.H, m.P, m.H, what);
+    if (!rc) rc = make_row_map(&md, m.a_dn, m.P, m.I, what);
+    if (rc) return rc;
+    a.k = m.H;
+    a.n = m.I;
+    rc = launch_tc<TC_GATEUP>(mg, mu, a, dim3(m.I / 128, m.max_items), st, what);
+    if (rc) return rc;
+    a.k = m.I;
+    a.n = m.H;
+    return launch_tc<TC_DOWN>(md, md, a, dim3((m.H + TC_BN - 1) / TC_BN, m.max_items), st, what);
+}
 
 }  // namespace exl3
 
@@ -433,8 +687,6 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
                  need);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     __half* xh = static_cast<__half*>(workspace);
-
-    // rotated activations, row-major fp16
     {
         const long jobs = (long)M * (k / 128);
         long blocks = (jobs + 7) / 8;
@@ -443,56 +695,22 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
                                    (int)(x_dtype == EXL3_BF16), M, k, static_cast<const __half*>(suh), xh);
         EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_gemm_tc: rotate launch failed: %s", cudaGetErrorString(e));
     }
-    // tensor map of xh: [M][k] fp16, box 64 x 256, 128-byte swizzle, zero fill beyond M
     CUtensorMap map;
-    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)M};
-    const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-    const cuuint32_t box[2] = {TC_BK, TC_BM < 256 ? TC_BM : 256};  // TC_BM / 256 boxes per stage
-    const cuuint32_t estr[2] = {1, 1};
-    // the driver entry point through the runtime (no link-time dependency on libcuda)
-    static PFN_encode_tiled encode = nullptr;
-    if (!encode) {
-        void* fn = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        EXL3_REQUIRE(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
-                         q == cudaDriverEntryPointSuccess && fn,
-                     EXL3_ERR_CUDA, "exl3_gemm_tc: cuTensorMapEncodeTiled is not available");
-        encode = reinterpret_cast<PFN_encode_tiled>(fn);
-    }
-    CUresult cr = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, xh, dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    EXL3_REQUIRE(cr == CUDA_SUCCESS, EXL3_ERR_CUDA, "exl3_gemm_tc: cuTensorMapEncodeTiled failed (%d)", (int)cr);
-
+    int rc = make_row_map(&map, xh, M, k, "exl3_gemm_tc");
+    if (rc) return rc;
     TcArgs a = {};
     a.packed = static_cast<const uint8_t*>(packed);
     a.svh = static_cast<const __half*>(svh);
+    a.K = K;
     a.y = y;
     a.ldy = ldy;
     a.y_dtype = y_dtype;
     a.M = M;
     a.k = k;
     a.n = n;
-    a.K = K;
-    a.t_stage_bytes = TC_NB * 4 * 8 * 32 * K;                // column blocks x 4 tile-rows x 8 tiles
-    a.t_stages = TC_T_RING / a.t_stage_bytes;
-    if (a.t_stages > TC_MAX_TSTAGES) a.t_stages = TC_MAX_TSTAGES;
     a.status = device_status_ptr();
-
-    static int configured[64] = {0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev >= 0 && dev < 64 && !configured[dev]) {
-        EXL3_REQUIRE(cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem::total) ==
-                         cudaSuccess,
-                     EXL3_ERR_CUDA, "exl3_gemm_tc: cudaFuncSetAttribute: %s",
-                     cudaGetErrorString(cudaGetLastError()));
-        configured[dev] = 1;
-    }
-    const dim3 grid((n + TC_BN - 1) / TC_BN, (M + TC_BM - 1) / TC_BM);
-    cudaError_t e = launch_pdl(k_gemm_tc, grid, dim3(TC_THREADS), TcSmem::total, st, map, a);
-    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_gemm_tc: launch failed: %s", cudaGetErrorString(e));
-    return EXL3_OK;
+    return launch_tc<TC_LINEAR>(map, map, a, dim3((n + TC_BN - 1) / TC_BN, (M + TC_BM - 1) / TC_BM), st,
+                                "exl3_gemm_tc");
 }
 
 }  // extern "C"

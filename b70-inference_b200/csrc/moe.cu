@@ -10,6 +10,7 @@
 //   the shared expert's row of token m), down input rows in xf order fp16 [P][I] (by position), ybuf fp32 [P][H],
 //   GEMV split-unit partial slots.
 #include "gemv.cuh"
+#include "tc.cuh"
 
 namespace exl3 {
 
@@ -571,11 +572,95 @@ static int run_combine(int M, int topk, int E, int shared, int H, int I, void* o
     return EXL3_OK;
 }
 
+// ------------------------------------------------------------------------------------------------ prefill
+
+// Workspace of exl3_moe_prefill: the alignment tables of ws_layout (items of <= 256 positions), then rotated gate/up
+// rows [2][P][H] fp16, the down projection's activation rows [P][I] fp16 and the weighted rows [P][H] fp32.
+struct PrefillLayout {
+    WsLayout t;
+    size_t a_gu, a_dn, ybuf, total;
+};
+constexpr int kPrefillItemRows = 256;
+inline PrefillLayout prefill_layout(int M, int topk, int E, int H, int I, int shared) {
+    PrefillLayout L;
+    L.t = ws_layout(M, topk, E, H, I, shared, kPrefillItemRows);
+    size_t o = L.t.xf_gu;
+    L.a_gu = o; o += align_up((size_t)2 * L.t.p_max * H * 2, 256);
+    L.a_dn = o; o += align_up((size_t)L.t.p_max * I * 2, 256);
+    L.ybuf = o; o += (size_t)L.t.p_max * H * 4;
+    L.total = o;
+    return L;
+}
+
 }  // namespace exl3
 
 using namespace exl3;
 
 extern "C" {
+
+size_t exl3_moe_prefill_workspace_size(int M, int topk, int E, int H, int I, int shared) {
+    if (M <= 0 || topk <= 0 || E <= 0 || H <= 0 || I <= 0) return 0;
+    return prefill_layout(M, topk, E, H, I, shared).total;
+}
+
+int exl3_moe_prefill(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w, int topk,
+                     const exl3_expert* experts, int E, int shared, int H, int I, float act_limit, void* out,
+                     int out_dtype, void* workspace, size_t ws_bytes, void* stream) {
+    int rc = moe_check(M, topk, experts, E, H, I, 0, "exl3_moe_prefill");
+    if (rc) return rc;
+    EXL3_REQUIRE(x && ids && w && out, EXL3_ERR_ARG, "exl3_moe_prefill: null pointer");
+    EXL3_REQUIRE(x_dtype == EXL3_F16 || x_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "exl3_moe_prefill: x dtype");
+    EXL3_REQUIRE(out_dtype == EXL3_F16 || out_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED, "exl3_moe_prefill: out dtype");
+    EXL3_REQUIRE(ldx >= H && ldx % 4 == 0 && (reinterpret_cast<uintptr_t>(x) & 7) == 0, EXL3_ERR_ARG,
+                 "exl3_moe_prefill: x rows must be 8-byte aligned (ldx=%d)", ldx);
+    if (M == 0) return EXL3_OK;
+    const PrefillLayout L = prefill_layout(M, topk, E, H, I, shared);
+    EXL3_REQUIRE(workspace && ws_bytes >= L.total && (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+                 EXL3_ERR_WORKSPACE, "exl3_moe_prefill: workspace %zu < %zu bytes (or not 256-byte aligned)",
+                 ws_bytes, L.total);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    rc = launch_align(ids, w, M, topk, E, shared, kPrefillItemRows, ws, L.t, st);
+    if (rc) return rc;
+    TcMoeArgs m = {};
+    m.x = x;
+    m.ldx = ldx;
+    m.x_bf16 = x_dtype == EXL3_BF16;
+    m.H = H;
+    m.I = I;
+    m.P = L.t.p_max;
+    m.max_items = L.t.max_items;
+    m.n_items = reinterpret_cast<const int*>(ws);
+    m.item_expert = reinterpret_cast<const int*>(ws + L.t.item_expert);
+    m.item_start = reinterpret_cast<const int*>(ws + L.t.item_start);
+    m.item_cnt = reinterpret_cast<const int*>(ws + L.t.item_cnt);
+    m.n_pos = reinterpret_cast<const int*>(ws) + 2;
+    m.pair_tok = reinterpret_cast<const int*>(ws + L.t.pair_tok);
+    m.pair_expert = reinterpret_cast<const int*>(ws + L.t.pair_expert);
+    m.pair_w = reinterpret_cast<const float*>(ws + L.t.pair_w);
+    m.experts = reinterpret_cast<const ExpertDesc*>(experts);
+    m.act_limit = act_limit;
+    m.a_gu = reinterpret_cast<__half*>(ws + L.a_gu);
+    m.a_dn = reinterpret_cast<__half*>(ws + L.a_dn);
+    m.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
+    rc = tc_moe_prefill(m, st);
+    if (rc) return rc;
+    const float* ybuf = m.ybuf;
+    const int* pair_of = reinterpret_cast<const int*>(ws + L.t.pair_of);
+    const int* wi = reinterpret_cast<const int*>(ws);
+    const dim3 grid((M * (H / 4) + 255) / 256);
+    cudaError_t e;
+    if (out_dtype == EXL3_F32)
+        e = launch_pdl(k_combine<float>, grid, dim3(256), 0, st, ybuf, pair_of, wi, M, H, topk, shared,
+                       static_cast<float*>(out));
+    else
+        e = launch_pdl(k_combine<__half>, grid, dim3(256), 0, st, ybuf, pair_of, wi, M, H, topk, shared,
+                       static_cast<__half*>(out));
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_moe_prefill: combine launch failed: %s",
+                 cudaGetErrorString(e));
+    return EXL3_OK;
+}
+
 
 int exl3_route(const float* logits, int ld, int R, int E, int kind, int k, const float* bias, const float* res,
                const float* mul, float scale, int renorm, void* ids, int ids64, float* w, void* want,

@@ -46,6 +46,8 @@ _PROTOS = [
     ("exl3_moe_workspace_size", sz, [i32, i32, i32, i32, i32, i32]),
     ("exl3_moe_decode", i32, [vp, i32, i32, i32, vp, vp, i32, vp, i32, i32, i32, i32, f32, vp, i32, vp, sz, i32,
                               vp]),
+    ("exl3_moe_prefill_workspace_size", sz, [i32, i32, i32, i32, i32, i32]),
+    ("exl3_moe_prefill", i32, [vp, i32, i32, i32, vp, vp, i32, vp, i32, i32, i32, i32, f32, vp, i32, vp, sz, vp]),
     ("exl3_moe_align", i32, [vp, vp, i32, i32, i32, i32, i32, vp, sz, vp]),
     ("exl3_moe_prepare", i32, [vp, i32, i32, i32, vp, vp, i32, vp, i32, i32, i32, i32, vp, sz, vp]),
     ("exl3_moe_gateup", i32, [i32, i32, vp, i32, i32, i32, i32, f32, vp, sz, i32, vp]),

@@ -162,6 +162,37 @@ def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, t
     return out
 
 
+def moe_prefill(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, table: ExpertTable,
+                act_limit: float = 0.0, out_dtype=torch.float32, out: torch.Tensor | None = None,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """moe_forward for prefill-sized batches on the tensor cores (C ABI exl3_moe_prefill): the same contract, with
+    pairs grouped into items of <= 256 positions per expert and grouped tcgen05 GEMMs for the projections."""
+    L.require_cuda(x, topk_ids, topk_w)
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.dtype not in (torch.float16, torch.bfloat16):
+        x2 = x2.half()
+    x2 = x2.contiguous()
+    M, H = x2.shape
+    if H != table.H:
+        raise L.Exl3Error(f"moe_prefill: hidden {H} != table hidden {table.H}")
+    ids = topk_ids.reshape(M, -1).to(torch.int32).contiguous()
+    w = topk_w.reshape(M, -1).to(torch.float32).contiguous()
+    k = ids.shape[1]
+    if out is None:
+        out = torch.empty((M, H), dtype=out_dtype, device=x2.device)
+    if M == 0:
+        return out
+    shared = int(table.shared is not None)
+    lib = L.lib()
+    need = lib.exl3_moe_prefill_workspace_size(M, k, table.E, H, table.I, shared)
+    ws = workspace if workspace is not None else L.workspace(x2.device, need, "moe_prefill")
+    rc = lib.exl3_moe_prefill(x2.data_ptr(), L.dtype_code(x2.dtype), x2.stride(0), M, ids.data_ptr(), w.data_ptr(),
+                              k, table.table.data_ptr(), table.E, shared, H, table.I, float(act_limit),
+                              out.data_ptr(), L.dtype_code(out.dtype), ws.data_ptr(), ws.numel(), L.stream_of(x2))
+    L.check(rc, "moe_prefill")
+    return out
+
+
 def moe_align(topk_ids: torch.Tensor, topk_w: torch.Tensor, E: int, shared: bool = False, chunk: int = 8):
     """Alignment tables as tensors (the reference's debug moe_align, glm/xpu/csrc/exl3_moe.n128.sycl:1442-1450):
     dict of n_items, n_valid, item_expert/start/cnt, pair_tok, pair_expert, pair_of, pair_w, pair_src."""

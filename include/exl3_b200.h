@@ -177,6 +177,20 @@ EXL3_API int exl3_moe_down(int M, int topk, const exl3_expert* experts, int E, i
 EXL3_API int exl3_moe_combine(int M, int topk, int E, int shared, int H, int I, void* out, int out_dtype,
                               void* workspace, size_t ws_bytes, void* stream);
 
+/* ---- MoE prefill (tcgen05) ----
+ * The routed MoE layer for prefill-sized batches, same contract as exl3_moe_decode (out = slot-order sum of the
+ * picks' expert outputs + shared expert). Pairs are grouped per expert into items of <= 256 positions; each
+ * projection is a grouped tcgen05 GEMM (trellis decoded to bit-exact fp16 into shared memory, fp32 accumulation in
+ * tensor memory): gate|up with SiLU * clamp and the down input's rotation fused in its epilogue, down with the
+ * routing weight; then the fixed-order combine. workspace >= exl3_moe_prefill_workspace_size(...), 256-byte aligned.
+ * Replaces the reference's MoE prefill (GateUpDpasKernel / DownDpasKernel / moe_prefill,
+ * glm/xpu/csrc/exl3_moe.n128.sycl:422-690,868-916) and dsv_xpu moe_prefill_grouped
+ * (dsv41/xpu/dsv_xpu/moe.py:1383-1448). */
+EXL3_API size_t exl3_moe_prefill_workspace_size(int M, int topk, int E, int H, int I, int shared);
+EXL3_API int exl3_moe_prefill(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w,
+                              int topk, const exl3_expert* experts, int E, int shared, int H, int I, float act_limit,
+                              void* out, int out_dtype, void* workspace, size_t ws_bytes, void* stream);
+
 /* Alignment step on its own (debug / reuse): writes into the workspace the item table and the pair permutation, in
  * the layout documented in moe.cu. Replaces moe_align (glm/xpu/csrc/exl3_moe.n128.sycl:1442-1450). */
 EXL3_API int exl3_moe_align(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
