@@ -2,14 +2,14 @@
 // linear (any M) and the grouped MoE expert projections (rows grouped per expert by the alignment step).
 //
 // Weights are decoded from the packed trellis (exl3_pack / exl3_pack_gateup layouts) to the reference's fp16 values
-// bit for bit, written into shared memory in the canonical K-major 128-byte-swizzled layout and multiplied with
+// bit for bit, written into shared memory in the canonical K-major swizzled layout and multiplied with
 // tcgen05.mma kind::f16, fp32 accumulation in tensor memory. One CTA computes a 256-row x 256-column tile over the
-// whole k range, in k-chunks of 64:
-//   warp 0        TMA: the chunk's rotated activation tile(s) [256 rows][64] fp16 (one per matrix), 128-byte swizzle;
+// whole k range, in k-chunks of TC_BK (32: 64-byte rows with the 64-byte swizzle, so that the rings are deep):
+//   warp 0        TMA: the chunk's rotated activation tile(s) [256 rows][TC_BK] fp16 (one per matrix), swizzled;
 //   warp 1        allocates the 512 TMEM columns, then one elected lane issues the chunk's MMAs (M 128, K 16) and
 //                 commits each stage's release and, after the last chunk, the accumulators;
 //   warp 2        bulk-copies the chunk's trellis tiles into a ring;
-//   warps 3..18   decode the trellis tiles into the B stage [256 columns][64]; after the main loop they run the
+//   warps 3..18   decode the trellis tiles into the B stage [256 columns][TC_BK]; after the main loop they run the
 //                 epilogue: TMEM -> registers -> shared memory (XOR-swizzled rows) -> output Hadamard per 128-column
 //                 block with warp shuffles -> the epilogue of the projection.
 // Epilogues: linear (y = H(acc) * svh), MoE gate|up (the tile's 256 columns are the fused gate and up blocks of one
@@ -25,27 +25,38 @@
 
 namespace exl3 {
 
-constexpr int TC_BM = 256, TC_BN = 256, TC_BK = 64;
+#ifndef EXL3_TC_BK
+#define EXL3_TC_BK 64
+#endif
+// k-chunk of 64 (128-byte rows, 128-byte swizzle) or 32 (64-byte rows, 64-byte swizzle)
+constexpr int TC_BM = 256, TC_BN = 256, TC_BK = EXL3_TC_BK;
+constexpr int TC_ROWB = TC_BK * 2;                            // bytes of one tile row
+constexpr int TC_ATOM = 8 * TC_ROWB;                          // swizzle atom: 8 rows
 constexpr int TC_DEC_WARPS = 16;
 constexpr int TC_WARPS = 3 + TC_DEC_WARPS;
 constexpr int TC_THREADS = TC_WARPS * 32;
-constexpr int TC_TILE_BYTES = TC_BM * TC_BK * 2;              // one activation tile (and the B stage): 32 KB
-constexpr int TC_A_REGION = 128 * 1024;                       // activation ring: 4 x 32 KB or 2 x 64 KB
-constexpr int TC_B_STAGES = 2;
+constexpr int TC_TILE_BYTES = TC_BM * TC_BK * 2;              // one activation tile (and the B stage)
+constexpr int TC_AB_REGION = 192 * 1024;                      // activation ring + B ring
 constexpr int TC_T_RING = 32 * 1024;                          // trellis ring bytes
 constexpr int TC_MAX_TSTAGES = 8;
-constexpr int TC_TPW = 4;                                     // trellis tiles per decoder warp per chunk (64 / 16)
+constexpr int TC_TR = TC_BK / 16;                             // tile-rows per chunk
+constexpr int TC_TPW = 2 * TC_TR * 8 / TC_DEC_WARPS;          // trellis tiles per decoder warp per chunk
+constexpr int TC_MAX_ASTAGES = 8, TC_MAX_BSTAGES = 8;
 
 __host__ __device__ constexpr int tc_nmat(int epi) { return epi == TC_GATEUP ? 2 : 1; }
-__host__ __device__ constexpr int tc_a_stages(int epi) { return TC_A_REGION / (tc_nmat(epi) * TC_TILE_BYTES); }
+// ring depths: gate|up (two activation tiles per stage) 2 + 2 stages, linear / down 3 + 3; the 192 KB of both
+// rings (free once the accumulators are complete) also hold the epilogue's 128 KB staging
+__host__ __device__ constexpr int tc_b_stages(int epi) { return epi == TC_GATEUP ? 2 : 3; }
+__host__ __device__ constexpr int tc_a_stages(int epi) {
+    return (TC_AB_REGION - tc_b_stages(epi) * TC_TILE_BYTES) / (tc_nmat(epi) * TC_TILE_BYTES);
+}
 
 struct TcSmem {
-    static constexpr int a0 = 0;                               // activation ring (1024-aligned)
-    static constexpr int b0 = TC_A_REGION;                     // B[2]
-    static constexpr int t0 = b0 + TC_B_STAGES * TC_TILE_BYTES;
+    static constexpr int a0 = 0;                               // activation ring then B ring (1024-aligned)
+    static constexpr int t0 = TC_AB_REGION;
     static constexpr int bars = t0 + TC_T_RING;
-    // a_full[4], a_empty[4], b_full[2], b_empty[2], t_full[8], t_empty[8], acc_full
-    static constexpr int n_bars = 4 + 4 + 2 + 2 + 2 * TC_MAX_TSTAGES + 1;
+    // a_full[], a_empty[], b_full[], b_empty[], t_full[8], t_empty[8], acc_full
+    static constexpr int n_bars = 2 * TC_MAX_ASTAGES + 2 * TC_MAX_BSTAGES + 2 * TC_MAX_TSTAGES + 1;
     static constexpr int tmem_slot = bars + n_bars * 8;
     static constexpr int total = tmem_slot + 16 + 1024;        // + slack for 1024-byte alignment of the base
 };
@@ -86,19 +97,22 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t r[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Shared-memory matrix descriptor: canonical K-major layout with the 128-byte swizzle (8-row atoms of 128 bytes,
-// atoms 1024 bytes apart), sm100 descriptor version 1.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
-           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+// Shared-memory matrix descriptor: canonical K-major layout with the 128-byte (TC_BK 64) or 64-byte (TC_BK 32)
+// swizzle (8-row atoms, TC_ATOM bytes apart), sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t sw_desc(uint32_t saddr) {
+    constexpr uint64_t layout = TC_BK == 64 ? 2 : 4;          // SWIZZLE_128B : SWIZZLE_64B
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(TC_ATOM >> 4) << 32) |
+           ((uint64_t)1 << 46) | (layout << 61);
 }
 // Instruction descriptor, kind::f16: fp16 A and B (K-major), fp32 D, M x N.
 __host__ __device__ constexpr uint32_t tc_idesc_f16(int M, int N) {
     return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-// Byte offset of element (row, k) of a [rows][64] fp16 tile in the 128-byte-swizzled K-major layout.
-__device__ __forceinline__ uint32_t sw128_off(int row, int k) {
-    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((((k >> 3) ^ (row & 7))) << 4) + (k & 7) * 2);
+// Byte offset of element (row, k) of a [rows][TC_BK] fp16 tile in the swizzled K-major layout: 16-byte chunk c of
+// a row lands at c ^ (row & 7) (128-byte swizzle) or c ^ ((row >> 1) & 3) (64-byte swizzle).
+__device__ __forceinline__ uint32_t sw_off(int row, int k) {
+    const int x = TC_BK == 64 ? (row & 7) : ((row >> 1) & 3);
+    return (uint32_t)((row >> 3) * TC_ATOM + (row & 7) * TC_ROWB + ((((k >> 3) ^ x)) << 4) + (k & 7) * 2);
 }
 
 struct TcArgs {
@@ -124,11 +138,11 @@ struct TcArgs {
 
 // ------------------------------------------------------------------------------------------------ decode
 
-// Per-thread constant addressing of the decode: for each of the warp's 4 tiles of a chunk, the tile's byte offset in
+// Per-thread constant addressing of the decode: for each of the warp's TC_TPW tiles of a chunk, the tile's byte offset in
 // a trellis stage and the four swizzled byte offsets in a B stage that receive the lane's fragment registers
 // {n, k..k+1}, {n + 8, k..}, {n, k + 8..}, {n + 8, k + 8..} (n = tile column + g, k = tile row + 2q).
-// Linear / down: a stage holds two column blocks [cb][4 tile-rows][8 tiles][32K bytes] of one matrix; warp dw takes
-// tiles 4dw .. 4dw+3 of the 64. Gate|up: a stage holds 4 tile-rows of the fused block, each [8 gate tiles (Kg) |
+// Linear / down: a stage holds two column blocks [cb][TC_TR tile-rows][8 tiles][32K bytes] of one matrix; warp dw
+// takes tiles TC_TPW dw ... Gate|up: a stage holds TC_TR tile-rows of the fused block, each [8 gate tiles (Kg) |
 // 8 up tiles (Ku)]; warps 0-7 take the gate tiles, 8-15 the up tiles, and B rows 0-127 / 128-255 are gate / up.
 struct TcDecodeMap {
     uint32_t tile[TC_TPW];
@@ -142,7 +156,7 @@ __device__ __forceinline__ TcDecodeMap tc_decode_map(int epi, int dw, int lane, 
     for (int j = 0; j < TC_TPW; ++j) {
         int n0, k0;
         if (epi == TC_GATEUP) {
-            const int mat = dw >> 3, idx = (dw & 7) * TC_TPW + j;    // 0..31 within the matrix
+            const int mat = dw >> 3, idx = (dw & 7) * TC_TPW + j;    // 0 .. 8 TC_TR - 1 within the matrix
             const int tr = idx >> 3, t = idx & 7;
             const int row_stride = 8 * 32 * Kg + 8 * 32 * Ku;
             mp.tile[j] = (uint32_t)(tr * row_stride + (mat ? 8 * 32 * Kg : 0) + t * 32 * (mat ? Ku : Kg));
@@ -150,15 +164,15 @@ __device__ __forceinline__ TcDecodeMap tc_decode_map(int epi, int dw, int lane, 
             k0 = tr * 16 + 2 * q;
         } else {
             const int ti = dw * TC_TPW + j;
-            const int cb = ti >> 5, tr = (ti >> 3) & 3, t = ti & 7;
-            mp.tile[j] = (uint32_t)(((cb * 4 + tr) * 8 + t) * 32 * Ku);
+            const int cb = ti / (8 * TC_TR), tr = (ti >> 3) % TC_TR, t = ti & 7;
+            mp.tile[j] = (uint32_t)(((cb * TC_TR + tr) * 8 + t) * 32 * Ku);
             n0 = cb * 128 + t * 16 + g;
             k0 = tr * 16 + 2 * q;
         }
-        mp.st[j][0] = sw128_off(n0, k0);
-        mp.st[j][1] = sw128_off(n0 + 8, k0);
-        mp.st[j][2] = sw128_off(n0, k0 + 8);
-        mp.st[j][3] = sw128_off(n0 + 8, k0 + 8);
+        mp.st[j][0] = sw_off(n0, k0);
+        mp.st[j][1] = sw_off(n0 + 8, k0);
+        mp.st[j][2] = sw_off(n0, k0 + 8);
+        mp.st[j][3] = sw_off(n0 + 8, k0 + 8);
     }
     return mp;
 }
@@ -176,17 +190,16 @@ __device__ __forceinline__ void tc_decode_chunk(const uint8_t* tst, uint8_t* bst
 }
 
 template <int K>
-__device__ void tc_decoder_loop(const TcDecodeMap& mp, uint8_t* smem, int t_stages, int t_stage_bytes,
-                                uint64_t* t_full, uint64_t* t_empty, uint64_t* b_full, uint64_t* b_empty, int nk,
-                                int lane, bool& to) {
+__device__ void tc_decoder_loop(const TcDecodeMap& mp, uint8_t* smem, uint8_t* bring, int bst, int t_stages,
+                                int t_stage_bytes, uint64_t* t_full, uint64_t* t_empty, uint64_t* b_full,
+                                uint64_t* b_empty, int nk, int lane, bool& to) {
     const LaneWords lw = lane_words<K>(lane);
     for (int kc = 0; kc < nk; ++kc) {
-        const int ts = kc % t_stages, s = kc % TC_B_STAGES;
+        const int ts = kc % t_stages, s = kc % bst;
         if (!to && !mbar_wait(&t_full[ts], (kc / t_stages) & 1)) to = true;
-        if (kc >= TC_B_STAGES && !to && !mbar_wait(&b_empty[s], ((kc / TC_B_STAGES) - 1) & 1)) to = true;
+        if (kc >= bst && !to && !mbar_wait(&b_empty[s], ((kc / bst) - 1) & 1)) to = true;
         if (!to)
-            tc_decode_chunk<K>(smem + TcSmem::t0 + (size_t)ts * t_stage_bytes, smem + TcSmem::b0 + s * TC_TILE_BYTES,
-                               mp, lw);
+            tc_decode_chunk<K>(smem + TcSmem::t0 + (size_t)ts * t_stage_bytes, bring + s * TC_TILE_BYTES, mp, lw);
         fence_proxy_async();                                  // generic-proxy writes -> the tensor core's reads
         __syncwarp();
         if (lane == 0) {
@@ -196,11 +209,12 @@ __device__ void tc_decoder_loop(const TcDecodeMap& mp, uint8_t* smem, int t_stag
     }
 }
 
-__device__ void tc_decoder_dispatch(int K, const TcDecodeMap& mp, uint8_t* smem, int t_stages, int t_stage_bytes,
-                                    uint64_t* t_full, uint64_t* t_empty, uint64_t* b_full, uint64_t* b_empty, int nk,
-                                    int lane, bool& to) {
-#define EXL3_TC_DEC(KK) \
-    tc_decoder_loop<KK>(mp, smem, t_stages, t_stage_bytes, t_full, t_empty, b_full, b_empty, nk, lane, to)
+__device__ void tc_decoder_dispatch(int K, const TcDecodeMap& mp, uint8_t* smem, uint8_t* bring, int bst,
+                                    int t_stages, int t_stage_bytes, uint64_t* t_full, uint64_t* t_empty,
+                                    uint64_t* b_full, uint64_t* b_empty, int nk, int lane, bool& to) {
+#define EXL3_TC_DEC(KK)                                                                                         \
+    tc_decoder_loop<KK>(mp, smem, bring, bst, t_stages, t_stage_bytes, t_full, t_empty, b_full, b_empty, nk, lane, \
+                        to)
     switch (K) {
         case 1: EXL3_TC_DEC(1); break;
         case 2: EXL3_TC_DEC(2); break;
@@ -222,7 +236,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
                                                            const TcArgs p) {
     constexpr int NMAT = tc_nmat(EPI);
     constexpr int AST = tc_a_stages(EPI);
+    constexpr int BST = tc_b_stages(EPI);
     constexpr int A_STAGE = NMAT * TC_TILE_BYTES;
+    static_assert(AST <= TC_MAX_ASTAGES && BST <= TC_MAX_BSTAGES && AST * A_STAGE + BST * TC_TILE_BYTES <= TC_AB_REGION,
+                  "rings");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -268,16 +285,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
     }
     const int nk = p.k / TC_BK;
     // trellis stage: linear / down two column blocks x 4 tile-rows x 8 tiles; gate|up 4 fused tile-rows
-    const int t_stage_bytes = EPI == TC_GATEUP ? 4 * (8 * 32 * Kg + 8 * 32 * Ku) : 2 * 4 * 8 * 32 * Ku;
+    const int t_stage_bytes = EPI == TC_GATEUP ? TC_TR * (8 * 32 * Kg + 8 * 32 * Ku) : 2 * TC_TR * 8 * 32 * Ku;
     int t_stages = TC_T_RING / t_stage_bytes;
     if (t_stages > TC_MAX_TSTAGES) t_stages = TC_MAX_TSTAGES;
 
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::bars);
     uint64_t* a_full = bars;
-    uint64_t* a_empty = a_full + 4;
-    uint64_t* b_full = a_empty + 4;
-    uint64_t* b_empty = b_full + TC_B_STAGES;
-    uint64_t* t_full = b_empty + TC_B_STAGES;
+    uint64_t* a_empty = a_full + TC_MAX_ASTAGES;
+    uint64_t* b_full = a_empty + TC_MAX_ASTAGES;
+    uint64_t* b_empty = b_full + TC_MAX_BSTAGES;
+    uint64_t* t_full = b_empty + TC_MAX_BSTAGES;
+    uint8_t* bring = smem + TcSmem::a0 + AST * A_STAGE;           // B ring after the activation ring
     uint64_t* t_empty = t_full + TC_MAX_TSTAGES;
     uint64_t* acc_full = t_empty + TC_MAX_TSTAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::tmem_slot);
@@ -287,7 +305,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
             mbar_init(&a_full[s], 1);
             mbar_init(&a_empty[s], 1);
         }
-        for (int s = 0; s < TC_B_STAGES; ++s) {
+        for (int s = 0; s < BST; ++s) {
             mbar_init(&b_full[s], TC_DEC_WARPS);
             mbar_init(&b_empty[s], 1);
         }
@@ -313,7 +331,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         // ---------------- activation tiles (TMA) ----------------
         pdl_wait();                                           // the rotated activations come from an earlier kernel
         if (lane == 0) {
-            int last_s[4] = {-1, -1, -1, -1};
+            int last_s[TC_MAX_ASTAGES];
+            for (int s = 0; s < TC_MAX_ASTAGES; ++s) last_s[s] = -1;
             for (int kc = 0; kc < nk && !to; ++kc) {
                 const int s = kc % AST;
                 if (kc >= AST && !mbar_wait(&a_empty[s], ((kc / AST) - 1) & 1)) { to = true; break; }
@@ -330,13 +349,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         // ---------------- MMA issue (one lane) ----------------
         if (lane == 0) {
             for (int kc = 0; kc < nk; ++kc) {
-                const int sa = kc % AST, sb = kc % TC_B_STAGES;
+                const int sa = kc % AST, sb = kc % BST;
                 if (!to && !mbar_wait(&a_full[sa], (kc / AST) & 1)) to = true;
-                if (!to && !mbar_wait(&b_full[sb], (kc / TC_B_STAGES) & 1)) to = true;
+                if (!to && !mbar_wait(&b_full[sb], (kc / BST) & 1)) to = true;
                 tc_fence_after();
                 if (!to) {
                     const uint32_t a_base = smem_u32(smem + TcSmem::a0 + sa * A_STAGE);
-                    const uint32_t b_base = smem_u32(smem + TcSmem::b0 + sb * TC_TILE_BYTES);
+                    const uint32_t b_base = smem_u32(bring + sb * TC_TILE_BYTES);
 #pragma unroll
                     for (int kk = 0; kk < TC_BK / 16; ++kk) {
                         const uint32_t acc = (kc | kk) != 0;
@@ -348,16 +367,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
 #pragma unroll
                                 for (int j = 0; j < 2; ++j)
                                     tc_mma_f16(tmem + (2 * mat + j) * 128,
-                                               sw128_desc(a_base + mat * TC_TILE_BYTES + j * (TC_TILE_BYTES / 2) +
-                                                          kk * 32),
-                                               sw128_desc(b_base + mat * (TC_TILE_BYTES / 2) + kk * 32),
+                                               sw_desc(a_base + mat * TC_TILE_BYTES + j * (TC_TILE_BYTES / 2) +
+                                                       kk * 32),
+                                               sw_desc(b_base + mat * (TC_TILE_BYTES / 2) + kk * 32),
                                                tc_idesc_f16(128, 128), acc);
                         } else {
 #pragma unroll
                             for (int j = 0; j < 2; ++j)
-                                tc_mma_f16(tmem + j * TC_BN,
-                                           sw128_desc(a_base + j * (TC_TILE_BYTES / 2) + kk * 32),
-                                           sw128_desc(b_base + kk * 32), tc_idesc_f16(128, TC_BN), acc);
+                                tc_mma_f16(tmem + j * TC_BN, sw_desc(a_base + j * (TC_TILE_BYTES / 2) + kk * 32),
+                                           sw_desc(b_base + kk * 32), tc_idesc_f16(128, TC_BN), acc);
                         }
                     }
                 }
@@ -391,14 +409,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         const int dw = warp - 3;
         const TcDecodeMap mp = tc_decode_map(EPI, dw, lane, Kg, Ku);
         const int Kw = (EPI == TC_GATEUP && dw < 8) ? Kg : Ku;
-        tc_decoder_dispatch(Kw, mp, smem, t_stages, t_stage_bytes, t_full, t_empty, b_full, b_empty, nk, lane, to);
+        tc_decoder_dispatch(Kw, mp, smem, bring, BST, t_stages, t_stage_bytes, t_full, t_empty, b_full, b_empty, nk,
+                            lane, to);
 
         pdl_wait();                                           // outputs may be in use by an earlier kernel until here
         if (!to && !mbar_wait(acc_full, 0)) to = true;
         tc_fence_after();
         // the four 128 x 128 accumulator blocks: block bi at TMEM column 128 bi. Linear / down: bi = 2 j + b
         // (row half j, column block b); gate|up: bi = 2 mat + j. The four warps of a TMEM lane quadrant each load
-        // one block; staging [2][128 rows][128 cols] fp32 in the activation ring (free after the main loop), columns
+        // one block; staging [2][128 rows][128 cols] fp32 in the activation + B rings (free after the main loop), columns
         // XOR-swizzled by the row. Pass 0: blocks of row half 0, pass 1: row half 1.
         const int quad = warp & 3, bi = dw >> 2;              // warps 3..18: quad covers 0..3 four times
         const int bj = EPI == TC_GATEUP ? (bi & 1) : (bi >> 1);   // row half of block bi
@@ -578,7 +597,8 @@ using PFN_encode_tiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint3
                                       const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// Tensor map of a row-major [rows][cols] fp16 matrix: boxes of 64 columns x 256 rows, 128-byte swizzle, zero fill.
+// Tensor map of a row-major [rows][cols] fp16 matrix: boxes of TC_BK columns x 256 rows, swizzled as the MMA
+// descriptors expect, zero fill.
 static int make_row_map(CUtensorMap* map, const __half* base, long rows, int cols, const char* what) {
     static PFN_encode_tiled encode = nullptr;
     if (!encode) {
@@ -594,7 +614,8 @@ static int make_row_map(CUtensorMap* map, const __half* base, long rows, int col
     const cuuint32_t box[2] = {TC_BK, TC_BM};
     const cuuint32_t estr[2] = {1, 1};
     CUresult cr = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         TC_BK == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     EXL3_REQUIRE(cr == CUDA_SUCCESS, EXL3_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)cr);
     return EXL3_OK;

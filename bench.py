@@ -37,6 +37,10 @@ WORKLOADS = {
     # BASELINE config 3 (one GLM-like layer, repeated 8 times so that a step's weights exceed L2)
     "glm_decode": dict(H=6144, E=160, I=1536, topk=8, Ks=(2, 3), layers=8, router="sigmoid", batch=1,
                        act_limit=10.0, shared_K=4, res_frac=0.25, scale=2.5),
+    # BASELINE config 5 (DeepSeek-V4-like MoE prefill, one layer per step): 8192 tokens, K in {1, 2} per projection
+    # with P(K = 2) = 0.62 (1.62 bits average), shared expert K = 2, sqrt-softplus router, bf16 activations
+    "dsv4_prefill": dict(H=7168, E=256, I=2048, topk=8, Ks=(1, 2), p_k2=0.62, layers=1, router="sqrt_softplus",
+                         batch=8192, act_limit=10.0, shared_K=2, res_frac=0.0, scale=2.5, prefill=True),
 }
 METRIC = "MoE-layer decode tok/s + compressed-weight HBM GB/s (% of peak)"
 
@@ -235,6 +239,79 @@ def build_layer(cfg, E_local, e_base, gen, dev):
             mats.append(moe.Exl3Matrix(tr, s1, s2, K))
         shared = moe.Expert(*mats)
     return moe.ExpertTable(experts, shared)
+
+
+def run_prefill(args, cfg):
+    """One MoE prefill layer per step (route + exl3_moe_prefill) on 1 GPU, timed with CUDA events over K steps.
+    roofline: tensor-bound; achieved = the layer's algorithmic flops (2 tokens topk 3 H I + shared 2 tokens 3 H I)
+    / the step time (router, alignment, rotations and combine included)."""
+    import numpy as np
+    import torch
+
+    from exl3_b200 import _lib as L
+    from exl3_b200 import moe, ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    H, E, I, topk, T = cfg["H"], cfg["E"], cfg["I"], cfg["topk"], cfg["batch"]
+    gen = torch.Generator(device=dev).manual_seed(11)
+    rng = np.random.default_rng(11)
+
+    def mat(k, n, K):
+        tr = torch.randint(-32768, 32767, (k // 16, n // 16, 16 * K), dtype=torch.int16, device=dev, generator=gen)
+        s1 = (torch.randint(0, 2, (k,), device=dev, generator=gen) * 2 - 1).half()
+        s2 = (torch.randint(0, 2, (n,), device=dev, generator=gen) * 2 - 1).half()
+        return moe.Exl3Matrix(tr, s1, s2, K)
+
+    experts = []
+    for _ in range(E):
+        Ks = [2 if rng.random() < cfg["p_k2"] else 1 for _ in range(3)]
+        experts.append(moe.Expert(mat(H, I, Ks[0]), mat(H, I, Ks[1]), mat(I, H, Ks[2])))
+    shared = moe.Expert(mat(H, I, cfg["shared_K"]), mat(H, I, cfg["shared_K"]), mat(I, H, cfg["shared_K"]))
+    table = moe.ExpertTable(experts, shared)
+    del experts, shared
+    x = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16)
+    logits = torch.randn(T, E, device=dev, generator=gen)
+    bias = torch.randn(E, device=dev, generator=gen) * 0.1
+    out = torch.empty(T, H, device=dev, dtype=torch.float32)
+    need = L.lib().exl3_moe_prefill_workspace_size(T, topk, E, H, I, 1)
+    ws = torch.empty(need, dtype=torch.uint8, device=dev)
+
+    def step():
+        ids, w, _ = ops.route(logits, L.ROUTE_SQRT_SOFTPLUS, topk, bias=bias, scale=cfg["scale"])
+        moe.moe_prefill(x, ids, w, table, cfg["act_limit"], out=out, workspace=ws)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        t1.record()
+        torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / args.steps
+    assert torch.isfinite(out).all(), "non-finite MoE output"
+    assert L.lib().exl3_device_status(0) == 0
+    flops = 2.0 * T * topk * 3 * H * I + 2.0 * T * 3 * H * I
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+        peak = float(json.load(f)["bf16_tflops"])
+    ach = flops / (ms * 1e-3) / 1e12
+    line = {
+        "metric": "MoE-layer prefill tok/s (tcgen05 grouped GEMM, tensor-pipe fraction)", "value": round(T / (ms * 1e-3), 1),
+        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded random trellis, +-1 signs, N(0,1) bf16 activations)",
+        "config": {"workload": args.workload, "tokens": T, "hidden": H, "experts": E, "intermediate": I, "topk": topk,
+                   "K": "1/2 (P(2)=0.62)", "shared_K": cfg["shared_K"], "router": cfg["router"],
+                   "l2": "inputs larger than L2 (2.3 GB of expert weights, 117 MB of activations per step)"},
+        "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(ach / peak, 4), "peak_kind": "measured bf16 burst", "traffic": None,
+                     "flops_per_step": flops},
+        "cpu_baseline": None, "gpu_launches": 6 * args.steps, "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
 
 
 def run_ours(args, cfg):
@@ -462,6 +539,8 @@ def main():
         cfg["layers"] = args.layers
     if args.impl == "reference":
         run_reference(args, cfg)
+    elif cfg.get("prefill"):
+        run_prefill(args, cfg)
     else:
         run_ours(args, cfg)
 
