@@ -1,21 +1,39 @@
-// EXL3 linears for prefill-sized batches on the 5th-generation tensor cores (tcgen05, TMEM accumulators): the dense
-// linear (any M) and the grouped MoE expert projections (rows grouped per expert by the alignment step).
+// EXL3 linears for prefill-sized batches on the 5th-generation tensor cores: the dense linear (any M) and the grouped
+// MoE expert projections (rows grouped per expert by the alignment step).
 //
-// Weights are decoded from the packed trellis (exl3_pack / exl3_pack_gateup layouts) to the reference's fp16 values
-// bit for bit, written into shared memory in the canonical K-major swizzled layout and multiplied with
-// tcgen05.mma kind::f16, fp32 accumulation in tensor memory. One CTA computes a 256-row x 256-column tile over the
-// whole k range, in k-chunks of TC_BK (32: 64-byte rows with the 64-byte swizzle, so that the rings are deep):
-//   warp 0        TMA: the chunk's rotated activation tile(s) [256 rows][TC_BK] fp16 (one per matrix), swizzled;
-//   warp 1        allocates the 512 TMEM columns, then one elected lane issues the chunk's MMAs (M 128, K 16) and
-//                 commits each stage's release and, after the last chunk, the accumulators;
-//   warp 2        bulk-copies the chunk's trellis tiles into a ring;
-//   warps 3..18   decode the trellis tiles into the B stage [256 columns][TC_BK]; after the main loop they run the
-//                 epilogue: TMEM -> registers -> shared memory (XOR-swizzled rows) -> output Hadamard per 128-column
-//                 block with warp shuffles -> the epilogue of the projection.
-// Epilogues: linear (y = H(acc) * svh), MoE gate|up (the tile's 256 columns are the fused gate and up blocks of one
-// column block; two activation matrices, four 128 x 128 accumulators; SiLU * clamp, then the down input's
-// rotation, stored as the down projection's activation rows), MoE down (routing weight x H(acc) * svh, fp32 rows).
-// All waits are bounded (EXL3_ERR_TIMEOUT in the device status word). No multicast, no clusters.
+// Shape of the contraction. The decoded weights are the MMA's A operand and live in TENSOR MEMORY; the rotated
+// activation rows are the B operand in shared memory; the accumulator is D[feature][row] in tensor memory. A pair of
+// CTAs (a 2-CTA cluster) runs one tile of 256 output features x up to 320 activation rows with
+// tcgen05.mma.cta_group::2: CTA r decodes features [128 r, 128 r + 128) of the pair into its own TMEM lanes; the
+// leader (rank 0) issues the MMAs for both. Per 16-deep k step the tile is two MMAs on the same decoded weights:
+// rows 0..255 (N 256: CTA r supplies rows [128 r, 128 r + 128)) and, when the tile has more than 256 rows, rows
+// 256..319 (N 64: CTA r supplies rows [256 + 32 r, 256 + 32 r + 32)). Each decoded weight thus serves up to 320
+// rows, and the decoded weights never pass through shared memory: decoder warps write their fragments straight
+// from registers with tcgen05.st; shared memory only carries the activations (TMA write + MMA read).
+//
+//   warp 0        TMA: the CTA's activation rows of the k-chunk ([160 rows][64 k] fp16 sub-tiles, 128-byte
+//                 swizzle), completion counted on the leader's barrier (cp.async.bulk.tensor .cta_group::2);
+//   warp 1        allocates the 512 TMEM columns of both CTAs; on the leader one lane issues the chunk's MMAs
+//                 (M 256, K 16, A from TMEM) and commits each stage's release and, after the last chunk, the
+//                 accumulators to both CTAs (tcgen05.commit multicast);
+//   warp 2        bulk-copies the CTA's trellis tiles of the chunk into a ring;
+//   warps 3..18   decode the trellis tiles (bit-exact fp16, register fragments) into the TMEM weight stage; after the
+//                 main loop they run the epilogue, 128 rows at a time: TMEM -> shared memory [row][feature] fp32 ->
+//                 output Hadamard per 128-feature block with warp shuffles -> the projection's epilogue.
+// TMEM of each CTA: columns 0..319 the accumulators (lane = feature, column = activation row of the tile),
+// 320..511 the weight ring (a k-chunk of 128 takes 64 columns: lane = feature, column c of a 16-deep step holds
+// two k values).
+//
+// k order inside the contraction. tcgen05.st.16x256b stores a decoded fragment's registers {pair q, pair q + 4} of a
+// 16-element k group into columns {2q, 2q + 1}; the MMA reads column c as k pair c. So every activation row is
+// stored with the same fixed permutation inside each 16-element group: k pair p goes to pair slot
+// (p < 4 ? 2p : 2p - 7). The rotation kernels below write rows in that order; the products are unchanged.
+//
+// Epilogues: linear (y = H(acc) * svh with the reference's fp16 roundings for fp16 y), MoE gate and up (the same
+// fp16 output into the [2][positions][I] gate/up buffer; gate and up are separate pair tiles because the two
+// matrices rotate the input with different signs), MoE down (routing weight x H(acc) * svh, fp32 rows). The
+// activation between gate|up and down (SiLU * clamp, then the down input's rotation) is its own small kernel.
+// All waits are bounded (EXL3_ERR_TIMEOUT in the device status word). No TMA multicast.
 //
 // Reference semantics: exl3_linear / ReconstructKernel + GEMM for M > 128 (glm/xpu/csrc/exl3_ops.sycl:539-555,
 // 651-757; glm/docs/ext-op-inventory.md:597-612), the MoE prefill GateUpDpasKernel / DownDpasKernel
@@ -25,65 +43,100 @@
 
 namespace exl3 {
 
-#ifndef EXL3_TC_BK
-#define EXL3_TC_BK 64
+#ifndef EXL3_TS_KS
+#define EXL3_TS_KS 2
 #endif
-// k-chunk of 64 (128-byte rows, 128-byte swizzle) or 32 (64-byte rows, 64-byte swizzle)
-constexpr int TC_BM = 256, TC_BN = 256, TC_BK = EXL3_TC_BK;
-constexpr int TC_ROWB = TC_BK * 2;                            // bytes of one tile row
-constexpr int TC_ATOM = 8 * TC_ROWB;                          // swizzle atom: 8 rows
-constexpr int TC_DEC_WARPS = 16;
-constexpr int TC_WARPS = 3 + TC_DEC_WARPS;
-constexpr int TC_THREADS = TC_WARPS * 32;
-constexpr int TC_TILE_BYTES = TC_BM * TC_BK * 2;              // one activation tile (and the B stage)
-constexpr int TC_AB_REGION = 192 * 1024;                      // activation ring + B ring
-constexpr int TC_T_RING = 32 * 1024;                          // trellis ring bytes
-constexpr int TC_MAX_TSTAGES = 8;
-constexpr int TC_TR = TC_BK / 16;                             // tile-rows per chunk
-constexpr int TC_TPW = 2 * TC_TR * 8 / TC_DEC_WARPS;          // trellis tiles per decoder warp per chunk
-constexpr int TC_MAX_ASTAGES = 8, TC_MAX_BSTAGES = 8;
+constexpr int TS_KS = EXL3_TS_KS;                             // 64-deep sub-chunks per k-chunk
+constexpr int TS_BK = 64 * TS_KS;                             // k-chunk
+constexpr int TS_N2 = 64;                                     // N of the second MMA (tile rows 256..319)
+constexpr int TS_TILE_ROWS = 256 + TS_N2;                     // activation rows per pair tile
+static_assert(TS_TILE_ROWS == kTcTileRows, "tile rows shared with the alignment step");
+constexpr int TS_CROWS = 128 + TS_N2 / 2;                     // activation rows per CTA
+constexpr int TS_DEC_WARPS = 16;
+constexpr int TS_WARPS = 3 + TS_DEC_WARPS;
+constexpr int TS_THREADS = TS_WARPS * 32;
+constexpr int TS_SUB = TS_CROWS * 64 * 2;                     // one swizzled [160 rows][64 k] fp16 sub-tile
+constexpr int TS_SUB2 = 128 * 64 * 2;                         // offset of the second MMA's rows in a sub-tile
+constexpr int TS_B_STAGE = TS_KS * TS_SUB;
+constexpr int TS_A_COL0 = 256 + TS_N2;                        // first TMEM column of the weight ring
+constexpr int TS_A_COLS = TS_BK / 2;                          // TMEM columns of one weight stage
+constexpr int TS_STAGES = (512 - TS_A_COL0) / TS_A_COLS;      // weight (and activation) stages
+constexpr int TS_B_RING = TS_STAGES * TS_B_STAGE;             // activation ring (also the epilogue staging)
+constexpr int TS_T_RING = 32 * 1024;                          // trellis ring
+constexpr int TS_MAX_TSTAGES = 8;
+constexpr int TS_TR = TS_BK / 16;                             // tile-rows per chunk
+static_assert(TS_STAGES >= 2 && TS_SUB % 1024 == 0 && TS_SUB2 % 1024 == 0, "ring geometry");
+static_assert(TS_B_RING >= 128 * 128 * 4, "epilogue staging [128 rows][128 features] fp32 fits the ring");
 
-__host__ __device__ constexpr int tc_nmat(int epi) { return epi == TC_GATEUP ? 2 : 1; }
-// ring depths: gate|up (two activation tiles per stage) 2 + 2 stages, linear / down 3 + 3; the 192 KB of both
-// rings (free once the accumulators are complete) also hold the epilogue's 128 KB staging
-__host__ __device__ constexpr int tc_b_stages(int epi) { return epi == TC_GATEUP ? 2 : 3; }
-__host__ __device__ constexpr int tc_a_stages(int epi) {
-    return (TC_AB_REGION - tc_b_stages(epi) * TC_TILE_BYTES) / (tc_nmat(epi) * TC_TILE_BYTES);
-}
-
-struct TcSmem {
-    static constexpr int a0 = 0;                               // activation ring then B ring (1024-aligned)
-    static constexpr int t0 = TC_AB_REGION;
-    static constexpr int bars = t0 + TC_T_RING;
-    // a_full[], a_empty[], b_full[], b_empty[], t_full[8], t_empty[8], acc_full
-    static constexpr int n_bars = 2 * TC_MAX_ASTAGES + 2 * TC_MAX_BSTAGES + 2 * TC_MAX_TSTAGES + 1;
+struct TsSmem {
+    static constexpr int b0 = 0;
+    static constexpr int t0 = TS_B_RING;
+    static constexpr int bars = t0 + TS_T_RING;
+    // b_full[S], a_full[S], empty[S], t_full[8], t_empty[8], acc_full
+    static constexpr int n_bars = 3 * TS_STAGES + 2 * TS_MAX_TSTAGES + 1;
     static constexpr int tmem_slot = bars + n_bars * 8;
     static constexpr int total = tmem_slot + 16 + 1024;        // + slack for 1024-byte alignment of the base
 };
 
-// ---- tcgen05 / TMA wrappers ----
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+// ---- cluster, TMA, tcgen05 wrappers ----
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on a barrier of either CTA of the pair (shared::cluster address). The data it publishes is tensor memory
+// written with tcgen05.st and completed by tcgen05.wait::st + tcgen05.fence::before_thread_sync, read by the MMAs the
+// leader issues after its wait; the default CTA-scope release suffices for that hand-off (a cluster-scope release is
+// a full fence per arrival and costs about a microsecond).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 2D tile load into this CTA's shared memory; the transaction bytes complete on the barrier at `bar_cluster` (the
+// leader CTA's barrier). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar_cluster) {
     asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
-        ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
         : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+// D[tmem] (+)= A[tmem] x B[smem desc]^T over both CTAs of the pair (M 256, N from idesc, K 16)
+__device__ __forceinline__ void tc2_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                            uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-        ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-__device__ __forceinline__ void tc_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+// Arrive once on the barrier at this offset in both CTAs of the pair when the MMAs issued so far have completed.
+__device__ __forceinline__ void tc2_commit_both(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+// 16 TMEM lanes x 8 columns from the warp's registers: thread t -> lanes t/4 and t/4 + 8, columns 2(t%4), 2(t%4)+1
+// (r0, r1 on the first lane, r2, r3 on the second).
+__device__ __forceinline__ void tmem_st_16x256b(uint32_t taddr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+    asm volatile("tcgen05.st.sync.aligned.16x256b.x1.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(r0), "r"(r1),
+                 "r"(r2), "r"(r3)
                  : "memory");
 }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // 32 consecutive fp32 columns of this warp's 32 TMEM lanes (thread i <- lane base + i).
 __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t r[32]) {
     asm volatile(
@@ -97,308 +150,263 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t r[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Shared-memory matrix descriptor: canonical K-major layout with the 128-byte (TC_BK 64) or 64-byte (TC_BK 32)
-// swizzle (8-row atoms, TC_ATOM bytes apart), sm100 descriptor version 1.
-__device__ __forceinline__ uint64_t sw_desc(uint32_t saddr) {
-    constexpr uint64_t layout = TC_BK == 64 ? 2 : 4;          // SWIZZLE_128B : SWIZZLE_64B
-    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(TC_ATOM >> 4) << 32) |
-           ((uint64_t)1 << 46) | (layout << 61);
+// Shared-memory matrix descriptor of a [rows][64] fp16 sub-tile: canonical K-major layout, 128-byte swizzle, 8-row
+// atoms 1024 bytes apart, sm100 descriptor version 1.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 // Instruction descriptor, kind::f16: fp16 A and B (K-major), fp32 D, M x N.
 __host__ __device__ constexpr uint32_t tc_idesc_f16(int M, int N) {
     return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
-// Byte offset of element (row, k) of a [rows][TC_BK] fp16 tile in the swizzled K-major layout: 16-byte chunk c of
-// a row lands at c ^ (row & 7) (128-byte swizzle) or c ^ ((row >> 1) & 3) (64-byte swizzle).
-__device__ __forceinline__ uint32_t sw_off(int row, int k) {
-    const int x = TC_BK == 64 ? (row & 7) : ((row >> 1) & 3);
-    return (uint32_t)((row >> 3) * TC_ATOM + (row & 7) * TC_ROWB + ((((k >> 3) ^ x)) << 4) + (k & 7) * 2);
-}
 
-struct TcArgs {
-    // linear: one packed matrix [n/128][k/16][8 tiles][8K words], its svh, y rows
+struct TsArgs {
+    // linear: one packed matrix [n/128][k/16][8 tiles][8K words], its svh
     const uint8_t* packed;
     const __half* svh;
     int K;
+    // linear: y [M][ldy]; gate|up: the gate/up buffer [2][M][ldy] fp16 (M = positions, ldy = I)
     void* y;
     int ldy, y_dtype;
-    int M, k, n;                  // linear: M rows; grouped: k, n of the launch's projection
-    // grouped: alignment tables (items of <= 256 rows of one expert) and the expert table
+    int M, k, n;                  // rows (linear) or positions (grouped); k, n of the projection
+    // grouped: alignment tables (items of <= 320 positions of one expert) and the expert table
     const int* n_items;
     const int* item_expert;
     const int* item_start;
     const int* item_cnt;
-    const float* pair_w;          // down: routing weight of a pair position
+    const float* pair_w;          // down: routing weight of a position
     const ExpertDesc* experts;
-    float act_limit;
-    __half* a_dn;                 // gate|up: the down projection's activation rows [positions][I]
-    float* ybuf;                  // down: weighted rows [positions][H]
+    float* ybuf;                  // down: weighted rows [positions][n] fp32
     int* status;
 };
 
 // ------------------------------------------------------------------------------------------------ decode
 
-// Per-thread constant addressing of the decode: for each of the warp's TC_TPW tiles of a chunk, the tile's byte offset in
-// a trellis stage and the four swizzled byte offsets in a B stage that receive the lane's fragment registers
-// {n, k..k+1}, {n + 8, k..}, {n, k + 8..}, {n + 8, k + 8..} (n = tile column + g, k = tile row + 2q).
-// Linear / down: a stage holds two column blocks [cb][TC_TR tile-rows][8 tiles][32K bytes] of one matrix; warp dw
-// takes tiles TC_TPW dw ... Gate|up: a stage holds TC_TR tile-rows of the fused block, each [8 gate tiles (Kg) |
-// 8 up tiles (Ku)]; warps 0-7 take the gate tiles, 8-15 the up tiles, and B rows 0-127 / 128-255 are gate / up.
-struct TcDecodeMap {
-    uint32_t tile[TC_TPW];
-    uint32_t st[TC_TPW][4];
-};
-
-__device__ __forceinline__ TcDecodeMap tc_decode_map(int epi, int dw, int lane, int Kg, int Ku) {
-    TcDecodeMap mp;
-    const int g = lane >> 2, q = lane & 3;
-#pragma unroll
-    for (int j = 0; j < TC_TPW; ++j) {
-        int n0, k0;
-        if (epi == TC_GATEUP) {
-            const int mat = dw >> 3, idx = (dw & 7) * TC_TPW + j;    // 0 .. 8 TC_TR - 1 within the matrix
-            const int tr = idx >> 3, t = idx & 7;
-            const int row_stride = 8 * 32 * Kg + 8 * 32 * Ku;
-            mp.tile[j] = (uint32_t)(tr * row_stride + (mat ? 8 * 32 * Kg : 0) + t * 32 * (mat ? Ku : Kg));
-            n0 = mat * 128 + t * 16 + g;
-            k0 = tr * 16 + 2 * q;
-        } else {
-            const int ti = dw * TC_TPW + j;
-            const int cb = ti / (8 * TC_TR), tr = (ti >> 3) % TC_TR, t = ti & 7;
-            mp.tile[j] = (uint32_t)(((cb * TC_TR + tr) * 8 + t) * 32 * Ku);
-            n0 = cb * 128 + t * 16 + g;
-            k0 = tr * 16 + 2 * q;
-        }
-        mp.st[j][0] = sw_off(n0, k0);
-        mp.st[j][1] = sw_off(n0 + 8, k0);
-        mp.st[j][2] = sw_off(n0, k0 + 8);
-        mp.st[j][3] = sw_off(n0 + 8, k0 + 8);
-    }
-    return mp;
-}
-
+// One decoder warp: lane quadrant q (TMEM lanes 32q..32q+31 = features of n-tiles 2q, 2q+1) and k-tile j of every
+// 64-deep sub-chunk; per chunk it decodes 2 TS_KS tiles and stores each as one 16x256b block of the weight stage.
 template <int K>
-__device__ __forceinline__ void tc_decode_chunk(const uint8_t* tst, uint8_t* bst, const TcDecodeMap& mp,
-                                                const LaneWords& lw) {
-#pragma unroll
-    for (int j = 0; j < TC_TPW; ++j) {
-        uint32_t a[4];
-        decode_frag<K>(reinterpret_cast<const uint32_t*>(tst + mp.tile[j]), lw, a);
-#pragma unroll
-        for (int r = 0; r < 4; ++r) *reinterpret_cast<uint32_t*>(bst + mp.st[j][r]) = a[r];
-    }
-}
-
-template <int K>
-__device__ void tc_decoder_loop(const TcDecodeMap& mp, uint8_t* smem, uint8_t* bring, int bst, int t_stages,
-                                int t_stage_bytes, uint64_t* t_full, uint64_t* t_empty, uint64_t* b_full,
-                                uint64_t* b_empty, int nk, int lane, bool& to) {
+__device__ void ts_decoder_loop(uint8_t* smem, uint32_t tmem, int q, int j, int lane, bool has_cols, int nk,
+                                int t_stages, uint32_t t_blk, uint64_t* t_full, uint64_t* t_empty, uint64_t* empty,
+                                uint32_t lead_a_full, bool& to) {
     const LaneWords lw = lane_words<K>(lane);
     for (int kc = 0; kc < nk; ++kc) {
-        const int ts = kc % t_stages, s = kc % bst;
-        if (!to && !mbar_wait(&t_full[ts], (kc / t_stages) & 1)) to = true;
-        if (kc >= bst && !to && !mbar_wait(&b_empty[s], ((kc / bst) - 1) & 1)) to = true;
-        if (!to)
-            tc_decode_chunk<K>(smem + TcSmem::t0 + (size_t)ts * t_stage_bytes, bring + s * TC_TILE_BYTES, mp, lw);
-        fence_proxy_async();                                  // generic-proxy writes -> the tensor core's reads
+        const int ts = kc % t_stages, s = kc % TS_STAGES;
+        bool ok = true;
+        if (has_cols && !to) ok = mbar_wait(&t_full[ts], (kc / t_stages) & 1);
+        if (ok && kc >= TS_STAGES && !to) ok = mbar_wait(&empty[s], ((kc / TS_STAGES) - 1) & 1);
+        if (!__all_sync(0xFFFFFFFFu, ok)) to = true;
+        if (has_cols && !to) {
+            const uint8_t* tst = smem + TsSmem::t0 + (size_t)ts * t_blk;
+#pragma unroll
+            for (int si = 0; si < TS_KS; ++si) {
+                const int tr = j + 4 * si;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t a[4];
+                    decode_frag<K>(reinterpret_cast<const uint32_t*>(tst + (tr * 8 + 2 * q + h) * 32 * K), lw, a);
+                    // a = {n g, pair q'}, {n g+8, pair q'}, {n g, pair q'+4}, {n g+8, pair q'+4}
+                    tmem_st_16x256b(tmem + ((uint32_t)(32 * q + 16 * h) << 16) +
+                                        (uint32_t)(TS_A_COL0 + s * TS_A_COLS + tr * 8),
+                                    a[0], a[2], a[1], a[3]);
+                }
+            }
+        }
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-            mbar_arrive(&t_empty[ts]);
-            mbar_arrive(&b_full[s]);
+            mbar_arrive_cluster(lead_a_full + 8u * s);
+            if (has_cols) mbar_arrive(&t_empty[ts]);
         }
     }
 }
 
-__device__ void tc_decoder_dispatch(int K, const TcDecodeMap& mp, uint8_t* smem, uint8_t* bring, int bst,
-                                    int t_stages, int t_stage_bytes, uint64_t* t_full, uint64_t* t_empty,
-                                    uint64_t* b_full, uint64_t* b_empty, int nk, int lane, bool& to) {
-#define EXL3_TC_DEC(KK)                                                                                         \
-    tc_decoder_loop<KK>(mp, smem, bring, bst, t_stages, t_stage_bytes, t_full, t_empty, b_full, b_empty, nk, lane, \
-                        to)
+__device__ void ts_decoder_dispatch(int K, uint8_t* smem, uint32_t tmem, int q, int j, int lane, bool has_cols,
+                                    int nk, int t_stages, uint32_t t_blk, uint64_t* t_full, uint64_t* t_empty,
+                                    uint64_t* empty, uint32_t lead_a_full, bool& to) {
+#define EXL3_TS_DEC(KK) \
+    ts_decoder_loop<KK>(smem, tmem, q, j, lane, has_cols, nk, t_stages, t_blk, t_full, t_empty, empty, lead_a_full, to)
     switch (K) {
-        case 1: EXL3_TC_DEC(1); break;
-        case 2: EXL3_TC_DEC(2); break;
-        case 3: EXL3_TC_DEC(3); break;
-        case 4: EXL3_TC_DEC(4); break;
-        case 5: EXL3_TC_DEC(5); break;
-        case 6: EXL3_TC_DEC(6); break;
-        case 7: EXL3_TC_DEC(7); break;
-        default: EXL3_TC_DEC(8); break;
+        case 1: EXL3_TS_DEC(1); break;
+        case 2: EXL3_TS_DEC(2); break;
+        case 3: EXL3_TS_DEC(3); break;
+        case 4: EXL3_TS_DEC(4); break;
+        case 5: EXL3_TS_DEC(5); break;
+        case 6: EXL3_TS_DEC(6); break;
+        case 7: EXL3_TS_DEC(7); break;
+        default: EXL3_TS_DEC(8); break;
     }
-#undef EXL3_TC_DEC
+#undef EXL3_TS_DEC
 }
 
 // ------------------------------------------------------------------------------------------------ kernel
 
+// Activation tensor maps of one launch: per matrix (gate|up: gate, up), boxes of 128 and of 32 rows.
+struct TsMaps {
+    CUtensorMap m[2][2];
+};
+
 template <int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant__ CUtensorMap amap0,
-                                                           const __grid_constant__ CUtensorMap amap1,
-                                                           const TcArgs p) {
-    constexpr int NMAT = tc_nmat(EPI);
-    constexpr int AST = tc_a_stages(EPI);
-    constexpr int BST = tc_b_stages(EPI);
-    constexpr int A_STAGE = NMAT * TC_TILE_BYTES;
-    static_assert(AST <= TC_MAX_ASTAGES && BST <= TC_MAX_BSTAGES && AST * A_STAGE + BST * TC_TILE_BYTES <= TC_AB_REGION,
-                  "rings");
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TS_THREADS, 1)
+    k_gemm_pair(const __grid_constant__ TsMaps maps, const TsArgs p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
     pdl_trigger();
 
-    // ---- the tile: rows [m0, m0 + rows) of the activation matrices, output columns from n0 ----
-    int m0, rows, n0, Ku = p.K, Kg = p.K, expert = 0;
-    const uint8_t* wmat;                                      // packed weights of the tile's first column block
-    size_t cb_bytes;                                          // bytes of one column block (all k)
-    const __half* svh0;
-    const __half* svh1 = nullptr;
+    // ---- the pair tile: activation rows [m0, m0 + rows), rows <= 320; this CTA's 128-feature column block cb ----
+    int m0, rows, Kw = p.K, cb, mat = 0, expert = 0;
+    const uint8_t* wsrc;                                      // the CTA's trellis, tile-row 0
+    size_t row_stride;                                        // bytes between tile-rows in wsrc
+    const __half* svh;
     if constexpr (EPI == TC_LINEAR) {
-        m0 = blockIdx.y * TC_BM;
-        rows = min(TC_BM, p.M - m0);
-        n0 = blockIdx.x * TC_BN;
-        cb_bytes = (size_t)(p.k / 16) * 8 * 32 * Ku;
-        wmat = p.packed + (size_t)(n0 / 128) * cb_bytes;
-        svh0 = p.svh;
+        m0 = blockIdx.y * TS_TILE_ROWS;
+        rows = min(TS_TILE_ROWS, p.M - m0);
+        cb = blockIdx.x;
+        row_stride = (size_t)8 * 32 * Kw;
+        wsrc = p.packed + (size_t)cb * (p.k / 16) * row_stride;
+        svh = p.svh;
     } else {
         pdl_wait();                                           // the alignment tables come from an earlier kernel
         const int item = blockIdx.y;
-        if (item >= __ldcg(p.n_items)) return;                // before any barrier or TMEM allocation
+        if (item >= __ldcg(p.n_items)) return;                // both CTAs of the pair: before any cluster barrier
         expert = __ldcg(p.item_expert + item);
         m0 = __ldcg(p.item_start + item);
         rows = __ldcg(p.item_cnt + item);
         const ExpertDesc& ed = p.experts[expert];
         if constexpr (EPI == TC_GATEUP) {
-            Kg = ed.K[0];
-            Ku = ed.K[1];
-            n0 = blockIdx.x * 128;                            // output column block of gate and up
-            cb_bytes = (size_t)(p.k / 16) * (8 * 32 * Kg + 8 * 32 * Ku);
-            wmat = reinterpret_cast<const uint8_t*>(ed.tr[0]) + (size_t)blockIdx.x * cb_bytes;
-            svh0 = ed.svh[0];
-            svh1 = ed.svh[1];
+            const int npm = (p.n + 255) / 256;                // pairs per matrix
+            const int pp = blockIdx.x >> 1;
+            mat = pp / npm;
+            cb = 2 * (pp % npm) + (int)rank;
+            const int Kg = ed.K[0], Ku = ed.K[1];
+            Kw = mat ? Ku : Kg;
+            row_stride = (size_t)8 * 32 * (Kg + Ku);          // fused [I/128][H/16][8 gate | 8 up]
+            wsrc = reinterpret_cast<const uint8_t*>(ed.tr[0]) + (size_t)cb * (p.k / 16) * row_stride +
+                   (mat ? 8 * 32 * Kg : 0);
+            svh = ed.svh[mat];
         } else {
-            Ku = ed.K[2];
-            Kg = Ku;
-            n0 = blockIdx.x * TC_BN;
-            cb_bytes = (size_t)(p.k / 16) * 8 * 32 * Ku;
-            wmat = reinterpret_cast<const uint8_t*>(ed.tr[2]) + (size_t)(n0 / 128) * cb_bytes;
-            svh0 = ed.svh[2];
+            Kw = ed.K[2];
+            cb = blockIdx.x;
+            row_stride = (size_t)8 * 32 * Kw;
+            wsrc = reinterpret_cast<const uint8_t*>(ed.tr[2]) + (size_t)cb * (p.k / 16) * row_stride;
+            svh = ed.svh[2];
         }
     }
-    const int nk = p.k / TC_BK;
-    // trellis stage: linear / down two column blocks x 4 tile-rows x 8 tiles; gate|up 4 fused tile-rows
-    const int t_stage_bytes = EPI == TC_GATEUP ? TC_TR * (8 * 32 * Kg + 8 * 32 * Ku) : 2 * TC_TR * 8 * 32 * Ku;
-    int t_stages = TC_T_RING / t_stage_bytes;
-    if (t_stages > TC_MAX_TSTAGES) t_stages = TC_MAX_TSTAGES;
+    const bool has_cols = (cb + 1) * 128 <= p.n;              // the last pair of an odd block count has one
+    const bool has2 = rows > 256;                             // the second MMA (rows 256..319) is needed
+    const int nk = p.k / TS_BK;
+    const uint32_t t_blk = (uint32_t)(TS_TR * 8 * 32 * Kw);  // trellis bytes of one chunk
+    int t_stages = TS_T_RING / (int)t_blk;
+    if (t_stages > TS_MAX_TSTAGES) t_stages = TS_MAX_TSTAGES;
 
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::bars);
-    uint64_t* a_full = bars;
-    uint64_t* a_empty = a_full + TC_MAX_ASTAGES;
-    uint64_t* b_full = a_empty + TC_MAX_ASTAGES;
-    uint64_t* b_empty = b_full + TC_MAX_BSTAGES;
-    uint64_t* t_full = b_empty + TC_MAX_BSTAGES;
-    uint8_t* bring = smem + TcSmem::a0 + AST * A_STAGE;           // B ring after the activation ring
-    uint64_t* t_empty = t_full + TC_MAX_TSTAGES;
-    uint64_t* acc_full = t_empty + TC_MAX_TSTAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::tmem_slot);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TsSmem::bars);
+    uint64_t* b_full = bars;                                  // leader: activation stage landed (both CTAs)
+    uint64_t* a_full = b_full + TS_STAGES;                    // leader: weight stage decoded (both CTAs)
+    uint64_t* empty = a_full + TS_STAGES;                     // both: the stage's MMAs completed
+    uint64_t* t_full = empty + TS_STAGES;
+    uint64_t* t_empty = t_full + TS_MAX_TSTAGES;
+    uint64_t* acc_full = t_empty + TS_MAX_TSTAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TsSmem::tmem_slot);
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < AST; ++s) {
-            mbar_init(&a_full[s], 1);
-            mbar_init(&a_empty[s], 1);
-        }
-        for (int s = 0; s < BST; ++s) {
-            mbar_init(&b_full[s], TC_DEC_WARPS);
-            mbar_init(&b_empty[s], 1);
+        for (int s = 0; s < TS_STAGES; ++s) {
+            mbar_init(&b_full[s], 1);
+            mbar_init(&a_full[s], 2 * TS_DEC_WARPS);
+            mbar_init(&empty[s], 1);
         }
         for (int s = 0; s < t_stages; ++s) {
             mbar_init(&t_full[s], 1);
-            mbar_init(&t_empty[s], TC_DEC_WARPS);
+            mbar_init(&t_empty[s], TS_DEC_WARPS);
         }
         mbar_init(acc_full, 1);
         fence_barrier_init();
     }
-    if (warp == 1) {                                          // TMEM: all 512 columns (four 128 x 128 fp32 blocks)
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+    if (warp == 1) {                                          // TMEM: all 512 columns of both CTAs
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
                      : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();                                           // barriers and TMEM ready in both CTAs
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const uint32_t lead_b_full = map_to_rank(smem_u32(b_full), 0);
+    const uint32_t lead_a_full = map_to_rank(smem_u32(a_full), 0);
     bool to = false;
 
     if (warp == 0) {
-        // ---------------- activation tiles (TMA) ----------------
-        pdl_wait();                                           // the rotated activations come from an earlier kernel
+        // ---------------- activation rows (TMA) ----------------
+        if constexpr (EPI == TC_LINEAR) pdl_wait();           // the rotated rows come from an earlier kernel
         if (lane == 0) {
-            int last_s[TC_MAX_ASTAGES];
-            for (int s = 0; s < TC_MAX_ASTAGES; ++s) last_s[s] = -1;
-            for (int kc = 0; kc < nk && !to; ++kc) {
-                const int s = kc % AST;
-                if (kc >= AST && !mbar_wait(&a_empty[s], ((kc / AST) - 1) & 1)) { to = true; break; }
-                mbar_expect_tx(&a_full[s], A_STAGE);
-                uint8_t* dst = smem + TcSmem::a0 + s * A_STAGE;
-                tma_load_2d(dst, &amap0, kc * TC_BK, m0, &a_full[s]);
-                if constexpr (NMAT == 2) tma_load_2d(dst + TC_TILE_BYTES, &amap1, kc * TC_BK, m0, &a_full[s]);
-                last_s[s] = kc;
+            const CUtensorMap* map1 = &maps.m[EPI == TC_GATEUP ? mat : 0][0];
+            const CUtensorMap* map2 = &maps.m[EPI == TC_GATEUP ? mat : 0][1];
+            const int row1 = m0 + 128 * (int)rank, row2 = m0 + 256 + (TS_N2 / 2) * (int)rank;
+            const uint32_t tx = 2u * TS_KS * (has2 ? TS_SUB : TS_SUB2);   // both CTAs' bytes of a stage
+            int last[TS_STAGES];
+            for (int s = 0; s < TS_STAGES; ++s) last[s] = -1;
+            for (int kc = 0; kc < nk; ++kc) {
+                const int s = kc % TS_STAGES;
+                if (kc >= TS_STAGES && !mbar_wait(&empty[s], ((kc / TS_STAGES) - 1) & 1)) { to = true; break; }
+                if (rank == 0) mbar_expect_tx(&b_full[s], tx);
+                uint8_t* dst = smem + TsSmem::b0 + s * TS_B_STAGE;
+#pragma unroll
+                for (int si = 0; si < TS_KS; ++si) {
+                    tma_load_2d_pair(dst + si * TS_SUB, map1, kc * TS_BK + si * 64, row1, lead_b_full + 8u * s);
+                    if (has2)
+                        tma_load_2d_pair(dst + si * TS_SUB + TS_SUB2, map2, kc * TS_BK + si * 64, row2,
+                                         lead_b_full + 8u * s);
+                }
+                last[s] = kc;
             }
-            for (int s = 0; s < AST; ++s)                     // copies landed before the CTA may exit
-                if (last_s[s] >= 0 && !mbar_wait(&a_full[s], (last_s[s] / AST) & 1)) to = true;
+            if (rank == 0)                                    // both CTAs' copies landed before the pair may exit
+                for (int s = 0; s < TS_STAGES; ++s)
+                    if (last[s] >= 0 && !mbar_wait(&b_full[s], (last[s] / TS_STAGES) & 1)) to = true;
         }
     } else if (warp == 1) {
-        // ---------------- MMA issue (one lane) ----------------
-        if (lane == 0) {
+        // ---------------- MMA issue (leader, one lane) ----------------
+        if (rank == 0 && lane == 0) {
+            constexpr uint32_t idesc1 = tc_idesc_f16(256, 256), idesc2 = tc_idesc_f16(256, TS_N2);
             for (int kc = 0; kc < nk; ++kc) {
-                const int sa = kc % AST, sb = kc % BST;
-                if (!to && !mbar_wait(&a_full[sa], (kc / AST) & 1)) to = true;
-                if (!to && !mbar_wait(&b_full[sb], (kc / BST) & 1)) to = true;
+                const int s = kc % TS_STAGES;
+                const uint32_t ph = (kc / TS_STAGES) & 1;
+                if (!to && !mbar_wait(&a_full[s], ph)) to = true;
+                if (!to && !mbar_wait(&b_full[s], ph)) to = true;
                 tc_fence_after();
                 if (!to) {
-                    const uint32_t a_base = smem_u32(smem + TcSmem::a0 + sa * A_STAGE);
-                    const uint32_t b_base = smem_u32(bring + sb * TC_TILE_BYTES);
+                    const uint32_t b_base = smem_u32(smem + TsSmem::b0 + s * TS_B_STAGE);
 #pragma unroll
-                    for (int kk = 0; kk < TC_BK / 16; ++kk) {
-                        const uint32_t acc = (kc | kk) != 0;
-                        if constexpr (EPI == TC_GATEUP) {
-                            // accumulator (mat, j) at TMEM column (2 mat + j) * 128: activation tile of the matrix,
-                            // row half j; B rows of the matrix (gate 0-127, up 128-255)
-#pragma unroll
-                            for (int mat = 0; mat < 2; ++mat)
-#pragma unroll
-                                for (int j = 0; j < 2; ++j)
-                                    tc_mma_f16(tmem + (2 * mat + j) * 128,
-                                               sw_desc(a_base + mat * TC_TILE_BYTES + j * (TC_TILE_BYTES / 2) +
-                                                       kk * 32),
-                                               sw_desc(b_base + mat * (TC_TILE_BYTES / 2) + kk * 32),
-                                               tc_idesc_f16(128, 128), acc);
-                        } else {
-#pragma unroll
-                            for (int j = 0; j < 2; ++j)
-                                tc_mma_f16(tmem + j * TC_BN, sw_desc(a_base + j * (TC_TILE_BYTES / 2) + kk * 32),
-                                           sw_desc(b_base + kk * 32), tc_idesc_f16(128, TC_BN), acc);
-                        }
+                    for (int kk = 0; kk < TS_BK / 16; ++kk) {
+                        const uint32_t a_t = tmem + (uint32_t)(TS_A_COL0 + s * TS_A_COLS + kk * 8);
+                        const uint32_t b_s = b_base + (kk >> 2) * TS_SUB + (kk & 3) * 32;
+                        tc2_mma_ts(tmem, a_t, sw128_desc(b_s), idesc1, (kc | kk) != 0);
+                        if (has2) tc2_mma_ts(tmem + 256, a_t, sw128_desc(b_s + TS_SUB2), idesc2, (kc | kk) != 0);
                     }
                 }
-                tc_commit(&a_empty[sa]);                      // the stages are free once these MMAs completed
-                tc_commit(&b_empty[sb]);
+                tc2_commit_both(&empty[s]);                   // both CTAs' stages are free once these completed
             }
-            tc_commit(acc_full);
+            tc2_commit_both(acc_full);
         }
     } else if (warp == 2) {
         // ---------------- trellis tiles (bulk copies) ----------------
-        if (lane == 0) {
-            int last[TC_MAX_TSTAGES];
-            for (int s = 0; s < TC_MAX_TSTAGES; ++s) last[s] = -1;
-            // column blocks present (the last tile of a linear or down projection may have 1); gate|up: one fused block
-            const int nbv = EPI == TC_GATEUP ? 1 : min(2, (p.n - n0) / 128);
-            const uint32_t blk = (uint32_t)(t_stage_bytes / (EPI == TC_GATEUP ? 1 : 2));
-            for (int kc = 0; kc < nk && !to; ++kc) {
+        if (lane == 0 && has_cols) {
+            int last[TS_MAX_TSTAGES];
+            for (int s = 0; s < TS_MAX_TSTAGES; ++s) last[s] = -1;
+            const uint32_t tile_row_bytes = (uint32_t)(8 * 32 * Kw);
+            for (int kc = 0; kc < nk; ++kc) {
                 const int ts = kc % t_stages;
                 if (kc >= t_stages && !mbar_wait(&t_empty[ts], ((kc / t_stages) - 1) & 1)) { to = true; break; }
-                mbar_expect_tx(&t_full[ts], blk * (uint32_t)nbv);
-                uint8_t* dst = smem + TcSmem::t0 + (size_t)ts * t_stage_bytes;
-                for (int b = 0; b < nbv; ++b)
-                    bulk_g2s(dst + b * blk, wmat + (size_t)b * cb_bytes + (size_t)kc * blk, blk, &t_full[ts]);
+                mbar_expect_tx(&t_full[ts], t_blk);
+                uint8_t* dst = smem + TsSmem::t0 + (size_t)ts * t_blk;
+                if constexpr (EPI == TC_GATEUP) {
+                    for (int tr = 0; tr < TS_TR; ++tr)
+                        bulk_g2s(dst + tr * tile_row_bytes, wsrc + (size_t)(kc * TS_TR + tr) * row_stride,
+                                 tile_row_bytes, &t_full[ts]);
+                } else {
+                    bulk_g2s(dst, wsrc + (size_t)kc * t_blk, t_blk, &t_full[ts]);
+                }
                 last[ts] = kc;
             }
             for (int s = 0; s < t_stages; ++s)
@@ -406,189 +414,233 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(const __grid_constant
         }
     } else {
         // ---------------- decoders, then the epilogue ----------------
-        const int dw = warp - 3;
-        const TcDecodeMap mp = tc_decode_map(EPI, dw, lane, Kg, Ku);
-        const int Kw = (EPI == TC_GATEUP && dw < 8) ? Kg : Ku;
-        tc_decoder_dispatch(Kw, mp, smem, bring, BST, t_stages, t_stage_bytes, t_full, t_empty, b_full, b_empty, nk,
-                            lane, to);
+        const int dw = warp - 3, q = warp & 3, j = dw >> 2;
+        ts_decoder_dispatch(Kw, smem, tmem, q, j, lane, has_cols, nk, t_stages, t_blk, t_full, t_empty, empty,
+                            lead_a_full, to);
 
-        pdl_wait();                                           // outputs may be in use by an earlier kernel until here
+        if constexpr (EPI == TC_LINEAR) pdl_wait();           // y may be in use by an earlier kernel until here
         if (!to && !mbar_wait(acc_full, 0)) to = true;
+        if (!__all_sync(0xFFFFFFFFu, !to)) to = true;
         tc_fence_after();
-        // the four 128 x 128 accumulator blocks: block bi at TMEM column 128 bi. Linear / down: bi = 2 j + b
-        // (row half j, column block b); gate|up: bi = 2 mat + j. The four warps of a TMEM lane quadrant each load
-        // one block; staging [2][128 rows][128 cols] fp32 in the activation + B rings (free after the main loop), columns
-        // XOR-swizzled by the row. Pass 0: blocks of row half 0, pass 1: row half 1.
-        const int quad = warp & 3, bi = dw >> 2;              // warps 3..18: quad covers 0..3 four times
-        const int bj = EPI == TC_GATEUP ? (bi & 1) : (bi >> 1);   // row half of block bi
-        const int bslot = EPI == TC_GATEUP ? (bi >> 1) : (bi & 1); // staging slot: column block, or gate / up
-        float* stage = reinterpret_cast<float*>(smem + TcSmem::a0);
-        for (int pass = 0; pass < 2; ++pass) {
-            if (bj == pass) {
-                float* st = stage + (size_t)bslot * 128 * 128;
-                const int row = quad * 32 + lane;             // accumulator row = TMEM lane
+        // 128 rows per pass: accumulator lanes 32q..32q+31 (features), columns 128 pass + 32j .. + 31 (rows) ->
+        // staging [128 rows][128 features]
+        float* stage = reinterpret_cast<float*>(smem + TsSmem::b0);
+        const int col = cb * 128 + 4 * lane;                  // output feature of the projection
+        for (int r0 = 0; r0 < rows; r0 += 128) {               // rows is uniform: every warp takes each barrier
+            if (!to && r0 + 32 * j < rows) {
+                uint32_t r[32];
+                tc_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(r0 + 32 * j), r);
 #pragma unroll
-                for (int c0 = 0; c0 < 128; c0 += 32) {
-                    uint32_t r[32];
-                    tc_ld32(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(bi * 128 + c0), r);
-#pragma unroll
-                    for (int c = 0; c < 32; ++c)
-                        st[row * 128 + ((c0 + c) ^ (row & 31))] = __uint_as_float(r[c]);
-                }
+                for (int c = 0; c < 32; ++c) stage[(32 * j + c) * 128 + 32 * q + lane] = __uint_as_float(r[c]);
             }
-            asm volatile("bar.sync 1, %0;" ::"r"(TC_DEC_WARPS * 32) : "memory");
-            if constexpr (EPI == TC_GATEUP) {
-                // row r of this half: gate and up blocks -> act -> the down input's rotation, into a_dn
-                const __half* suh_d = p.experts[expert].suh[2];
-                for (int row = dw; row < 128; row += TC_DEC_WARPS) {
-                    const int rr = pass * 128 + row;
-                    if (rr >= rows) continue;
-                    float gv[4], uv[4];
+            asm volatile("bar.sync 1, %0;" ::"r"(TS_DEC_WARPS * 32) : "memory");
+            for (int t = r0 + dw; t < min(rows, r0 + 128) && has_cols && !to; t += TS_DEC_WARPS) {
+                const float4 s4 = *reinterpret_cast<const float4*>(stage + (t - r0) * 128 + 4 * lane);
+                float v[4] = {s4.x, s4.y, s4.z, s4.w};
+                fwht128_warp(v, lane);
+                const int m = m0 + t;
+                if constexpr (EPI == TC_DOWN) {
+                    const float wgt = __ldcg(p.pair_w + m);
+                    float o[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) o[e] = wgt * (v[e] * kRsqrt128 * __half2float(svh[col + e]));
+                    *reinterpret_cast<float4*>(p.ybuf + (size_t)m * p.n + col) = make_float4(o[0], o[1], o[2], o[3]);
+                } else {
+                    const int ydt = EPI == TC_GATEUP ? EXL3_F16 : p.y_dtype;
+                    float o[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        gv[e] = stage[row * 128 + ((4 * lane + e) ^ (row & 31))];
-                        uv[e] = stage[128 * 128 + row * 128 + ((4 * lane + e) ^ (row & 31))];
+                        const float sv = __half2float(svh[col + e]);
+                        if (ydt == EXL3_F16)
+                            o[e] = __half2float(__float2half_rn(__half2float(__float2half_rn(v[e] * kRsqrt128)) * sv));
+                        else
+                            o[e] = v[e] * kRsqrt128 * sv;
                     }
-                    fwht128_warp(gv, lane);
-                    fwht128_warp(uv, lane);
-                    const int col = n0 + 4 * lane;            // column of I
-                    float h[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float gg = __half2float(__float2half_rn(
-                            __half2float(__float2half_rn(gv[e] * kRsqrt128)) * __half2float(svh0[col + e])));
-                        float uu = __half2float(__float2half_rn(
-                            __half2float(__float2half_rn(uv[e] * kRsqrt128)) * __half2float(svh1[col + e])));
-                        float sg = silu_f(gg);
-                        if (p.act_limit != 0.f) {
-                            sg = fminf(sg, p.act_limit);
-                            uu = fminf(fmaxf(uu, -p.act_limit), p.act_limit);
-                        }
-                        const float act = __half2float(__float2half_rn(sg * uu));
-                        h[e] = __half2float(__float2half_rn(act * __half2float(suh_d[col + e])));
-                    }
-                    fwht128_warp(h, lane);
-                    __half2 h01 = __floats2half2_rn(h[0] * kRsqrt128, h[1] * kRsqrt128);
-                    __half2 h23 = __floats2half2_rn(h[2] * kRsqrt128, h[3] * kRsqrt128);
-                    uint2 u;
-                    u.x = *reinterpret_cast<uint32_t*>(&h01);
-                    u.y = *reinterpret_cast<uint32_t*>(&h23);
-                    *reinterpret_cast<uint2*>(p.a_dn + (size_t)(m0 + rr) * p.n + col) = u;
-                }
-            } else {
-                // 2 column blocks x 128 rows over 16 warps, one row at a time
-                for (int rb = dw; rb < 2 * 128; rb += TC_DEC_WARPS) {
-                    const int b = rb >> 7, row = rb & 127;
-                    const int rr = pass * 128 + row;
-                    const int col = n0 + b * 128 + 4 * lane;
-                    if (rr >= rows || col >= p.n) continue;
-                    const float* src = stage + (size_t)b * 128 * 128 + row * 128;
-                    float v[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) v[e] = src[(4 * lane + e) ^ (row & 31)];
-                    fwht128_warp(v, lane);
-                    if constexpr (EPI == TC_DOWN) {
-                        const float wgt = __ldcg(p.pair_w + m0 + rr);
-                        float o[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) o[e] = wgt * (v[e] * kRsqrt128 * __half2float(svh0[col + e]));
-                        *reinterpret_cast<float4*>(p.ybuf + (size_t)(m0 + rr) * p.n + col) =
+                    const size_t yrow = (EPI == TC_GATEUP ? (size_t)mat * p.M : 0) + (size_t)m;
+                    if (ydt == EXL3_F32) {
+                        *reinterpret_cast<float4*>(static_cast<float*>(p.y) + yrow * p.ldy + col) =
                             make_float4(o[0], o[1], o[2], o[3]);
+                    } else if (ydt == EXL3_F16) {
+                        __half2 h01 = __floats2half2_rn(o[0], o[1]), h23 = __floats2half2_rn(o[2], o[3]);
+                        uint2 u;
+                        u.x = *reinterpret_cast<uint32_t*>(&h01);
+                        u.y = *reinterpret_cast<uint32_t*>(&h23);
+                        *reinterpret_cast<uint2*>(static_cast<__half*>(p.y) + yrow * p.ldy + col) = u;
                     } else {
-                        const int m = m0 + rr;
-                        float o[4];
+                        __nv_bfloat16* yp = static_cast<__nv_bfloat16*>(p.y) + yrow * p.ldy + col;
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float sv = __half2float(svh0[col + e]);
-                            if (p.y_dtype == EXL3_F16)
-                                o[e] = __half2float(
-                                    __float2half_rn(__half2float(__float2half_rn(v[e] * kRsqrt128)) * sv));
-                            else
-                                o[e] = v[e] * kRsqrt128 * sv;
-                        }
-                        if (p.y_dtype == EXL3_F32) {
-                            *reinterpret_cast<float4*>(static_cast<float*>(p.y) + (size_t)m * p.ldy + col) =
-                                make_float4(o[0], o[1], o[2], o[3]);
-                        } else if (p.y_dtype == EXL3_F16) {
-                            __half2 h01 = __floats2half2_rn(o[0], o[1]), h23 = __floats2half2_rn(o[2], o[3]);
-                            uint2 u;
-                            u.x = *reinterpret_cast<uint32_t*>(&h01);
-                            u.y = *reinterpret_cast<uint32_t*>(&h23);
-                            *reinterpret_cast<uint2*>(static_cast<__half*>(p.y) + (size_t)m * p.ldy + col) = u;
-                        } else {
-                            __nv_bfloat16* yp = static_cast<__nv_bfloat16*>(p.y) + (size_t)m * p.ldy + col;
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) yp[e] = __float2bfloat16_rn(o[e]);
-                        }
+                        for (int e = 0; e < 4; ++e) yp[e] = __float2bfloat16_rn(o[e]);
                     }
                 }
             }
-            asm volatile("bar.sync 1, %0;" ::"r"(TC_DEC_WARPS * 32) : "memory");
+            asm volatile("bar.sync 1, %0;" ::"r"(TS_DEC_WARPS * 32) : "memory");
         }
     }
     if (to) report(p.status, EXL3_ERR_TIMEOUT);
+    __syncwarp();
     tc_fence_before();
-    __syncthreads();
+    cluster_sync();                                           // both CTAs done with TMEM and shared memory
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
     }
 }
 
 // ------------------------------------------------------------------------------------------------ activation rows
 
-// Rotated input rows in plain row-major order: xh[m][k] = fp16(H(fp16(x * suh)) / sqrt(128)) per 128-block.
-static __global__ void __launch_bounds__(256) k_rotate_rows(const void* x, int ldx, int x_bf16, int M, int k,
-                                                            const __half* suh, __half* xh) {
+// Store the lane's 4 values of a 128-block (k = 4l..4l+3) as fp16 in the operand's k order: inside each 16-element
+// group, k pair p goes to pair slot p < 4 ? 2p : 2p - 7 (lane l holds pairs 2i, 2i+1 of group l/4, i = l % 4).
+__device__ __forceinline__ void store_operand_block(__half* blk, int lane, const float v[4]) {
+    const int i = lane & 3;
+    const int slot = i < 2 ? 4 * i : 4 * i - 7;
+    uint32_t* d = reinterpret_cast<uint32_t*>(blk) + (lane >> 2) * 8 + slot;
+    __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
+    d[0] = *reinterpret_cast<uint32_t*>(&h01);
+    d[2] = *reinterpret_cast<uint32_t*>(&h23);
+}
+// The lane's 4 consecutive 16-bit values (8-byte aligned) widened to fp32.
+template <typename T>
+__device__ __forceinline__ void load4(const T* src, float v[4]) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(src));
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = to_f32<T>(e[j]);
+}
+// xh = fp16(H(fp16(x * suh)) / sqrt(128)) for one 128-block, the lane's 4 values (x and suh already loaded).
+__device__ __forceinline__ void rotate4(float v[4], const float s[4], int lane) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = __half2float(__float2half_rn(v[j] * s[j]));
+    fwht128_warp(v, lane);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = __half2float(__float2half_rn(v[j] * kRsqrt128));
+}
+
+constexpr int kRotJobs = 4;                                   // 128-blocks in flight per warp
+
+// Rotated input rows of the dense linear, in the operand's k order: xh[m][k].
+template <typename T>
+static __global__ void __launch_bounds__(256) k_rotate_rows(const T* x, int ldx, int M, int k, const __half* suh,
+                                                            __half* xh) {
     pdl_wait();
     pdl_trigger();
     const int KB = k / 128, lane = threadIdx.x & 31;
-    for (long j = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < (long)M * KB;
-         j += ((long)gridDim.x * blockDim.x) >> 5) {
-        const int row = (int)(j / KB), kb = (int)(j % KB);
-        float v[4];
-        const __half* su = suh ? suh + kb * 128 : nullptr;
-        if (x_bf16)
-            rotated_block<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x) + (size_t)row * ldx + kb * 128, su,
-                                         lane, v);
-        else
-            rotated_block<__half>(static_cast<const __half*>(x) + (size_t)row * ldx + kb * 128, su, lane, v);
-        __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
-        uint2 u;
-        u.x = *reinterpret_cast<uint32_t*>(&h01);
-        u.y = *reinterpret_cast<uint32_t*>(&h23);
-        *reinterpret_cast<uint2*>(xh + (size_t)row * k + kb * 128 + 4 * lane) = u;
+    const long njobs = (long)M * KB;
+    const long nw = ((long)gridDim.x * blockDim.x) >> 5;
+    for (long j0 = (((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kRotJobs; j0 < njobs; j0 += nw * kRotJobs) {
+        float v[kRotJobs][4], s[kRotJobs][4];
+#pragma unroll
+        for (int u = 0; u < kRotJobs; ++u) {
+            const long j = j0 + u;
+            if (j >= njobs) break;
+            const int row = (int)(j / KB), kb = (int)(j % KB);
+            load4<T>(x + (size_t)row * ldx + kb * 128 + 4 * lane, v[u]);
+            if (suh)
+                load4<__half>(suh + kb * 128 + 4 * lane, s[u]);
+            else
+                s[u][0] = s[u][1] = s[u][2] = s[u][3] = 1.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kRotJobs; ++u) {
+            const long j = j0 + u;
+            if (j >= njobs) break;
+            const int row = (int)(j / KB), kb = (int)(j % KB);
+            rotate4(v[u], s[u], lane);
+            store_operand_block(xh + (size_t)row * k + kb * 128, lane, v[u]);
+        }
     }
 }
 
-// Rotated gate and up input rows of every pair position, row-major: a_gu[mat][pos][H] = rot(x[token] * suh of the
-// position's expert's matrix mat). Positions beyond the count in use are skipped.
-static __global__ void __launch_bounds__(256) k_rotate_pairs(const void* x, int ldx, int x_bf16, int H, int P,
-                                                             const int* n_pos, const int* pair_tok,
-                                                             const int* pair_expert, const ExpertDesc* experts,
-                                                             __half* a_gu) {
+// Rotated gate and up input rows of every pair position, in the operand's k order: a_gu[mat][pos][H] =
+// rot(x[token] * suh of the position's expert's matrix mat). The token's block is loaded once for both matrices.
+template <typename T>
+static __global__ void __launch_bounds__(256) k_rotate_pairs(const T* x, int ldx, int H, int P, const int* n_pos,
+                                                             const int* pair_tok, const int* pair_expert,
+                                                             const ExpertDesc* experts, __half* a_gu) {
     pdl_wait();
     pdl_trigger();
     const int KB = H / 128, lane = threadIdx.x & 31;
-    const int np = min(P, __ldcg(n_pos));
-    for (long j = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; j < (long)np * 2 * KB;
-         j += ((long)gridDim.x * blockDim.x) >> 5) {
-        const int pos = (int)(j / (2 * KB)), mat = (int)((j / KB) % 2), kb = (int)(j % KB);
-        const int tok = __ldcg(pair_tok + pos), e = __ldcg(pair_expert + pos);
-        const __half* suh = experts[e].suh[mat];
-        const __half* su = suh ? suh + kb * 128 : nullptr;
-        float v[4];
-        if (x_bf16)
-            rotated_block<__nv_bfloat16>(static_cast<const __nv_bfloat16*>(x) + (size_t)tok * ldx + kb * 128, su,
-                                         lane, v);
-        else
-            rotated_block<__half>(static_cast<const __half*>(x) + (size_t)tok * ldx + kb * 128, su, lane, v);
-        __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
-        uint2 u;
-        u.x = *reinterpret_cast<uint32_t*>(&h01);
-        u.y = *reinterpret_cast<uint32_t*>(&h23);
-        *reinterpret_cast<uint2*>(a_gu + ((size_t)mat * P + pos) * H + kb * 128 + 4 * lane) = u;
+    const long njobs = (long)min(P, __ldcg(n_pos)) * KB;
+    const long nw = ((long)gridDim.x * blockDim.x) >> 5;
+    for (long j0 = (((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kRotJobs; j0 < njobs; j0 += nw * kRotJobs) {
+        float v[kRotJobs][4], sg[kRotJobs][4], su[kRotJobs][4];
+#pragma unroll
+        for (int u = 0; u < kRotJobs; ++u) {
+            const long j = j0 + u;
+            if (j >= njobs) break;
+            const int pos = (int)(j / KB), kb = (int)(j % KB);
+            const int tok = __ldcg(pair_tok + pos), e = __ldcg(pair_expert + pos);
+            load4<T>(x + (size_t)tok * ldx + kb * 128 + 4 * lane, v[u]);
+            const __half* s0 = experts[e].suh[0];
+            const __half* s1 = experts[e].suh[1];
+            if (s0) load4<__half>(s0 + kb * 128 + 4 * lane, sg[u]);
+            else sg[u][0] = sg[u][1] = sg[u][2] = sg[u][3] = 1.0f;
+            if (s1) load4<__half>(s1 + kb * 128 + 4 * lane, su[u]);
+            else su[u][0] = su[u][1] = su[u][2] = su[u][3] = 1.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kRotJobs; ++u) {
+            const long j = j0 + u;
+            if (j >= njobs) break;
+            const int pos = (int)(j / KB), kb = (int)(j % KB);
+            float w[4] = {v[u][0], v[u][1], v[u][2], v[u][3]};
+            rotate4(w, sg[u], lane);
+            store_operand_block(a_gu + (size_t)pos * H + kb * 128, lane, w);
+            rotate4(v[u], su[u], lane);
+            store_operand_block(a_gu + ((size_t)P + pos) * H + kb * 128, lane, v[u]);
+        }
     }
+}
+
+// The down projection's input rows from the gate and up outputs, in the operand's k order:
+// a = fp16(min(silu(g), L) * clamp(u, -L, L)) (no clamp when L = 0), a_dn[pos] = fp16(H(fp16(a * suh_down)) / sqrt(128)).
+static __global__ void __launch_bounds__(256) k_act(const __half* gu, int I, int P, const int* n_pos,
+                                                    const int* pair_expert, const ExpertDesc* experts,
+                                                    float act_limit, __half* a_dn) {
+    pdl_wait();
+    pdl_trigger();
+    const int KB = I / 128, lane = threadIdx.x & 31;
+    const long njobs = (long)min(P, __ldcg(n_pos)) * KB;
+    const long nw = ((long)gridDim.x * blockDim.x) >> 5;
+    for (long j0 = (((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kRotJobs; j0 < njobs; j0 += nw * kRotJobs) {
+        float g[kRotJobs][4], u4[kRotJobs][4], s[kRotJobs][4];
+#pragma unroll
+        for (int u = 0; u < kRotJobs; ++u) {
+            const long j = j0 + u;
+            if (j >= njobs) break;
+            const int pos = (int)(j / KB), kb = (int)(j % KB);
+            load4<__half>(gu + (size_t)pos * I + kb * 128 + 4 * lane, g[u]);
+            load4<__half>(gu + ((size_t)P + pos) * I + kb * 128 + 4 * lane, u4[u]);
+            const __half* sd = experts[__ldcg(pair_expert + pos)].suh[2];
+            if (sd) load4<__half>(sd + kb * 128 + 4 * lane, s[u]);
+            else s[u][0] = s[u][1] = s[u][2] = s[u][3] = 1.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < kRotJobs; ++u) {
+            const long j = j0 + u;
+            if (j >= njobs) break;
+            const int pos = (int)(j / KB), kb = (int)(j % KB);
+            float a[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float sg = silu_f(g[u][e]), uu = u4[u][e];
+                if (act_limit != 0.f) {
+                    sg = fminf(sg, act_limit);
+                    uu = fminf(fmaxf(uu, -act_limit), act_limit);
+                }
+                a[e] = __half2float(__float2half_rn(sg * uu));
+            }
+            rotate4(a, s[u], lane);
+            store_operand_block(a_dn + (size_t)pos * I + kb * 128, lane, a);
+        }
+    }
+}
+
+// Grid of the element-wise row kernels: warps enough for the jobs (kRotJobs per warp), at most 8 CTAs per SM.
+static dim3 row_grid(long jobs) {
+    long blocks = (jobs + 8L * kRotJobs - 1) / (8L * kRotJobs);
+    if (blocks > 8L * num_sms()) blocks = 8L * num_sms();
+    if (blocks < 1) blocks = 1;
+    return dim3((unsigned)blocks);
 }
 
 // ------------------------------------------------------------------------------------------------ host launch
@@ -597,9 +649,9 @@ using PFN_encode_tiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint3
                                       const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                       CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// Tensor map of a row-major [rows][cols] fp16 matrix: boxes of TC_BK columns x 256 rows, swizzled as the MMA
-// descriptors expect, zero fill.
-static int make_row_map(CUtensorMap* map, const __half* base, long rows, int cols, const char* what) {
+// Tensor map of a row-major [rows][cols] fp16 matrix: boxes of 64 columns x box_rows rows, 128-byte swizzle (the
+// MMA descriptors' layout), zero fill beyond the last row.
+static int make_row_map(CUtensorMap* map, const __half* base, long rows, int cols, int box_rows, const char* what) {
     static PFN_encode_tiled encode = nullptr;
     if (!encode) {
         void* fn = nullptr;
@@ -611,67 +663,81 @@ static int make_row_map(CUtensorMap* map, const __half* base, long rows, int col
     }
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {TC_BK, TC_BM};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     CUresult cr = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE,
-                         TC_BK == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     EXL3_REQUIRE(cr == CUDA_SUCCESS, EXL3_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)cr);
     return EXL3_OK;
 }
 
+// The two maps (128-row and 32-row boxes) of a [rows][cols] activation matrix.
+static int make_maps(CUtensorMap m[2], const __half* base, long rows, int cols, const char* what) {
+    int rc = make_row_map(&m[0], base, rows, cols, 128, what);
+    return rc ? rc : make_row_map(&m[1], base, rows, cols, TS_N2 / 2, what);
+}
+
 template <int EPI>
-static int launch_tc(const CUtensorMap& m0, const CUtensorMap& m1, const TcArgs& a, dim3 grid, cudaStream_t st,
-                     const char* what) {
+static int launch_pair(const TsMaps& maps, const TsArgs& a, dim3 grid, cudaStream_t st, const char* what) {
     static int configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !configured[dev]) {
-        EXL3_REQUIRE(cudaFuncSetAttribute(k_gemm_tc<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          TcSmem::total) == cudaSuccess,
+        EXL3_REQUIRE(cudaFuncSetAttribute(k_gemm_pair<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          TsSmem::total) == cudaSuccess,
                      EXL3_ERR_CUDA, "%s: cudaFuncSetAttribute: %s", what, cudaGetErrorString(cudaGetLastError()));
         configured[dev] = 1;
     }
-    cudaError_t e = launch_pdl(k_gemm_tc<EPI>, grid, dim3(TC_THREADS), TcSmem::total, st, m0, m1, a);
+    cudaError_t e = launch_pdl(k_gemm_pair<EPI>, grid, dim3(TS_THREADS), TsSmem::total, st, maps, a);
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
     return EXL3_OK;
 }
 
 int tc_moe_prefill(const TcMoeArgs& m, cudaStream_t st) {
     const char* what = "exl3_moe_prefill";
-    {
-        const long jobs = (long)m.P * 2 * (m.H / 128);
-        long blocks = (jobs + 7) / 8;
-        if (blocks > 8L * num_sms()) blocks = 8L * num_sms();
-        cudaError_t e = launch_pdl(k_rotate_pairs, dim3((unsigned)blocks), dim3(256), 0, st, m.x, m.ldx, m.x_bf16,
-                                   m.H, m.P, m.n_pos, m.pair_tok, m.pair_expert, m.experts, m.a_gu);
-        EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "%s: rotate launch failed: %s", what, cudaGetErrorString(e));
-    }
+    cudaError_t e;
+    const dim3 rg = row_grid((long)m.P * (m.H / 128));
+    if (m.x_bf16)
+        e = launch_pdl(k_rotate_pairs<__nv_bfloat16>, rg, dim3(256), 0, st,
+                       static_cast<const __nv_bfloat16*>(m.x), m.ldx, m.H, m.P, m.n_pos, m.pair_tok, m.pair_expert,
+                       m.experts, m.a_gu);
+    else
+        e = launch_pdl(k_rotate_pairs<__half>, rg, dim3(256), 0, st, static_cast<const __half*>(m.x), m.ldx, m.H,
+                       m.P, m.n_pos, m.pair_tok, m.pair_expert, m.experts, m.a_gu);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "%s: rotate launch failed: %s", what, cudaGetErrorString(e));
     if (m.max_items == 0) return EXL3_OK;
-    TcArgs a = {};
+    TsArgs a = {};
     a.n_items = m.n_items;
     a.item_expert = m.item_expert;
     a.item_start = m.item_start;
     a.item_cnt = m.item_cnt;
     a.pair_w = m.pair_w;
     a.experts = m.experts;
-    a.act_limit = m.act_limit;
-    a.a_dn = m.a_dn;
     a.ybuf = m.ybuf;
     a.status = device_status_ptr();
-    CUtensorMap mg, mu, md;
-    int rc = make_row_map(&mg, m.a_gu, m.P, m.H, what);
-    if (!rc) rc = make_row_map(&mu, m.a_gu + (size_t)m.P * m.H, m.P, m.H, what);
-    if (!rc) rc = make_row_map(&md, m.a_dn, m.P, m.I, what);
+    a.M = m.P;
+    TsMaps mgu, mdn;
+    int rc = make_maps(mgu.m[0], m.a_gu, m.P, m.H, what);
+    if (!rc) rc = make_maps(mgu.m[1], m.a_gu + (size_t)m.P * m.H, m.P, m.H, what);
+    if (!rc) rc = make_maps(mdn.m[0], m.a_dn, m.P, m.I, what);
     if (rc) return rc;
+    mdn.m[1][0] = mdn.m[0][0];
+    mdn.m[1][1] = mdn.m[0][1];
+    // gate and up: (I/256 rounded up) pairs per matrix, both matrices, into the gate/up buffer
     a.k = m.H;
     a.n = m.I;
-    rc = launch_tc<TC_GATEUP>(mg, mu, a, dim3(m.I / 128, m.max_items), st, what);
+    a.y = m.gu;
+    a.ldy = m.I;
+    rc = launch_pair<TC_GATEUP>(mgu, a, dim3(2 * 2 * ((m.I + 255) / 256), m.max_items), st, what);
     if (rc) return rc;
+    e = launch_pdl(k_act, row_grid((long)m.P * (m.I / 128)), dim3(256), 0, st, static_cast<const __half*>(m.gu), m.I,
+                   m.P, m.n_pos, m.pair_expert, m.experts, m.act_limit, m.a_dn);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "%s: activation launch failed: %s", what, cudaGetErrorString(e));
     a.k = m.I;
     a.n = m.H;
-    return launch_tc<TC_DOWN>(md, md, a, dim3((m.H + TC_BN - 1) / TC_BN, m.max_items), st, what);
+    a.y = nullptr;
+    return launch_pair<TC_DOWN>(mdn, a, dim3(2 * ((m.H + 255) / 256), m.max_items), st, what);
 }
 
 }  // namespace exl3
@@ -694,6 +760,8 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
                  "exl3_gemm_tc: k=%d, n=%d must be multiples of 128", k, n);
     EXL3_REQUIRE(x && packed && svh && y, EXL3_ERR_ARG, "exl3_gemm_tc: null pointer");
     EXL3_REQUIRE(aligned16(packed) && aligned16(y), EXL3_ERR_ARG, "exl3_gemm_tc: packed and y must be 16-byte aligned");
+    EXL3_REQUIRE(!suh || (reinterpret_cast<uintptr_t>(suh) & 7) == 0, EXL3_ERR_ARG,
+                 "exl3_gemm_tc: suh must be 8-byte aligned");
     EXL3_REQUIRE(x_dtype == EXL3_F16 || x_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "exl3_gemm_tc: x dtype %d",
                  x_dtype);
     EXL3_REQUIRE(y_dtype == EXL3_F16 || y_dtype == EXL3_BF16 || y_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED,
@@ -709,17 +777,23 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     __half* xh = static_cast<__half*>(workspace);
     {
-        const long jobs = (long)M * (k / 128);
-        long blocks = (jobs + 7) / 8;
-        if (blocks > 8L * num_sms()) blocks = 8L * num_sms();
-        cudaError_t e = launch_pdl(k_rotate_rows, dim3((unsigned)blocks), dim3(256), 0, st, x, ldx,
-                                   (int)(x_dtype == EXL3_BF16), M, k, static_cast<const __half*>(suh), xh);
+        const dim3 rg = row_grid((long)M * (k / 128));
+        const __half* s = static_cast<const __half*>(suh);
+        cudaError_t e;
+        if (x_dtype == EXL3_BF16)
+            e = launch_pdl(k_rotate_rows<__nv_bfloat16>, rg, dim3(256), 0, st, static_cast<const __nv_bfloat16*>(x),
+                           ldx, M, k, s, xh);
+        else
+            e = launch_pdl(k_rotate_rows<__half>, rg, dim3(256), 0, st, static_cast<const __half*>(x), ldx, M, k, s,
+                           xh);
         EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_gemm_tc: rotate launch failed: %s", cudaGetErrorString(e));
     }
-    CUtensorMap map;
-    int rc = make_row_map(&map, xh, M, k, "exl3_gemm_tc");
+    TsMaps maps;
+    int rc = make_maps(maps.m[0], xh, M, k, "exl3_gemm_tc");
     if (rc) return rc;
-    TcArgs a = {};
+    maps.m[1][0] = maps.m[0][0];
+    maps.m[1][1] = maps.m[0][1];
+    TsArgs a = {};
     a.packed = static_cast<const uint8_t*>(packed);
     a.svh = static_cast<const __half*>(svh);
     a.K = K;
@@ -730,8 +804,8 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
     a.k = k;
     a.n = n;
     a.status = device_status_ptr();
-    return launch_tc<TC_LINEAR>(map, map, a, dim3((n + TC_BN - 1) / TC_BN, (M + TC_BM - 1) / TC_BM), st,
-                                "exl3_gemm_tc");
+    return launch_pair<TC_LINEAR>(maps, a, dim3(2 * ((n + 255) / 256), (M + TS_TILE_ROWS - 1) / TS_TILE_ROWS), st,
+                                  "exl3_gemm_tc");
 }
 
 }  // extern "C"

@@ -574,18 +574,20 @@ static int run_combine(int M, int topk, int E, int shared, int H, int I, void* o
 
 // ------------------------------------------------------------------------------------------------ prefill
 
-// Workspace of exl3_moe_prefill: the alignment tables of ws_layout (items of <= 256 positions), then rotated gate/up
-// rows [2][P][H] fp16, the down projection's activation rows [P][I] fp16 and the weighted rows [P][H] fp32.
+// Workspace of exl3_moe_prefill: the alignment tables of ws_layout (items of <= kTcTileRows positions), then the
+// rotated gate/up input rows [2][P][H] fp16, the gate/up outputs [2][P][I] fp16, the down projection's input rows
+// [P][I] fp16 and the weighted rows [P][H] fp32.
 struct PrefillLayout {
     WsLayout t;
-    size_t a_gu, a_dn, ybuf, total;
+    size_t a_gu, gu, a_dn, ybuf, total;
 };
-constexpr int kPrefillItemRows = 256;
+constexpr int kPrefillItemRows = kTcTileRows;
 inline PrefillLayout prefill_layout(int M, int topk, int E, int H, int I, int shared) {
     PrefillLayout L;
     L.t = ws_layout(M, topk, E, H, I, shared, kPrefillItemRows);
     size_t o = L.t.xf_gu;
     L.a_gu = o; o += align_up((size_t)2 * L.t.p_max * H * 2, 256);
+    L.gu = o; o += align_up((size_t)2 * L.t.p_max * I * 2, 256);
     L.a_dn = o; o += align_up((size_t)L.t.p_max * I * 2, 256);
     L.ybuf = o; o += (size_t)L.t.p_max * H * 4;
     L.total = o;
@@ -641,6 +643,7 @@ int exl3_moe_prefill(const void* x, int x_dtype, int ldx, int M, const int32_t* 
     m.experts = reinterpret_cast<const ExpertDesc*>(experts);
     m.act_limit = act_limit;
     m.a_gu = reinterpret_cast<__half*>(ws + L.a_gu);
+    m.gu = reinterpret_cast<__half*>(ws + L.gu);
     m.a_dn = reinterpret_cast<__half*>(ws + L.a_dn);
     m.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
     rc = tc_moe_prefill(m, st);

@@ -8,9 +8,13 @@ namespace exl3 {
 
 enum { TC_LINEAR = 0, TC_GATEUP = 1, TC_DOWN = 2 };
 
-// The MoE prefill path after alignment: rotated gate/up input rows of every pair position, the grouped gate|up
-// projection (+ SiLU * clamp + the down input's rotation) and the grouped down projection (x routing weight) on the
-// tensor cores. Items hold at most 256 positions of one expert.
+// Activation rows of one tensor-core tile (a pair of SMs): the MoE prefill groups each expert's positions into items
+// of at most this many rows.
+constexpr int kTcTileRows = 320;
+
+// The MoE prefill path after alignment: rotated gate/up input rows of every pair position, the grouped gate and up
+// projections on the tensor cores, SiLU * clamp + the down input's rotation, and the grouped down projection
+// (x routing weight) on the tensor cores. Items hold at most kTcTileRows positions of one expert.
 struct TcMoeArgs {
     const void* x;
     int ldx, x_bf16;
@@ -27,8 +31,9 @@ struct TcMoeArgs {
     const float* pair_w;
     const ExpertDesc* experts;
     float act_limit;
-    __half* a_gu;                 // [2][P][H] fp16
-    __half* a_dn;                 // [P][I] fp16
+    __half* a_gu;                 // [2][P][H] fp16, rotated input rows (operand k order)
+    __half* gu;                   // [2][P][I] fp16, gate and up outputs
+    __half* a_dn;                 // [P][I] fp16, rotated down input rows (operand k order)
     float* ybuf;                  // [P][H] fp32
 };
 

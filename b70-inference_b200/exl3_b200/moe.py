@@ -70,6 +70,8 @@ class ExpertTable:
             for m in (ex.gate, ex.up, ex.down):
                 if m.trellis.data_ptr() % 16:
                     raise L.Exl3Error("ExpertTable: trellis tensors must be 16-byte aligned")
+                if m.suh.data_ptr() % 8 or m.svh.data_ptr() % 8:
+                    raise L.Exl3Error("ExpertTable: suh / svh tensors must be 8-byte aligned")
         if shared is not None and shared.gate.n != self.I:
             raise L.Exl3Error("ExpertTable: the shared expert must have the routed intermediate size "
                               "(run a wider shared expert as its own BC_GatedMLP)")
@@ -166,7 +168,7 @@ def moe_prefill(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, t
                 act_limit: float = 0.0, out_dtype=torch.float32, out: torch.Tensor | None = None,
                 workspace: torch.Tensor | None = None) -> torch.Tensor:
     """moe_forward for prefill-sized batches on the tensor cores (C ABI exl3_moe_prefill): the same contract, with
-    pairs grouped into items of <= 256 positions per expert and grouped tcgen05 GEMMs for the projections."""
+    pairs grouped into items of <= 320 positions per expert and grouped tcgen05 GEMMs for the projections."""
     L.require_cuda(x, topk_ids, topk_w)
     x2 = x.reshape(-1, x.shape[-1])
     if x2.dtype not in (torch.float16, torch.bfloat16):

@@ -106,8 +106,9 @@ EXL3_API int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* p
 
 /* ---- EXL3 linear, prefill sizes (tcgen05) ----
  * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for any M, on the 5th-generation tensor cores: trellis tiles decoded to
- * the reference's fp16 weights bit for bit into shared memory, tcgen05.mma kind::f16 with fp32 accumulation in
- * tensor memory, 512 x 128 output tiles. k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2; packed = exl3_pack.
+ * the reference's fp16 weights bit for bit straight into tensor memory, tcgen05.mma.cta_group::2 kind::f16 (weights
+ * from tensor memory, rotated activations from shared memory) with fp32 accumulation, 256 x 256 tiles per pair of
+ * SMs. k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2; packed = exl3_pack; suh 8-byte aligned.
  * workspace >= exl3_gemm_tc_workspace_size(M, k) bytes, 256-byte aligned (the rotated input rows).
  * Replaces the reconstruct + GEMM linear for M > 128 (glm/xpu/csrc/exl3_ops.sycl:539-555,651-757) and exllamav3
  * exl3_gemm's large-M shapes (glm/docs/ext-op-inventory.md:498-557). */
@@ -179,10 +180,11 @@ EXL3_API int exl3_moe_combine(int M, int topk, int E, int shared, int H, int I, 
 
 /* ---- MoE prefill (tcgen05) ----
  * The routed MoE layer for prefill-sized batches, same contract as exl3_moe_decode (out = slot-order sum of the
- * picks' expert outputs + shared expert). Pairs are grouped per expert into items of <= 256 positions; each
- * projection is a grouped tcgen05 GEMM (trellis decoded to bit-exact fp16 into shared memory, fp32 accumulation in
- * tensor memory): gate|up with SiLU * clamp and the down input's rotation fused in its epilogue, down with the
- * routing weight; then the fixed-order combine. workspace >= exl3_moe_prefill_workspace_size(...), 256-byte aligned.
+ * picks' expert outputs + shared expert). Pairs are grouped per expert into items of <= 320 positions; gate, up and
+ * down are grouped tcgen05 GEMMs (as exl3_gemm_tc: trellis decoded to bit-exact fp16 into tensor memory, fp32
+ * accumulation), gate and up with fp16 outputs, then SiLU * clamp and the down input's rotation, down with the
+ * routing weight; then the fixed-order combine. The experts' suh / svh vectors must be 8-byte aligned.
+ * workspace >= exl3_moe_prefill_workspace_size(...), 256-byte aligned.
  * Replaces the reference's MoE prefill (GateUpDpasKernel / DownDpasKernel / moe_prefill,
  * glm/xpu/csrc/exl3_moe.n128.sycl:422-690,868-916) and dsv_xpu moe_prefill_grouped
  * (dsv41/xpu/dsv_xpu/moe.py:1383-1448). */

@@ -1,6 +1,6 @@
 """GPU parity of the tcgen05 MoE prefill (exl3_moe_prefill): against the CPU oracle on a small batch and against
 the oracle-checked decode path (exl3_moe_decode) at prefill sizes; mixed bit widths per projection, shared expert,
-dropped picks, experts split into several 256-row items."""
+dropped picks, experts split into several 320-row items."""
 import numpy as np
 import pytest
 import torch
@@ -70,7 +70,7 @@ def test_moe_prefill_matches_oracle(shared):
 
 @pytest.mark.parametrize("M,E,topk,shared", [(600, 8, 4, True), (1100, 16, 8, False)])
 def test_moe_prefill_matches_decode_path(M, E, topk, shared):
-    """Hundreds of rows per expert (several 256-row items), against the decode kernels on the same inputs."""
+    """Hundreds of rows per expert (several 320-row items), against the decode kernels on the same inputs."""
     rng = np.random.default_rng(M + E)
     H, I, Lc = 512, 256, 10.0
     Ks = [(2, 3, 2) if e % 2 else (3, 2, 4) for e in range(E)]
