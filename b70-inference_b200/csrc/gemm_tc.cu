@@ -150,6 +150,15 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, uint32_t r[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Four fp16 values (8 bytes) widened to fp32.
+__device__ __forceinline__ void unpack_h4(uint2 u, float v[4]) {
+    const __half2 a = *reinterpret_cast<const __half2*>(&u.x), b = *reinterpret_cast<const __half2*>(&u.y);
+    v[0] = __low2float(a);
+    v[1] = __high2float(a);
+    v[2] = __low2float(b);
+    v[3] = __high2float(b);
+}
+
 // Shared-memory matrix descriptor of a [rows][64] fp16 sub-tile: canonical K-major layout, 128-byte swizzle, 8-row
 // atoms 1024 bytes apart, sm100 descriptor version 1.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
@@ -190,27 +199,34 @@ __device__ void ts_decoder_loop(uint8_t* smem, uint32_t tmem, int q, int j, int 
                                 int t_stages, uint32_t t_blk, uint64_t* t_full, uint64_t* t_empty, uint64_t* empty,
                                 uint32_t lead_a_full, bool& to) {
     const LaneWords lw = lane_words<K>(lane);
+    int ts = 0, s = 0;                                        // ring slots, advanced per chunk (no divisions)
+    uint32_t tph = 0, eph = 1;                                // parity awaited on t_full[ts] / on empty[s]
     for (int kc = 0; kc < nk; ++kc) {
-        const int ts = kc % t_stages, s = kc % TS_STAGES;
         bool ok = true;
-        if (has_cols && !to) ok = mbar_wait(&t_full[ts], (kc / t_stages) & 1);
-        if (ok && kc >= TS_STAGES && !to) ok = mbar_wait(&empty[s], ((kc / TS_STAGES) - 1) & 1);
+        if (has_cols && !to) ok = mbar_wait(&t_full[ts], tph);
+        if (ok && kc >= TS_STAGES && !to) ok = mbar_wait(&empty[s], eph);
         if (!__all_sync(0xFFFFFFFFu, ok)) to = true;
         if (has_cols && !to) {
-            const uint8_t* tst = smem + TsSmem::t0 + (size_t)ts * t_blk;
+            // all words of the chunk's tiles first, then the decodes, then the stores (the stores are ordered
+            // asm statements; loads issued after one would wait for it)
+            constexpr int NT = 2 * TS_KS;
+            const uint32_t* tst = reinterpret_cast<const uint32_t*>(smem + TsSmem::t0 + (size_t)ts * t_blk);
+            uint32_t w[NT][3];
 #pragma unroll
-            for (int si = 0; si < TS_KS; ++si) {
-                const int tr = j + 4 * si;
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint32_t a[4];
-                    decode_frag<K>(reinterpret_cast<const uint32_t*>(tst + (tr * 8 + 2 * q + h) * 32 * K), lw, a);
-                    // a = {n g, pair q'}, {n g+8, pair q'}, {n g, pair q'+4}, {n g+8, pair q'+4}
-                    tmem_st_16x256b(tmem + ((uint32_t)(32 * q + 16 * h) << 16) +
-                                        (uint32_t)(TS_A_COL0 + s * TS_A_COLS + tr * 8),
-                                    a[0], a[2], a[1], a[3]);
-                }
+            for (int t = 0; t < NT; ++t) {
+                const uint32_t* tile = tst + ((j + 4 * (t >> 1)) * 8 + 2 * q + (t & 1)) * 8 * K;
+                w[t][0] = tile[lw.i0];
+                w[t][1] = tile[lw.i1];
+                w[t][2] = K >= 3 ? tile[lw.i2] : 0u;          // K <= 2: the lane's bits span two words
             }
+            uint32_t a[NT][4];
+#pragma unroll
+            for (int t = 0; t < NT; ++t) decode_frag_words<K>(w[t][0], w[t][1], w[t][2], lw.off, a[t]);
+#pragma unroll
+            for (int t = 0; t < NT; ++t)   // a = {n g, pair q'}, {n g+8, pair q'}, {n g, pair q'+4}, {n g+8, pair q'+4}
+                tmem_st_16x256b(tmem + ((uint32_t)(32 * q + 16 * (t & 1)) << 16) +
+                                    (uint32_t)(TS_A_COL0 + s * TS_A_COLS + (j + 4 * (t >> 1)) * 8),
+                                a[t][0], a[t][2], a[t][1], a[t][3]);
         }
         tmem_wait_st();
         tc_fence_before();
@@ -219,6 +235,8 @@ __device__ void ts_decoder_loop(uint8_t* smem, uint32_t tmem, int q, int j, int 
             mbar_arrive_cluster(lead_a_full + 8u * s);
             if (has_cols) mbar_arrive(&t_empty[ts]);
         }
+        if (++ts == t_stages) { ts = 0; tph ^= 1u; }
+        if (++s == TS_STAGES) { s = 0; eph ^= 1u; }
     }
 }
 
@@ -347,9 +365,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TS_THREADS, 1)
             const uint32_t tx = 2u * TS_KS * (has2 ? TS_SUB : TS_SUB2);   // both CTAs' bytes of a stage
             int last[TS_STAGES];
             for (int s = 0; s < TS_STAGES; ++s) last[s] = -1;
-            for (int kc = 0; kc < nk; ++kc) {
-                const int s = kc % TS_STAGES;
-                if (kc >= TS_STAGES && !mbar_wait(&empty[s], ((kc / TS_STAGES) - 1) & 1)) { to = true; break; }
+            int s = 0;
+            uint32_t eph = 1;
+            for (int kc = 0; kc < nk; ++kc, s = s + 1 == TS_STAGES ? 0 : s + 1, eph ^= (s == 0)) {
+                if (kc >= TS_STAGES && !mbar_wait(&empty[s], eph)) { to = true; break; }
                 if (rank == 0) mbar_expect_tx(&b_full[s], tx);
                 uint8_t* dst = smem + TsSmem::b0 + s * TS_B_STAGE;
 #pragma unroll
@@ -369,12 +388,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TS_THREADS, 1)
         // ---------------- MMA issue (leader, one lane) ----------------
         if (rank == 0 && lane == 0) {
             constexpr uint32_t idesc1 = tc_idesc_f16(256, 256), idesc2 = tc_idesc_f16(256, TS_N2);
-            for (int kc = 0; kc < nk; ++kc) {
-                const int s = kc % TS_STAGES;
-                const uint32_t ph = (kc / TS_STAGES) & 1;
+            int s = 0;
+            uint32_t ph = 0;
+            for (int kc = 0; kc < nk; ++kc, s = s + 1 == TS_STAGES ? 0 : s + 1, ph ^= (s == 0)) {
+                // no tcgen05 fence per chunk: the decoders complete their tensor-memory stores (tcgen05.wait::st)
+                // before arriving, and a fence here would hold the MMAs until the queue drains every chunk
                 if (!to && !mbar_wait(&a_full[s], ph)) to = true;
                 if (!to && !mbar_wait(&b_full[s], ph)) to = true;
-                tc_fence_after();
                 if (!to) {
                     const uint32_t b_base = smem_u32(smem + TsSmem::b0 + s * TS_B_STAGE);
 #pragma unroll
@@ -395,9 +415,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TS_THREADS, 1)
             int last[TS_MAX_TSTAGES];
             for (int s = 0; s < TS_MAX_TSTAGES; ++s) last[s] = -1;
             const uint32_t tile_row_bytes = (uint32_t)(8 * 32 * Kw);
-            for (int kc = 0; kc < nk; ++kc) {
-                const int ts = kc % t_stages;
-                if (kc >= t_stages && !mbar_wait(&t_empty[ts], ((kc / t_stages) - 1) & 1)) { to = true; break; }
+            int ts = 0;
+            uint32_t eph = 1;
+            for (int kc = 0; kc < nk; ++kc, ts = ts + 1 == t_stages ? 0 : ts + 1, eph ^= (ts == 0)) {
+                if (kc >= t_stages && !mbar_wait(&t_empty[ts], eph)) { to = true; break; }
                 mbar_expect_tx(&t_full[ts], t_blk);
                 uint8_t* dst = smem + TsSmem::t0 + (size_t)ts * t_blk;
                 if constexpr (EPI == TC_GATEUP) {
@@ -426,6 +447,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TS_THREADS, 1)
         // staging [128 rows][128 features]
         float* stage = reinterpret_cast<float*>(smem + TsSmem::b0);
         const int col = cb * 128 + 4 * lane;                  // output feature of the projection
+        // per-lane constants of the epilogue, loaded once: the lane's svh values and (down) the routing weights of
+        // the warp's rows (row dw + 16 i in lane i)
+        float sv[4] = {0.f, 0.f, 0.f, 0.f};
+        float wrow = 0.f;
+        if (has_cols) {
+            const uint2 u = __ldg(reinterpret_cast<const uint2*>(svh + col));
+            unpack_h4(u, sv);
+        }
+        if constexpr (EPI == TC_DOWN)
+            if (dw + TS_DEC_WARPS * lane < rows) wrow = __ldcg(p.pair_w + m0 + dw + TS_DEC_WARPS * lane);
         for (int r0 = 0; r0 < rows; r0 += 128) {               // rows is uniform: every warp takes each barrier
             if (!to && r0 + 32 * j < rows) {
                 uint32_t r[32];
@@ -440,21 +471,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TS_THREADS, 1)
                 fwht128_warp(v, lane);
                 const int m = m0 + t;
                 if constexpr (EPI == TC_DOWN) {
-                    const float wgt = __ldcg(p.pair_w + m);
+                    const float wgt = __shfl_sync(0xFFFFFFFFu, wrow, (t - dw) / TS_DEC_WARPS);
                     float o[4];
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) o[e] = wgt * (v[e] * kRsqrt128 * __half2float(svh[col + e]));
+                    for (int e = 0; e < 4; ++e) o[e] = wgt * (v[e] * kRsqrt128 * sv[e]);
                     *reinterpret_cast<float4*>(p.ybuf + (size_t)m * p.n + col) = make_float4(o[0], o[1], o[2], o[3]);
                 } else {
                     const int ydt = EPI == TC_GATEUP ? EXL3_F16 : p.y_dtype;
                     float o[4];
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const float sv = __half2float(svh[col + e]);
                         if (ydt == EXL3_F16)
-                            o[e] = __half2float(__float2half_rn(__half2float(__float2half_rn(v[e] * kRsqrt128)) * sv));
+                            o[e] = __half2float(__float2half_rn(__half2float(__float2half_rn(v[e] * kRsqrt128)) * sv[e]));
                         else
-                            o[e] = v[e] * kRsqrt128 * sv;
+                            o[e] = v[e] * kRsqrt128 * sv[e];
                     }
                     const size_t yrow = (EPI == TC_GATEUP ? (size_t)mat * p.M : 0) + (size_t)m;
                     if (ydt == EXL3_F32) {
@@ -488,157 +518,181 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(TS_THREADS, 1)
 
 // ------------------------------------------------------------------------------------------------ activation rows
 
-// Store the lane's 4 values of a 128-block (k = 4l..4l+3) as fp16 in the operand's k order: inside each 16-element
-// group, k pair p goes to pair slot p < 4 ? 2p : 2p - 7 (lane l holds pairs 2i, 2i+1 of group l/4, i = l % 4).
-__device__ __forceinline__ void store_operand_block(__half* blk, int lane, const float v[4]) {
-    const int i = lane & 3;
-    const int slot = i < 2 ? 4 * i : 4 * i - 7;
-    uint32_t* d = reinterpret_cast<uint32_t*>(blk) + (lane >> 2) * 8 + slot;
-    __half2 h01 = __floats2half2_rn(v[0], v[1]), h23 = __floats2half2_rn(v[2], v[3]);
-    d[0] = *reinterpret_cast<uint32_t*>(&h01);
-    d[2] = *reinterpret_cast<uint32_t*>(&h23);
-}
-// The lane's 4 consecutive 16-bit values (8-byte aligned) widened to fp32.
+// A 128-element block lives in a lane quad: lane i = lane % 4 holds elements 32 i .. 32 i + 31, so a warp works on 8
+// blocks at once (8 consecutive blocks of one row) and only the last two of the seven Hadamard stages cross lanes.
+constexpr int kQuadBlocks = 8;                                // blocks per warp (one per quad)
+constexpr uint2 kOnes4 = {0x3C003C00u, 0x3C003C00u};          // four fp16 ones (a missing sign vector)
+
 template <typename T>
-__device__ __forceinline__ void load4(const T* src, float v[4]) {
-    const uint2 u = __ldg(reinterpret_cast<const uint2*>(src));
+__device__ __forceinline__ void unpack4(uint2 u, float* v) {
     const T* e = reinterpret_cast<const T*>(&u);
 #pragma unroll
     for (int j = 0; j < 4; ++j) v[j] = to_f32<T>(e[j]);
 }
-// xh = fp16(H(fp16(x * suh)) / sqrt(128)) for one 128-block, the lane's 4 values (x and suh already loaded).
-__device__ __forceinline__ void rotate4(float v[4], const float s[4], int lane) {
+// The lane's 32 consecutive 16-bit values (8-byte aligned) as 8 raw 8-byte words; `ones` when src is null.
+__device__ __forceinline__ void load32_raw(const void* src, uint2 r[8]) {
+    const uint2* p = reinterpret_cast<const uint2*>(src);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = __half2float(__float2half_rn(v[j] * s[j]));
-    fwht128_warp(v, lane);
+    for (int c = 0; c < 8; ++c) r[c] = p ? __ldg(p + c) : kOnes4;
+}
+__device__ __forceinline__ void load32_raw_cg(const void* src, uint2 r[8]) {
+    const uint2* p = reinterpret_cast<const uint2*>(src);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = __half2float(__float2half_rn(v[j] * kRsqrt128));
+    for (int c = 0; c < 8; ++c) r[c] = __ldcg(p + c);
 }
 
-constexpr int kRotJobs = 4;                                   // 128-blocks in flight per warp
+// 128-point Walsh-Hadamard transform of a quad's block: stages h = 1 .. 16 inside the lane, h = 32 and 64 across
+// the quad (lane xor 1, 2); the natural stage order with (a, b) -> (a + b, a - b) in fp32, as fwht128_warp.
+__device__ __forceinline__ void fwht128_quad(float v[32], int lane) {
+#pragma unroll
+    for (int h = 1; h < 32; h <<= 1)
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+            if ((e & h) == 0) {
+                const float a = v[e], b = v[e + h];
+                v[e] = a + b;
+                v[e + h] = a - b;
+            }
+#pragma unroll
+    for (int m = 1; m < 4; m <<= 1) {
+        const float sgn = (lane & m) ? -1.0f : 1.0f;      // fma(v, -1, p) = p - v, fma(v, 1, p) = v + p
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] = fmaf(v[e], sgn, __shfl_xor_sync(0xFFFFFFFFu, v[e], m));
+    }
+}
 
-// Rotated input rows of the dense linear, in the operand's k order: xh[m][k].
+// xh = fp16(H(fp16(v * s)) / sqrt(128)) for the quad's block (v: the lane's 32 values, s: its 32 signs), stored at
+// dst (the lane's 32 elements, 16-byte aligned) in the operand's k order: inside each 16-element group, k pair p goes
+// to pair slot p < 4 ? 2p : 2p - 7, i.e. the group's pair words in the order 0 4 1 5 2 6 3 7. `store` is per lane;
+// every lane of the warp must call this (the transform shuffles).
+__device__ __forceinline__ void rotate_store32(float v[32], const uint2 sraw[8], int lane, __half* dst, bool store) {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+        float sg[4];
+        unpack4<__half>(sraw[c], sg);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[4 * c + j] = __half2float(__float2half_rn(v[4 * c + j] * sg[j]));
+    }
+    fwht128_quad(v, lane);
+    if (!store) return;
+    uint32_t w[16];
+#pragma unroll
+    for (int pp = 0; pp < 16; ++pp) {
+        const __half2 h = __floats2half2_rn(v[2 * pp] * kRsqrt128, v[2 * pp + 1] * kRsqrt128);
+        w[pp] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int g = 0; g < 2; ++g) {
+        const uint32_t* P = w + 8 * g;
+        d[2 * g] = make_uint4(P[0], P[4], P[1], P[5]);
+        d[2 * g + 1] = make_uint4(P[2], P[6], P[3], P[7]);
+    }
+}
+
+// Rotated input rows of the dense linear, in the operand's k order: xh[m][k]. One warp per (row, 8 blocks).
 template <typename T>
-static __global__ void __launch_bounds__(256) k_rotate_rows(const T* x, int ldx, int M, int k, const __half* suh,
-                                                            __half* xh) {
+static __global__ void __launch_bounds__(256, 2) k_rotate_rows(const T* x, int ldx, int M, int k, const __half* suh,
+                                                               __half* xh) {
     pdl_wait();
     pdl_trigger();
-    const int KB = k / 128, lane = threadIdx.x & 31;
-    const long njobs = (long)M * KB;
+    const int KB = k / 128, lane = threadIdx.x & 31, i = lane & 3;
+    const int nkg = (KB + kQuadBlocks - 1) / kQuadBlocks;
+    const long njobs = (long)M * nkg;
     const long nw = ((long)gridDim.x * blockDim.x) >> 5;
-    for (long j0 = (((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kRotJobs; j0 < njobs; j0 += nw * kRotJobs) {
-        float v[kRotJobs][4], s[kRotJobs][4];
+    for (long job = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; job < njobs; job += nw) {
+        const int row = (int)(job / nkg), kb = (int)(job % nkg) * kQuadBlocks + (lane >> 2);
+        const bool act = kb < KB;
+        const int off = (act ? kb : 0) * 128 + 32 * i;
+        uint2 xr[8], sr[8];
+        load32_raw(x + (size_t)row * ldx + off, xr);
+        load32_raw(suh ? suh + off : nullptr, sr);
+        float v[32];
 #pragma unroll
-        for (int u = 0; u < kRotJobs; ++u) {
-            const long j = j0 + u;
-            if (j >= njobs) break;
-            const int row = (int)(j / KB), kb = (int)(j % KB);
-            load4<T>(x + (size_t)row * ldx + kb * 128 + 4 * lane, v[u]);
-            if (suh)
-                load4<__half>(suh + kb * 128 + 4 * lane, s[u]);
-            else
-                s[u][0] = s[u][1] = s[u][2] = s[u][3] = 1.0f;
-        }
-#pragma unroll
-        for (int u = 0; u < kRotJobs; ++u) {
-            const long j = j0 + u;
-            if (j >= njobs) break;
-            const int row = (int)(j / KB), kb = (int)(j % KB);
-            rotate4(v[u], s[u], lane);
-            store_operand_block(xh + (size_t)row * k + kb * 128, lane, v[u]);
-        }
+        for (int c = 0; c < 8; ++c) unpack4<T>(xr[c], v + 4 * c);
+        rotate_store32(v, sr, lane, xh + (size_t)row * k + off, act);
     }
 }
 
 // Rotated gate and up input rows of every pair position, in the operand's k order: a_gu[mat][pos][H] =
-// rot(x[token] * suh of the position's expert's matrix mat). The token's block is loaded once for both matrices.
+// rot(x[token] * suh of the position's expert's matrix mat). One warp per (position, 8 blocks); the token's values
+// are loaded once for both matrices.
 template <typename T>
-static __global__ void __launch_bounds__(256) k_rotate_pairs(const T* x, int ldx, int H, int P, const int* n_pos,
-                                                             const int* pair_tok, const int* pair_expert,
-                                                             const ExpertDesc* experts, __half* a_gu) {
+static __global__ void __launch_bounds__(256, 2) k_rotate_pairs(const T* x, int ldx, int H, int P, const int* n_pos,
+                                                                const int* pair_tok, const int* pair_expert,
+                                                                const ExpertDesc* experts, __half* a_gu) {
     pdl_wait();
     pdl_trigger();
-    const int KB = H / 128, lane = threadIdx.x & 31;
-    const long njobs = (long)min(P, __ldcg(n_pos)) * KB;
+    const int KB = H / 128, lane = threadIdx.x & 31, i = lane & 3;
+    const int nkg = (KB + kQuadBlocks - 1) / kQuadBlocks;
+    const long njobs = (long)min(P, __ldcg(n_pos)) * nkg;
     const long nw = ((long)gridDim.x * blockDim.x) >> 5;
-    for (long j0 = (((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kRotJobs; j0 < njobs; j0 += nw * kRotJobs) {
-        float v[kRotJobs][4], sg[kRotJobs][4], su[kRotJobs][4];
+    for (long job = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; job < njobs; job += nw) {
+        const int pos = (int)(job / nkg), kb = (int)(job % nkg) * kQuadBlocks + (lane >> 2);
+        const bool act = kb < KB;
+        const int off = (act ? kb : 0) * 128 + 32 * i;
+        const int tok = __ldcg(pair_tok + pos), e = __ldcg(pair_expert + pos);
+        const __half* s0 = experts[e].suh[0];
+        const __half* s1 = experts[e].suh[1];
+        uint2 xr[8], gr[8], ur[8];
+        load32_raw(x + (size_t)tok * ldx + off, xr);
+        load32_raw(s0 ? s0 + off : nullptr, gr);
+        load32_raw(s1 ? s1 + off : nullptr, ur);
+        float v[32];
 #pragma unroll
-        for (int u = 0; u < kRotJobs; ++u) {
-            const long j = j0 + u;
-            if (j >= njobs) break;
-            const int pos = (int)(j / KB), kb = (int)(j % KB);
-            const int tok = __ldcg(pair_tok + pos), e = __ldcg(pair_expert + pos);
-            load4<T>(x + (size_t)tok * ldx + kb * 128 + 4 * lane, v[u]);
-            const __half* s0 = experts[e].suh[0];
-            const __half* s1 = experts[e].suh[1];
-            if (s0) load4<__half>(s0 + kb * 128 + 4 * lane, sg[u]);
-            else sg[u][0] = sg[u][1] = sg[u][2] = sg[u][3] = 1.0f;
-            if (s1) load4<__half>(s1 + kb * 128 + 4 * lane, su[u]);
-            else su[u][0] = su[u][1] = su[u][2] = su[u][3] = 1.0f;
-        }
+        for (int c = 0; c < 8; ++c) unpack4<T>(xr[c], v + 4 * c);
+        rotate_store32(v, gr, lane, a_gu + (size_t)pos * H + off, act);
 #pragma unroll
-        for (int u = 0; u < kRotJobs; ++u) {
-            const long j = j0 + u;
-            if (j >= njobs) break;
-            const int pos = (int)(j / KB), kb = (int)(j % KB);
-            float w[4] = {v[u][0], v[u][1], v[u][2], v[u][3]};
-            rotate4(w, sg[u], lane);
-            store_operand_block(a_gu + (size_t)pos * H + kb * 128, lane, w);
-            rotate4(v[u], su[u], lane);
-            store_operand_block(a_gu + ((size_t)P + pos) * H + kb * 128, lane, v[u]);
-        }
+        for (int c = 0; c < 8; ++c) unpack4<T>(xr[c], v + 4 * c);
+        rotate_store32(v, ur, lane, a_gu + ((size_t)P + pos) * H + off, act);
     }
 }
 
 // The down projection's input rows from the gate and up outputs, in the operand's k order:
 // a = fp16(min(silu(g), L) * clamp(u, -L, L)) (no clamp when L = 0), a_dn[pos] = fp16(H(fp16(a * suh_down)) / sqrt(128)).
-static __global__ void __launch_bounds__(256) k_act(const __half* gu, int I, int P, const int* n_pos,
-                                                    const int* pair_expert, const ExpertDesc* experts,
-                                                    float act_limit, __half* a_dn) {
+// One warp per (position, 8 blocks).
+static __global__ void __launch_bounds__(256, 2) k_act(const __half* gu, int I, int P, const int* n_pos,
+                                                       const int* pair_expert, const ExpertDesc* experts,
+                                                       float act_limit, __half* a_dn) {
     pdl_wait();
     pdl_trigger();
-    const int KB = I / 128, lane = threadIdx.x & 31;
-    const long njobs = (long)min(P, __ldcg(n_pos)) * KB;
+    const int KB = I / 128, lane = threadIdx.x & 31, i = lane & 3;
+    const int nkg = (KB + kQuadBlocks - 1) / kQuadBlocks;
+    const long njobs = (long)min(P, __ldcg(n_pos)) * nkg;
     const long nw = ((long)gridDim.x * blockDim.x) >> 5;
-    for (long j0 = (((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5) * kRotJobs; j0 < njobs; j0 += nw * kRotJobs) {
-        float g[kRotJobs][4], u4[kRotJobs][4], s[kRotJobs][4];
+    for (long job = ((long)blockIdx.x * blockDim.x + threadIdx.x) >> 5; job < njobs; job += nw) {
+        const int pos = (int)(job / nkg), kb = (int)(job % nkg) * kQuadBlocks + (lane >> 2);
+        const bool act = kb < KB;
+        const int off = (act ? kb : 0) * 128 + 32 * i;
+        const __half* sd = experts[__ldcg(pair_expert + pos)].suh[2];
+        uint2 gr[8], ur[8], sr[8];
+        load32_raw_cg(gu + (size_t)pos * I + off, gr);
+        load32_raw_cg(gu + ((size_t)P + pos) * I + off, ur);
+        load32_raw(sd ? sd + off : nullptr, sr);
+        float v[32];
 #pragma unroll
-        for (int u = 0; u < kRotJobs; ++u) {
-            const long j = j0 + u;
-            if (j >= njobs) break;
-            const int pos = (int)(j / KB), kb = (int)(j % KB);
-            load4<__half>(gu + (size_t)pos * I + kb * 128 + 4 * lane, g[u]);
-            load4<__half>(gu + ((size_t)P + pos) * I + kb * 128 + 4 * lane, u4[u]);
-            const __half* sd = experts[__ldcg(pair_expert + pos)].suh[2];
-            if (sd) load4<__half>(sd + kb * 128 + 4 * lane, s[u]);
-            else s[u][0] = s[u][1] = s[u][2] = s[u][3] = 1.0f;
-        }
+        for (int c = 0; c < 8; ++c) {
+            float g[4], u[4];
+            unpack4<__half>(gr[c], g);
+            unpack4<__half>(ur[c], u);
 #pragma unroll
-        for (int u = 0; u < kRotJobs; ++u) {
-            const long j = j0 + u;
-            if (j >= njobs) break;
-            const int pos = (int)(j / KB), kb = (int)(j % KB);
-            float a[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                float sg = silu_f(g[u][e]), uu = u4[u][e];
+            for (int j = 0; j < 4; ++j) {
+                float sg = silu_f(g[j]), uu = u[j];
                 if (act_limit != 0.f) {
                     sg = fminf(sg, act_limit);
                     uu = fminf(fmaxf(uu, -act_limit), act_limit);
                 }
-                a[e] = __half2float(__float2half_rn(sg * uu));
+                v[4 * c + j] = __half2float(__float2half_rn(sg * uu));
             }
-            rotate4(a, s[u], lane);
-            store_operand_block(a_dn + (size_t)pos * I + kb * 128, lane, a);
         }
+        rotate_store32(v, sr, lane, a_dn + (size_t)pos * I + off, act);
     }
 }
 
-// Grid of the element-wise row kernels: warps enough for the jobs (kRotJobs per warp), at most 8 CTAs per SM.
+// Grid of the element-wise kernels: one warp per job, up to 2 CTAs of 8 warps per SM resident.
 static dim3 row_grid(long jobs) {
-    long blocks = (jobs + 8L * kRotJobs - 1) / (8L * kRotJobs);
-    if (blocks > 8L * num_sms()) blocks = 8L * num_sms();
+    long blocks = (jobs + 7) / 8;
+    if (blocks > 4L * num_sms()) blocks = 4L * num_sms();
     if (blocks < 1) blocks = 1;
     return dim3((unsigned)blocks);
 }
@@ -697,7 +751,7 @@ static int launch_pair(const TsMaps& maps, const TsArgs& a, dim3 grid, cudaStrea
 int tc_moe_prefill(const TcMoeArgs& m, cudaStream_t st) {
     const char* what = "exl3_moe_prefill";
     cudaError_t e;
-    const dim3 rg = row_grid((long)m.P * (m.H / 128));
+    const dim3 rg = row_grid((long)m.P * ((m.H / 128 + kQuadBlocks - 1) / kQuadBlocks));
     if (m.x_bf16)
         e = launch_pdl(k_rotate_pairs<__nv_bfloat16>, rg, dim3(256), 0, st,
                        static_cast<const __nv_bfloat16*>(m.x), m.ldx, m.H, m.P, m.n_pos, m.pair_tok, m.pair_expert,
@@ -731,8 +785,8 @@ int tc_moe_prefill(const TcMoeArgs& m, cudaStream_t st) {
     a.ldy = m.I;
     rc = launch_pair<TC_GATEUP>(mgu, a, dim3(2 * 2 * ((m.I + 255) / 256), m.max_items), st, what);
     if (rc) return rc;
-    e = launch_pdl(k_act, row_grid((long)m.P * (m.I / 128)), dim3(256), 0, st, static_cast<const __half*>(m.gu), m.I,
-                   m.P, m.n_pos, m.pair_expert, m.experts, m.act_limit, m.a_dn);
+    e = launch_pdl(k_act, row_grid((long)m.P * ((m.I / 128 + kQuadBlocks - 1) / kQuadBlocks)), dim3(256), 0, st,
+                   static_cast<const __half*>(m.gu), m.I, m.P, m.n_pos, m.pair_expert, m.experts, m.act_limit, m.a_dn);
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "%s: activation launch failed: %s", what, cudaGetErrorString(e));
     a.k = m.I;
     a.n = m.H;
@@ -760,8 +814,8 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
                  "exl3_gemm_tc: k=%d, n=%d must be multiples of 128", k, n);
     EXL3_REQUIRE(x && packed && svh && y, EXL3_ERR_ARG, "exl3_gemm_tc: null pointer");
     EXL3_REQUIRE(aligned16(packed) && aligned16(y), EXL3_ERR_ARG, "exl3_gemm_tc: packed and y must be 16-byte aligned");
-    EXL3_REQUIRE(!suh || (reinterpret_cast<uintptr_t>(suh) & 7) == 0, EXL3_ERR_ARG,
-                 "exl3_gemm_tc: suh must be 8-byte aligned");
+    EXL3_REQUIRE((!suh || (reinterpret_cast<uintptr_t>(suh) & 7) == 0) && (reinterpret_cast<uintptr_t>(svh) & 7) == 0,
+                 EXL3_ERR_ARG, "exl3_gemm_tc: suh and svh must be 8-byte aligned");
     EXL3_REQUIRE(x_dtype == EXL3_F16 || x_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "exl3_gemm_tc: x dtype %d",
                  x_dtype);
     EXL3_REQUIRE(y_dtype == EXL3_F16 || y_dtype == EXL3_BF16 || y_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED,
@@ -777,7 +831,7 @@ int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void* packed,
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     __half* xh = static_cast<__half*>(workspace);
     {
-        const dim3 rg = row_grid((long)M * (k / 128));
+        const dim3 rg = row_grid((long)M * ((k / 128 + kQuadBlocks - 1) / kQuadBlocks));
         const __half* s = static_cast<const __half*>(suh);
         cudaError_t e;
         if (x_dtype == EXL3_BF16)

@@ -232,7 +232,9 @@ __device__ __forceinline__ void consume_k(int K, float d[TPW][4], const uint8_t*
 #undef EXL3_CONSUME
 }
 
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + expf(-g)); }
+// silu(g) = g / (1 + e^-g), fp32 with the fast exponential and division intrinsics (relative error ~1e-6, far below
+// the fp16 rounding of the activation that follows; g -> -inf gives -0).
+__device__ __forceinline__ float silu_f(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
 // What a unit needs: packed weights of its column block, bit widths, rows, and the activation row of each MMA
 // column (linear: row g; gate|up: the pair's source row; down: the pair position).

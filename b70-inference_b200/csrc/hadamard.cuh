@@ -15,14 +15,15 @@ __device__ __forceinline__ void fwht128_warp(float v[4], int lane) {
     v[1] = a1 + a3;
     v[2] = a0 - a2;
     v[3] = a1 - a3;
-    // h = 4 .. 64 across lanes: partner = lane ^ (h / 4)
+    // h = 4 .. 64 across lanes: partner = lane ^ (h / 4). The butterfly is one fma with a +-1 factor:
+    // fma(v, -1, p) = p - v and fma(v, 1, p) = v + p, each rounded once, as the subtraction / addition.
 #pragma unroll
     for (int m = 1; m < 32; m <<= 1) {
-        const bool upper = (lane & m) != 0;
+        const float sgn = (lane & m) ? -1.0f : 1.0f;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            float p = __shfl_xor_sync(0xFFFFFFFFu, v[j], m);
-            v[j] = upper ? (p - v[j]) : (v[j] + p);
+            const float p = __shfl_xor_sync(0xFFFFFFFFu, v[j], m);
+            v[j] = fmaf(v[j], sgn, p);
         }
     }
 }

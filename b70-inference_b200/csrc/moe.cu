@@ -18,10 +18,12 @@ namespace exl3 {
 inline int item_rows(int M) { return M < 8 ? (M > 0 ? M : 1) : 8; }
 
 struct WsLayout {
-    size_t item_expert, item_start, item_cnt, pair_tok, pair_expert, pair_of, pair_w, pair_src, tickets, xf_gu,
-        xf_dn, ybuf, partial, total;
+    size_t item_expert, item_start, item_cnt, pair_tok, pair_expert, pair_of, pair_w, pair_src, tickets, seg_cnt,
+        xf_gu, xf_dn, ybuf, partial, total;
     int max_items, p_max, n_tickets;
 };
+
+constexpr int kAlignSegPairs = 8192;                            // pairs per CTA of the multi-CTA alignment
 
 inline WsLayout ws_layout(int M, int topk, int E, int H, int I, int shared, int chunk) {
     WsLayout L;
@@ -41,6 +43,7 @@ inline WsLayout ws_layout(int M, int topk, int E, int H, int I, int shared, int 
     L.pair_w = o; o += (size_t)L.p_max * 4;
     L.pair_src = o; o += (size_t)L.p_max * 4;
     L.tickets = o; o += (size_t)L.n_tickets * 4;
+    L.seg_cnt = o; o += (size_t)((npairs + kAlignSegPairs - 1) / kAlignSegPairs) * E * 4;   // multi-CTA alignment
     o = align_up(o, 256);
     L.xf_gu = o; o += align_up((size_t)L.p_max * 2 * H * 2, 256);
     L.xf_dn = o; o += align_up((size_t)L.p_max * I * 2, 256);
@@ -206,48 +209,12 @@ struct AlignOut {
     int* pair_src;
 };
 
-// One CTA. Pairs are split into 32 contiguous warp segments; per-(warp, expert) counts give every pair a stable
-// position (experts ascending, pair index ascending within an expert): deterministic, unlike an atomic fill
-// (glm/xpu/csrc/exl3_moe.n128.sycl:693-734 fills positions in atomic order). Items: ceil(count / chunk) per active
-// expert in expert order, then the shared expert's rows (expert id E, weight 1) at positions n_valid + m.
-// pair_src[position] = the routed pair index (the gate|up activation row), npairs + m for shared rows.
-__device__ void align_cta(const int32_t* __restrict__ ids, const float* __restrict__ w, int npairs, int topk, int E,
-                          int M, int shared, int chunk, const AlignOut& o, int* sm) {
-    int* cnt = sm;                             // [kAlignWarps][E]
-    int* scan = sm + kAlignWarps * E;          // [kAlignThreads]
-    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
-    for (int i = t; i < kAlignWarps * E; i += kAlignThreads) cnt[i] = 0;
-    __syncthreads();
-    const int seg = (npairs + kAlignWarps - 1) / kAlignWarps;
-    const int a0 = min(npairs, warp * seg), a1 = min(npairs, a0 + seg);
-    for (int i = a0 + lane; i < a1; i += 32) {
-        const int e = ids[i];
-        if (e >= 0 && e < E) atomicAdd(&cnt[warp * E + e], 1);
-    }
-    __syncthreads();
-    int total = 0;
-    if (t < E)
-        for (int ww = 0; ww < kAlignWarps; ++ww) total += cnt[ww * E + t];
-    const int nch = (total + chunk - 1) / chunk;
-    int n_valid = 0, n_routed_items = 0;
-    const int start = block_excl_scan(total, scan, &n_valid);
-    if (t < E) {
-        int run = start;
-        for (int ww = 0; ww < kAlignWarps; ++ww) {
-            const int c = cnt[ww * E + t];
-            cnt[ww * E + t] = run;
-            run += c;
-        }
-    }
-    const int ibase = block_excl_scan(nch, scan, &n_routed_items);
-    const int shared_items = shared ? (M + chunk - 1) / chunk : 0;
-    if (t == 0) {
-        o.ws_i[0] = n_routed_items + shared_items;
-        o.ws_i[1] = n_valid;
-        o.ws_i[2] = n_valid + (shared ? M : 0);
-    }
-    __syncthreads();
-    // stable placement: each warp walks its segment in order, 32 pairs at a time
+// Stable placement of the pairs [a0, a1) of one warp: cnt_w[e] is the warp's next position for expert e (experts
+// ascending, pair index ascending within an expert). Deterministic, unlike an atomic fill
+// (glm/xpu/csrc/exl3_moe.n128.sycl:693-734 fills positions in atomic order).
+__device__ void place_pairs(const int32_t* __restrict__ ids, const float* __restrict__ w, int topk, int E, int a0,
+                            int a1, int* cnt_w, const AlignOut& o) {
+    const int lane = threadIdx.x & 31;
     for (int base = a0; base < a1; base += 32) {
         const int i = base + lane;
         const bool act = i < a1;
@@ -258,7 +225,7 @@ __device__ void align_cta(const int32_t* __restrict__ ids, const float* __restri
             const unsigned peers = __match_any_sync(amask, valid ? e : -1);
             const unsigned before = peers & ((1u << lane) - 1u);
             if (valid) {
-                const int pos = cnt[warp * E + e] + __popc(before);
+                const int pos = cnt_w[e] + __popc(before);
                 o.pair_tok[pos] = i / topk;
                 o.pair_expert[pos] = e;
                 o.pair_w[pos] = w[i];
@@ -268,9 +235,26 @@ __device__ void align_cta(const int32_t* __restrict__ ids, const float* __restri
                 o.pair_of[i] = -1;
             }
             __syncwarp(amask);
-            if (valid && before == 0) cnt[warp * E + e] += __popc(peers);
+            if (valid && before == 0) cnt_w[e] += __popc(peers);
             __syncwarp(amask);
         }
+    }
+}
+
+// Item table and counters (thread t = expert t holds its count `total` and first position `start`): ceil(count /
+// chunk) items per active expert in expert order, then the shared expert's rows (expert id E, weight 1) at positions
+// n_valid + m. Every thread of the CTA calls this (it scans).
+__device__ void write_items(int total, int start, int n_valid, int E, int M, int npairs, int shared, int chunk,
+                            const AlignOut& o, int* scan) {
+    const int t = threadIdx.x;
+    const int nch = t < E ? (total + chunk - 1) / chunk : 0;
+    int n_routed_items = 0;
+    const int ibase = block_excl_scan(nch, scan, &n_routed_items);
+    const int shared_items = shared ? (M + chunk - 1) / chunk : 0;
+    if (t == 0) {
+        o.ws_i[0] = n_routed_items + shared_items;
+        o.ws_i[1] = n_valid;
+        o.ws_i[2] = n_valid + (shared ? M : 0);
     }
     if (t < E)
         for (int c = 0; c < nch; ++c) {
@@ -291,6 +275,103 @@ __device__ void align_cta(const int32_t* __restrict__ ids, const float* __restri
             o.item_cnt[n_routed_items + c] = min(chunk, M - c * chunk);
         }
     }
+}
+
+// One CTA. Pairs are split into 32 contiguous warp segments; per-(warp, expert) counts give every pair a stable
+// position (experts ascending, pair index ascending within an expert). pair_src[position] = the routed pair index
+// (the gate|up activation row), npairs + m for shared rows.
+__device__ void align_cta(const int32_t* __restrict__ ids, const float* __restrict__ w, int npairs, int topk, int E,
+                          int M, int shared, int chunk, const AlignOut& o, int* sm) {
+    int* cnt = sm;                             // [kAlignWarps][E]
+    int* scan = sm + kAlignWarps * E;          // [kAlignThreads]
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    for (int i = t; i < kAlignWarps * E; i += kAlignThreads) cnt[i] = 0;
+    __syncthreads();
+    const int seg = (npairs + kAlignWarps - 1) / kAlignWarps;
+    const int a0 = min(npairs, warp * seg), a1 = min(npairs, a0 + seg);
+    for (int i = a0 + lane; i < a1; i += 32) {
+        const int e = ids[i];
+        if (e >= 0 && e < E) atomicAdd(&cnt[warp * E + e], 1);
+    }
+    __syncthreads();
+    int total = 0;
+    if (t < E)
+        for (int ww = 0; ww < kAlignWarps; ++ww) total += cnt[ww * E + t];
+    int n_valid = 0;
+    const int start = block_excl_scan(total, scan, &n_valid);
+    if (t < E) {
+        int run = start;
+        for (int ww = 0; ww < kAlignWarps; ++ww) {
+            const int c = cnt[ww * E + t];
+            cnt[ww * E + t] = run;
+            run += c;
+        }
+    }
+    write_items(total, start, n_valid, E, M, npairs, shared, chunk, o, scan);
+    __syncthreads();
+    place_pairs(ids, w, topk, E, a0, a1, cnt + warp * E, o);
+}
+
+// Multi-CTA alignment of large pair counts (prefill), the same tables as align_cta: segments of kAlignSeg pairs,
+// pass 1 counts per (segment, expert), pass 2 gives each segment its offsets from those counts and places its pairs.
+constexpr int kAlignSeg = kAlignSegPairs;
+
+__global__ void __launch_bounds__(kAlignThreads) k_align_count(const int32_t* __restrict__ ids, int npairs, int E,
+                                                               int* __restrict__ seg_cnt) {
+    extern __shared__ int h[];                                // [E]
+    pdl_wait();
+    pdl_trigger();
+    for (int e = threadIdx.x; e < E; e += kAlignThreads) h[e] = 0;
+    __syncthreads();
+    const int a0 = blockIdx.x * kAlignSeg, a1 = min(npairs, a0 + kAlignSeg);
+    for (int i = a0 + threadIdx.x; i < a1; i += kAlignThreads) {
+        const int e = ids[i];
+        if (e >= 0 && e < E) atomicAdd(&h[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += kAlignThreads) seg_cnt[(size_t)blockIdx.x * E + e] = h[e];
+}
+
+__global__ void __launch_bounds__(kAlignThreads) k_align_place(const int32_t* __restrict__ ids,
+                                                               const float* __restrict__ w, int npairs, int topk,
+                                                               int E, int M, int shared, int chunk,
+                                                               const int* __restrict__ seg_cnt, const AlignOut o) {
+    extern __shared__ int sm[];
+    int* cnt = sm;                             // [kAlignWarps][E]
+    int* scan = sm + kAlignWarps * E;          // [kAlignThreads]
+    pdl_wait();
+    pdl_trigger();
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5, sg = blockIdx.x;
+    int total = 0, before = 0;
+    if (t < E)
+        for (int ss = 0; ss < (int)gridDim.x; ++ss) {
+            const int c = __ldcg(seg_cnt + (size_t)ss * E + t);
+            total += c;
+            if (ss < sg) before += c;
+        }
+    int n_valid = 0;
+    const int start = block_excl_scan(total, scan, &n_valid);
+    for (int i = t; i < kAlignWarps * E; i += kAlignThreads) cnt[i] = 0;
+    __syncthreads();
+    const int s0 = sg * kAlignSeg, s1 = min(npairs, s0 + kAlignSeg);
+    const int wseg = (s1 - s0 + kAlignWarps - 1) / kAlignWarps;
+    const int a0 = min(s1, s0 + warp * wseg), a1 = min(s1, a0 + wseg);
+    for (int i = a0 + lane; i < a1; i += 32) {
+        const int e = ids[i];
+        if (e >= 0 && e < E) atomicAdd(&cnt[warp * E + e], 1);
+    }
+    __syncthreads();
+    if (t < E) {
+        int run = start + before;
+        for (int ww = 0; ww < kAlignWarps; ++ww) {
+            const int c = cnt[ww * E + t];
+            cnt[ww * E + t] = run;
+            run += c;
+        }
+    }
+    if (sg == 0) write_items(total, start, n_valid, E, M, npairs, shared, chunk, o, scan);
+    __syncthreads();
+    place_pairs(ids, w, topk, E, a0, a1, cnt + warp * E, o);
 }
 
 __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restrict__ ids, const float* __restrict__ w,
@@ -424,8 +505,13 @@ static int set_max_smem_once(Kern kern, int* configured, const char* what) {
 
 static size_t align_smem(int E) { return (size_t)(kAlignWarps * E + kAlignThreads) * 4; }
 
+static int launch_align_multi(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
+                              uint8_t* ws, const WsLayout& L, cudaStream_t st);
+
+// The alignment kernels: one CTA up to kAlignSeg pairs, the two-pass multi-CTA version beyond.
 static int launch_align(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
                         uint8_t* ws, const WsLayout& L, cudaStream_t st) {
+    if (M * topk > kAlignSeg) return launch_align_multi(ids, w, M, topk, E, shared, chunk, ws, L, st);
     const size_t smem = align_smem(E);
     EXL3_REQUIRE(smem <= 227 * 1024, EXL3_ERR_UNSUPPORTED, "moe align: E=%d too large", E);
     static int configured[64] = {0};
@@ -433,6 +519,26 @@ static int launch_align(const int32_t* ids, const float* w, int M, int topk, int
     if (rc) return rc;
     cudaError_t e = launch_pdl(k_align, dim3(1), dim3(kAlignThreads), smem, st, ids, w, M * topk, topk, E, M, shared,
                                chunk, align_out(ws, L));
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "moe align: launch failed: %s", cudaGetErrorString(e));
+    return EXL3_OK;
+}
+
+// Alignment of a large batch over several CTAs (per-segment counts in the workspace's seg_cnt region).
+static int launch_align_multi(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
+                              uint8_t* ws, const WsLayout& L, cudaStream_t st) {
+    const int npairs = M * topk;
+    const int nseg = (npairs + kAlignSeg - 1) / kAlignSeg;
+    int* seg_cnt = reinterpret_cast<int*>(ws + L.seg_cnt);
+    const size_t smem = align_smem(E);
+    EXL3_REQUIRE(smem <= 227 * 1024, EXL3_ERR_UNSUPPORTED, "moe align: E=%d too large", E);
+    static int configured[64] = {0};
+    int rc = set_max_smem_once(k_align_place, configured, "moe align");
+    if (rc) return rc;
+    cudaError_t e = launch_pdl(k_align_count, dim3(nseg), dim3(kAlignThreads), (size_t)E * 4, st, ids, npairs, E,
+                               seg_cnt);
+    if (e == cudaSuccess)
+        e = launch_pdl(k_align_place, dim3(nseg), dim3(kAlignThreads), smem, st, ids, w, npairs, topk, E, M, shared,
+                       chunk, static_cast<const int*>(seg_cnt), align_out(ws, L));
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "moe align: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }

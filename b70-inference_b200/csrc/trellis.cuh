@@ -82,16 +82,22 @@ __device__ __forceinline__ __half mul1_one(uint32_t s) {
     return __ushort_as_half(static_cast<unsigned short>(r & 0xFFFFu));
 }
 
-// Decode the lane's A fragment (4 x half2) of one tile whose words start at `tile` (shared or global memory).
+// Decode the lane's A fragment (4 x half2) of one tile from its three words (tile words lw.i0, lw.i1, lw.i2).
 // Register order follows the m16n8k16 A layout: {pos0,pos1} {pos4,pos5} {pos2,pos3} {pos6,pos7}.
 template <int K>
-__device__ __forceinline__ void decode_frag(const uint32_t* tile, const LaneWords& lw, uint32_t a[4]) {
+__device__ __forceinline__ void decode_frag_words(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t off, uint32_t a[4]) {
     uint32_t st[8];
-    lane_states<K>(tile[lw.i0], tile[lw.i1], tile[lw.i2], lw.off, st);
+    lane_states<K>(w0, w1, w2, off, st);
     a[0] = mul1_pair(st[0], st[1]);
     a[1] = mul1_pair(st[4], st[5]);
     a[2] = mul1_pair(st[2], st[3]);
     a[3] = mul1_pair(st[6], st[7]);
+}
+
+// Decode the lane's A fragment of one tile whose words start at `tile` (shared or global memory).
+template <int K>
+__device__ __forceinline__ void decode_frag(const uint32_t* tile, const LaneWords& lw, uint32_t a[4]) {
+    decode_frag_words<K>(tile[lw.i0], tile[lw.i1], tile[lw.i2], lw.off, a);
 }
 
 // D[16x8] += A[16x16] * B[16x8], fp16 inputs, fp32 accumulators.

@@ -206,7 +206,8 @@ def moe_align(topk_ids: torch.Tensor, topk_w: torch.Tensor, E: int, shared: bool
     shared_items = (M + chunk - 1) // chunk if shared else 0
     max_items = (npairs + active * (chunk - 1)) // chunk + shared_items
     p_max = npairs + (M if shared else 0)
-    nbytes = 32 + 4 * (3 * max_items + 4 * p_max + npairs + max_items)     # tables + tickets (moe.cu layout)
+    nseg = (npairs + 8191) // 8192                                          # multi-CTA alignment segments
+    nbytes = 32 + 4 * (3 * max_items + 4 * p_max + npairs + max_items + nseg * E)   # tables, tickets, counts
     ws = torch.zeros(nbytes + 4096, dtype=torch.uint8, device=ids.device)
     rc = L.lib().exl3_moe_align(ids.data_ptr(), w.data_ptr(), M, k, E, int(shared), chunk, ws.data_ptr(), ws.numel(),
                                 L.stream_of(ids))

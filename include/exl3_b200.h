@@ -108,7 +108,7 @@ EXL3_API int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* p
  * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for any M, on the 5th-generation tensor cores: trellis tiles decoded to
  * the reference's fp16 weights bit for bit straight into tensor memory, tcgen05.mma.cta_group::2 kind::f16 (weights
  * from tensor memory, rotated activations from shared memory) with fp32 accumulation, 256 x 256 tiles per pair of
- * SMs. k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2; packed = exl3_pack; suh 8-byte aligned.
+ * SMs. k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2; packed = exl3_pack; suh, svh 8-byte aligned.
  * workspace >= exl3_gemm_tc_workspace_size(M, k) bytes, 256-byte aligned (the rotated input rows).
  * Replaces the reconstruct + GEMM linear for M > 128 (glm/xpu/csrc/exl3_ops.sycl:539-555,651-757) and exllamav3
  * exl3_gemm's large-M shapes (glm/docs/ext-op-inventory.md:498-557). */
