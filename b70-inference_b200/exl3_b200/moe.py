@@ -108,14 +108,16 @@ class ExpertTable:
 
 def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, table: ExpertTable,
                 act_limit: float = 0.0, out_dtype=torch.float32, out: torch.Tensor | None = None,
-                workspace: torch.Tensor | None = None, n_ctas: int = 0, events: dict | None = None) -> torch.Tensor:
+                workspace: torch.Tensor | None = None, n_ctas: int = 0, events: dict | None = None,
+                include_shared: bool = True) -> torch.Tensor:
     """Routed MoE sum (+ the table's shared expert, weight 1) for x [M, H] fp16/bf16:
     out[m] = sum_j topk_w[m, j] * expert_{topk_ids[m, j]}(x[m]) + shared(x[m]), fp32 (or fp16) [M, H].
     topk_ids int32 [M, k] (other int types converted; ids < 0 or >= E skipped), topk_w fp32 [M, k].
     The exl3xpu_moe.moe_forward contract (glm/xpu/csrc/exl3_moe.n128.sycl:1338-1341) over ExpertTable descriptors.
     events: if a dict is given, the phases run as separate C-ABI calls and (start, end) CUDA event pairs around the
     gate|up and down GEMV launches are appended to events["gateup"] / events["down"] (benchmark instrumentation;
-    events["external"] = True makes them event-record nodes when the call is captured in a CUDA graph)."""
+    events["external"] = True makes them event-record nodes when the call is captured in a CUDA graph).
+    include_shared=False leaves out the table's shared expert (expert parallelism adds it once, on the token's rank)."""
     L.require_cuda(x, topk_ids, topk_w)
     x2 = x.reshape(-1, x.shape[-1])
     if x2.dtype not in (torch.float16, torch.bfloat16):
@@ -131,7 +133,7 @@ def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, t
         out = torch.empty((M, H), dtype=out_dtype, device=x2.device)
     if M == 0:
         return out
-    shared = int(table.shared is not None)
+    shared = int(table.shared is not None and include_shared)
     lib = L.lib()
     need = lib.exl3_moe_workspace_size(M, k, table.E, H, table.I, shared)
     ws = workspace if workspace is not None else L.workspace(x2.device, need, "moe")
@@ -166,7 +168,7 @@ def moe_forward(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, t
 
 def moe_prefill(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, table: ExpertTable,
                 act_limit: float = 0.0, out_dtype=torch.float32, out: torch.Tensor | None = None,
-                workspace: torch.Tensor | None = None) -> torch.Tensor:
+                workspace: torch.Tensor | None = None, include_shared: bool = True) -> torch.Tensor:
     """moe_forward for prefill-sized batches on the tensor cores (C ABI exl3_moe_prefill): the same contract, with
     pairs grouped into items of <= 320 positions per expert and grouped tcgen05 GEMMs for the projections."""
     L.require_cuda(x, topk_ids, topk_w)
@@ -184,7 +186,7 @@ def moe_prefill(x: torch.Tensor, topk_ids: torch.Tensor, topk_w: torch.Tensor, t
         out = torch.empty((M, H), dtype=out_dtype, device=x2.device)
     if M == 0:
         return out
-    shared = int(table.shared is not None)
+    shared = int(table.shared is not None and include_shared)
     lib = L.lib()
     need = lib.exl3_moe_prefill_workspace_size(M, k, table.E, H, table.I, shared)
     ws = workspace if workspace is not None else L.workspace(x2.device, need, "moe_prefill")

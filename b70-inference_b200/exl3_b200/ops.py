@@ -13,7 +13,6 @@ import torch
 from . import _lib as L
 
 SMALL_M_MAX = int(os.environ.get("EXL3_SMALL_M_MAX", "32"))        # rows up to this: fused decode GEMV (8-row calls)
-RECON_SLICE_N = int(os.environ.get("EXL3_RECON_SLICE_N", "16384"))  # prefill: dequantised column slice width
 
 
 def _f16(t: torch.Tensor) -> torch.Tensor:
@@ -138,8 +137,9 @@ class BC_LinearEXL3:
 
     run(x, y): x fp16/bf16 [..., k] -> y (fp16/bf16/fp32, preallocated) [..., n].
       rows <= SMALL_M_MAX: the fused decode GEMV, 8 rows per launch (weights streamed once per launch);
-      larger: rotate x, dequantise W_hat in RECON_SLICE_N-column slices, library GEMM, rotate back
-      (the reference's prefill path, glm/xpu/csrc/exl3_ops.sycl:651-757)."""
+      larger: the tcgen05 linear (exl3_gemm_tc: trellis decoded into tensor memory, 2-SM MMAs, weights decoded once
+      per 320 rows), in place of the reference's dequantise + library GEMM prefill path
+      (glm/xpu/csrc/exl3_ops.sycl:651-757)."""
 
     def __init__(self, trellis, suh, svh, K, bias, mcg, mul1, xh):
         if mcg or not mul1:
@@ -178,31 +178,16 @@ class BC_LinearEXL3:
             for m0 in range(0, M, 8):
                 exl3_gemv(x2[m0:m0 + 8], pk, self.suh, self.svh, self.Ki, y2[m0:m0 + 8])
         else:
-            self._run_recon(x2, y2)
+            suh = self.suh if self.suh is None or self.suh.data_ptr() % 8 == 0 else self.suh.clone()
+            svh = self.svh if self.svh.data_ptr() % 8 == 0 else self.svh.clone()
+            if y2.stride(-1) != 1 or y2.stride(0) % 4 or y2.data_ptr() % 16:
+                tmp = torch.empty((M, self.out_features), dtype=y2.dtype, device=y2.device)
+                exl3_gemm_tc(x2, self.packed(), suh, svh, self.Ki, tmp)
+                y2.copy_(tmp)
+            else:
+                exl3_gemm_tc(x2, self.packed(), suh, svh, self.Ki, y2)
         if self.bias is not None:
             y2.add_(self.bias)
-
-    def _run_recon(self, x2: torch.Tensor, y2: torch.Tensor) -> None:
-        M, k, n = x2.shape[0], self.in_features, self.out_features
-        xh = torch.empty((M, k), dtype=torch.float16, device=x2.device)
-        had_r_128(x2.half(), xh, self.suh, None, 1.0)
-        acc = torch.empty((M, n), dtype=torch.float16 if y2.dtype != torch.float32 else torch.float32,
-                          device=x2.device)
-        w = torch.empty((k, min(RECON_SLICE_N, n)), dtype=torch.float16, device=x2.device)
-        for n0 in range(0, n, RECON_SLICE_N):
-            n1 = min(n0 + RECON_SLICE_N, n)
-            ws = w[:, :n1 - n0]
-            exl3_reconstruct(self.trellis, ws, n0, self.Ki)
-            if acc.dtype == torch.float32:
-                acc[:, n0:n1] = torch.matmul(xh.float(), ws.float())
-            else:
-                torch.matmul(xh, ws, out=acc[:, n0:n1])
-        if y2.dtype == torch.float32:
-            had_r_128(acc, acc, None, self.svh.float(), 1.0)
-            y2.copy_(acc)
-        else:
-            had_r_128(acc, acc, None, self.svh, 1.0)
-            y2.copy_(acc)
 
     def run_alloc(self, x: torch.Tensor, out_features: int, output_fp32: bool) -> torch.Tensor:
         y = torch.empty(x.shape[:-1] + (out_features,), dtype=torch.float if output_fp32 else torch.half,

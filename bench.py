@@ -242,20 +242,37 @@ def build_layer(cfg, E_local, e_base, gen, dev):
 
 
 def run_prefill(args, cfg):
-    """One MoE prefill layer per step (route + exl3_moe_prefill) on 1 GPU, timed with CUDA events over K steps.
-    roofline: tensor-bound; achieved = the layer's algorithmic flops (2 tokens topk 3 H I + shared 2 tokens 3 H I)
-    / the step time (router, alignment, rotations and combine included)."""
+    """One MoE prefill layer per step (route + exl3_moe_prefill) timed with CUDA events over K steps. N > 1:
+    expert parallelism (weak scaling): every rank routes its own `batch` tokens, holds E/N of the routed experts
+    (plus the shared expert) and exchanges token rows with the others through ExpertParallelMoE (NCCL all-to-all
+    dispatch and combine, the tcgen05 prefill kernels locally); value = all ranks' tokens / the slowest rank's step.
+    roofline: tensor-bound; achieved = one rank's algorithmic flops (2 tokens topk 3 H I + shared 2 tokens 3 H I)
+    / the step time (router, alignment, rotations, combine and the exchange included)."""
     import numpy as np
     import torch
+    import torch.distributed as dist
 
     from exl3_b200 import _lib as L
-    from exl3_b200 import moe, ops
+    from exl3_b200 import ep, moe, ops
 
-    dev = torch.device("cuda", 0)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE {world}")
+    cores = os.cpu_count() or 1
+    pool = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        pool = mp.get_context("spawn").Pool(cores)          # started before the first CUDA call
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     H, E, I, topk, T = cfg["H"], cfg["E"], cfg["I"], cfg["topk"], cfg["batch"]
-    gen = torch.Generator(device=dev).manual_seed(11)
-    rng = np.random.default_rng(11)
+    E_local = E // world
+    e0 = rank * E_local
+    gen = torch.Generator(device=dev).manual_seed(11 + rank)
 
     def mat(k, n, K):
         tr = torch.randint(-32768, 32767, (k // 16, n // 16, 16 * K), dtype=torch.int16, device=dev, generator=gen)
@@ -264,7 +281,8 @@ def run_prefill(args, cfg):
         return moe.Exl3Matrix(tr, s1, s2, K)
 
     experts = []
-    for _ in range(E):
+    for e in range(e0, e0 + E_local):
+        rng = np.random.default_rng(1000 + e)               # the expert's bit widths do not depend on the rank count
         Ks = [2 if rng.random() < cfg["p_k2"] else 1 for _ in range(3)]
         experts.append(moe.Expert(mat(H, I, Ks[0]), mat(H, I, Ks[1]), mat(I, H, Ks[2])))
     shared = moe.Expert(mat(H, I, cfg["shared_K"]), mat(H, I, cfg["shared_K"]), mat(I, H, cfg["shared_K"]))
@@ -272,46 +290,105 @@ def run_prefill(args, cfg):
     del experts, shared
     x = torch.randn(T, H, device=dev, generator=gen).to(torch.bfloat16)
     logits = torch.randn(T, E, device=dev, generator=gen)
-    bias = torch.randn(E, device=dev, generator=gen) * 0.1
+    ggen = torch.Generator(device=dev).manual_seed(7)       # router bias shared by all ranks
+    bias = torch.randn(E, device=dev, generator=ggen) * 0.1
     out = torch.empty(T, H, device=dev, dtype=torch.float32)
-    need = L.lib().exl3_moe_prefill_workspace_size(T, topk, E, H, I, 1)
-    ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    ws = None
+    epm = None
+    if world == 1:
+        need = L.lib().exl3_moe_prefill_workspace_size(T, topk, E, H, I, 1)
+        ws = torch.empty(need, dtype=torch.uint8, device=dev)
+    else:
+        epm = ep.ExpertParallelMoE(E, H, topk, None, table, cfg["act_limit"])
 
     def step():
         ids, w, _ = ops.route(logits, L.ROUTE_SQRT_SOFTPLUS, topk, bias=bias, scale=cfg["scale"])
-        moe.moe_prefill(x, ids, w, table, cfg["act_limit"], out=out, workspace=ws)
+        if world == 1:
+            moe.moe_prefill(x, ids, w, table, cfg["act_limit"], out=out, workspace=ws)
+        else:
+            out.copy_(epm.forward(x, ids, w))
+
+    def timed(body):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            body()
+        t1.record()
+        torch.cuda.synchronize()
+        ms_ = t0.elapsed_time(t1) / args.steps
+        if world > 1:
+            tt = torch.tensor([ms_], device=dev)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            ms_ = float(tt.item())
+        return ms_
 
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(0) as clk:
-        t0.record()
-        for _ in range(args.steps):
-            step()
-        t1.record()
-        torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1) / args.steps
+    with ClockSampler(local) as clk:
+        ms = timed(step)
     assert torch.isfinite(out).all(), "non-finite MoE output"
-    assert L.lib().exl3_device_status(0) == 0
+    assert L.lib().exl3_device_status(local) == 0
+
+    # e2e: the same step from pinned host buffers (x, router logits) to a host output, copies inside the timed region
+    xh, lh = x.cpu().pin_memory(), logits.cpu().pin_memory()
+    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def e2e_step():
+        x.copy_(xh, non_blocking=True)
+        logits.copy_(lh, non_blocking=True)
+        step()
+        oh.copy_(out, non_blocking=True)
+
+    ms_e2e = timed(e2e_step)
+    assert torch.isfinite(oh).all(), "non-finite MoE output"
+
+    cpu = None
+    if pool is not None:
+        rng2 = np.random.default_rng(5)
+        cpu_picks_seconds(cfg, pool, rng2, cores)
+        tcpu = statistics.median(cpu_picks_seconds(cfg, pool, rng2, cores) for _ in range(3))
+        pool.close()
+        cpu = {"value": round(cores / topk / tcpu, 5), "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": f"{cores} expert picks of this layer (trellis decoded and applied per call) in parallel on "
+                         f"{cores} spawn workers, median of 3; tok/s = picks/topk/time; numpy restatement of the "
+                         f"reference's torch path"}
     flops = 2.0 * T * topk * 3 * H * I + 2.0 * T * 3 * H * I
     with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
         peak = float(json.load(f)["bf16_tflops"])
     ach = flops / (ms * 1e-3) / 1e12
-    line = {
-        "metric": "MoE-layer prefill tok/s (tcgen05 grouped GEMM, tensor-pipe fraction)", "value": round(T / (ms * 1e-3), 1),
-        "unit": "tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic (seeded random trellis, +-1 signs, N(0,1) bf16 activations)",
-        "config": {"workload": args.workload, "tokens": T, "hidden": H, "experts": E, "intermediate": I, "topk": topk,
-                   "K": "1/2 (P(2)=0.62)", "shared_K": cfg["shared_K"], "router": cfg["router"],
-                   "l2": "inputs larger than L2 (2.3 GB of expert weights, 117 MB of activations per step)"},
-        "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(ach / peak, 4), "peak_kind": "measured bf16 burst", "traffic": None,
-                     "flops_per_step": flops},
-        "cpu_baseline": None, "gpu_launches": 6 * args.steps, "clocks": clk.summary(),
-    }
-    print(json.dumps(line), flush=True)
+    # route, alignment (count + place when the pairs exceed one CTA's segment), rotation, gate and up GEMM,
+    # activation, down GEMM, combine; N > 1: the local step on the received rows and the shared expert's own call
+    per_call = lambda rows: 8 if rows * topk > 8192 else 7
+    launches = (per_call(T) if world == 1 else 1 + per_call(T * world) + per_call(T)) * args.steps
+    if rank == 0:
+        line = {
+            "metric": "MoE-layer prefill tok/s (tcgen05 grouped GEMM, tensor-pipe fraction)",
+            "value": round(world * T / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (seeded random trellis, +-1 signs, N(0,1) bf16 activations)",
+            "config": {"workload": args.workload, "tokens_per_gpu": T, "hidden": H, "experts": E,
+                       "intermediate": I, "topk": topk, "K": "1/2 (P(2)=0.62)", "shared_K": cfg["shared_K"],
+                       "router": cfg["router"], "parallelism": f"ep{world}" if world > 1 else "none",
+                       "l2": "inputs larger than L2 (expert weights of 2.3 GB per 256 experts, 117 MB of activations "
+                             "per rank and step)"},
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(ach / peak, 4), "peak_kind": "measured bf16 burst", "traffic": None,
+                         "flops_per_step_per_gpu": flops},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * T / (ms_e2e * 1e-3), 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": int(xh.numel() * 2 + lh.numel() * 4),
+                    "d2h_bytes_per_step": int(oh.numel() * 4)},
+            "gpu_launches": launches, "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_ours(args, cfg):

@@ -21,11 +21,11 @@ def _free_port():
     return p
 
 
-def _experts():
+def _experts(n=E, seed=42):
     from oracle import oracle as O
-    rng = np.random.default_rng(42)
+    rng = np.random.default_rng(seed)
     ex = []
-    for e in range(E):
+    for e in range(n):
         K = 2 + e % 3
         mats = [(O.random_trellis(rng, kk, nn, K), O.random_signs(rng, kk), O.random_signs(rng, nn), K)
                 for kk, nn in ((H, I), (H, I), (I, H))]
@@ -64,7 +64,14 @@ def _worker(rank, world, port, mode, q):
                         out[r] = (out[r] + np.float32(ww[r, j]) * d).astype(np.float32)
             return torch.from_numpy(out)
 
-        m = ep.ExpertParallelMoE(E, H, TOPK, local_fn=local_fn)
+        shared_fn = None
+        if mode == "shared":
+            shared = _experts(1, seed=7)[0]
+
+            def shared_fn(x):
+                return torch.from_numpy(O.expert_forward(x.numpy(), shared, 10.0).astype(np.float32))
+
+        m = ep.ExpertParallelMoE(E, H, TOPK, local_fn=local_fn, shared_fn=shared_fn)
         x, ids, w = _tokens(rank)
         if mode == "fail" and rank == 1:
             raise RuntimeError("rank 1 fails before the dispatch")
@@ -108,6 +115,21 @@ def test_ep_dispatch_combine_matches_oracle():
         x, ids, w = _tokens(r)
         ref = O.moe_forward(x, ids, w, experts, 10.0)
         assert_close(out, ref, what=f"EP rank {r}")
+
+
+def test_ep_shared_expert_counted_once():
+    """A shared expert runs once per token, on the token's own rank (not on every rank that received the row)."""
+    from oracle import oracle as O
+    from tests.tolerance import assert_close
+    res = _run("shared")
+    experts = _experts()
+    shared = _experts(1, seed=7)[0]
+    for r in range(2):
+        st, out = res[r]
+        assert st == "ok", out
+        x, ids, w = _tokens(r)
+        ref = O.moe_forward(x, ids, w, experts, 10.0, shared=shared)
+        assert_close(out, ref, what=f"EP rank {r} with shared expert")
 
 
 def test_ep_rank_failure_is_reported_not_hung():
