@@ -50,7 +50,12 @@ __device__ __forceinline__ void lane_states(uint32_t w0, uint32_t w1, uint32_t w
     for (int i = 0; i < 8; ++i) {
         const int s = 48 - i * K;   // right shift of the 64-bit (hi:mid) that aligns window i at bit 0
         uint32_t v;
-        if (s >= 32) {
+        if (s >= 32 && (K % 2 == 0) && s - 32 < 16) {
+            // even K: the windows inside hi sit at few bit offsets mod 8; shift once per offset (the shifted copies
+            // are shared between windows) and take the window's two bytes with a zero-filling byte permute
+            const int r = s - 32, sh = r & 7, b = (r - sh) >> 3;
+            v = __byte_perm(sh ? hi >> sh : hi, 0u, (uint32_t)(b | ((b + 1) << 4) | 0x4400));
+        } else if (s >= 32) {
             v = (s - 32 == 16) ? (hi >> 16) : ((hi >> (s - 32)) & 0xFFFFu);
         } else if (s >= 16) {
             v = __funnelshift_r(mid, hi, s) & 0xFFFFu;
