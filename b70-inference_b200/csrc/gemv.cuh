@@ -96,6 +96,7 @@ struct GemvArgs {
     const ExpertDesc* experts;
     ItemTable items;
     float* ybuf;            // [positions, H] fp32 weighted down outputs
+    int ybuf_round_f16;     // down: round as the fp16 linear does, fp16(fp16(H(acc) / sqrt(128)) * svh), before the weight
     float act_limit;
     // activations in xf order: linear: [M][k]; gate|up: [rows][2][k] (row = pair_src of a position); down: [pos][k]
     const __half* xf;
@@ -368,7 +369,12 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
             const float w = __ldcg(a.items.pair_w + ui.s0 + row);
             float o[4];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) o[j] = w * (v[0][j] * kRsqrt128 * __half2float(svh[0][col + j]));
+            for (int j = 0; j < 4; ++j) {
+                const float sv = __half2float(svh[0][col + j]);
+                o[j] = a.ybuf_round_f16
+                           ? w * __half2float(__float2half_rn(__half2float(__float2half_rn(v[0][j] * kRsqrt128)) * sv))
+                           : w * (v[0][j] * kRsqrt128 * sv);
+            }
             float* dst = a.ybuf + (size_t)(ui.s0 + row) * a.n + col;
             *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
         }

@@ -41,6 +41,9 @@ _PROTOS = [
     ("exl3_gemm_tc_workspace_size", sz, [i32, i32]),
     ("exl3_gemm_tc", i32, [vp, i32, i32, i32, vp, vp, vp, i32, i32, i32, i32, vp, i32, i32, vp, sz, vp]),
     ("exl3_gemv_noalloc", i32, [vp, i32, i32, i32, vp, vp, vp, i32, i32, i32, i32, vp, i32, i32, vp]),
+    ("exl3_mgemm_workspace_size", sz, [i32, i32, i32, i32, i32]),
+    ("exl3_mgemm", i32, [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, i32, vp, i32, vp, i32, i32, i32, vp, i32,
+                         i32, vp, sz, vp]),
     ("exl3_silu_mul", i32, [vp, vp, vp, i64, f32, vp]),
     ("exl3_route", i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp, f32, i32, vp, i32, vp, vp, vp]),
     ("exl3_moe_workspace_size", sz, [i32, i32, i32, i32, i32, i32]),

@@ -7,6 +7,7 @@ its C ABI; none has a CPU path.
 from __future__ import annotations
 
 import os
+import weakref
 
 import torch
 
@@ -161,6 +162,7 @@ class BC_LinearEXL3:
             raise L.Exl3Error(f"BC_LinearEXL3: trellis {tuple(trellis.shape)} does not match K={K}")
         # the decode GEMV reads a column-block-major copy of the trellis (packed once, on first use)
         self._packed = None
+        _LINEARS[trellis.data_ptr()] = self          # exl3_mgemm resolves trellis addresses to linears
 
     def packed(self) -> torch.Tensor:
         if self._packed is None or self._packed.device != self.trellis.device:
@@ -196,6 +198,74 @@ class BC_LinearEXL3:
             return y
         self.run(x.reshape(-1, x.shape[-1]), y.view(-1, out_features))
         return y
+
+
+# trellis device address -> the BC_LinearEXL3 that owns it (weak: the registry does not keep linears alive)
+_LINEARS: "weakref.WeakValueDictionary[int, BC_LinearEXL3]" = weakref.WeakValueDictionary()
+_MG_TABLES: dict = {}
+
+
+def register_linear(trellis: torch.Tensor, suh: torch.Tensor | None, svh: torch.Tensor, K) -> "BC_LinearEXL3":
+    """A BC_LinearEXL3 for tensors created outside one (exl3_mgemm finds matrices by trellis address); keep the
+    returned object alive while its address may appear in a pointer table."""
+    return BC_LinearEXL3(trellis, suh, svh, K, None, False, True, None)
+
+
+def _mg_tables(B: torch.Tensor):
+    """Packed-trellis address table and bit widths for a table of trellis addresses (cached per table: exllamav3
+    builds its pointer tables once; the first call reads the table to the host)."""
+    key = (B.data_ptr(), B.numel(), B.device)
+    hit = _MG_TABLES.get(key)
+    if hit is not None and all(r() is not None for r in hit[2]):
+        return hit[0], hit[1]
+    addrs = [int(a) for a in B.reshape(-1).tolist()]
+    lins = []
+    for a in addrs:
+        lin = _LINEARS.get(a)
+        if lin is None:
+            raise L.Exl3Error(f"exl3_mgemm: trellis at 0x{a:x} belongs to no BC_LinearEXL3 (create one, or call "
+                              f"register_linear)")
+        lins.append(lin)
+    packed = torch.tensor([lin.packed().data_ptr() for lin in lins], dtype=torch.int64, device=B.device)
+    ks = torch.tensor([lin.Ki for lin in lins], dtype=torch.int32, device=B.device)
+    _MG_TABLES[key] = (packed, ks, [weakref.ref(lin) for lin in lins], [lin.packed() for lin in lins])
+    return packed, ks
+
+
+def exl3_mgemm(A, B, C, suh, A_had, svh, indices=None, weights=None, K=None, force_shape_idx=-1, mcg=False,
+               mul1=True, min_index=-1, max_index=-1, force_num_sms=0, num_tokens=1, size_n_list=None, c_ptrs=None,
+               n_stride_list=None, had_src_list=None, num_had_src=0) -> int:
+    """exllamav3 exl3_mgemm(A, B, C, suh, A_had, svh, indices, weights, K, ...) (glm/docs/ext-op-inventory.md:664-688,
+    1104-1120) on the C ABI exl3_mgemm: B / suh / svh are int64 device tables of trellis / suh / svh addresses (the
+    trellis tensors of BC_LinearEXL3 objects); A fp16/bf16 [a_batches, m, k]; C fp16/bf16/fp32 [c_batches, m, n].
+    Slot j: C[j] = lin(A[j or 0], B[indices[j] or j]); with weights, C[t] = sum of token t's weighted slots.
+    A_had is not needed (the rotated rows live in the library's workspace). Returns 0."""
+    if size_n_list is not None or c_ptrs is not None or n_stride_list is not None or had_src_list is not None:
+        raise L.Exl3Error("exl3_mgemm: the sliced mode is not supported")
+    if mcg or not mul1:
+        raise L.Exl3Error("exl3_mgemm: only the mul1 codebook is supported")
+    L.require_cuda(A, B, C, svh)
+    A3 = A if A.dim() == 3 else A.reshape(1, *A.shape)
+    A3 = _f16(A3)
+    a_batches, m, k = A3.shape
+    n = C.shape[-1]
+    packed, ks = _mg_tables(B)
+    n_mats = packed.numel()
+    idx = None if indices is None else indices.reshape(-1).to(torch.int32).contiguous()
+    slots = n_mats if idx is None else idx.numel()
+    w = None if weights is None else weights.reshape(-1).to(torch.float32).contiguous()
+    C3 = C.reshape(-1, m, n)
+    if C3.stride(-1) != 1 or C3.stride(1) != n or C3.stride(0) != m * n:
+        raise L.Exl3Error("exl3_mgemm: C must be contiguous")
+    lib = L.lib()
+    need = lib.exl3_mgemm_workspace_size(slots, m, k, n, n_mats)
+    ws = L.workspace(A3.device, need, "mgemm")
+    rc = lib.exl3_mgemm(A3.data_ptr(), L.dtype_code(A3.dtype), a_batches, k, m, k, n, packed.data_ptr(),
+                        L.ptr(suh), svh.data_ptr(), ks.data_ptr(), n_mats, L.ptr(idx), slots, L.ptr(w),
+                        int(num_tokens), int(min_index), int(max_index), C3.data_ptr(), L.dtype_code(C3.dtype), n,
+                        ws.data_ptr(), ws.numel(), L.stream_of(A3))
+    L.check(rc, "exl3_mgemm")
+    return 0
 
 
 def exl3_gemm(A, B, C, suh, A_had, svh, force_shape_idx=-1, mcg=False, mul1=True, force_num_sms=0) -> int:

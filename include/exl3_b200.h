@@ -127,6 +127,26 @@ EXL3_API int exl3_gemv_noalloc(const void* x, int x_dtype, int ldx, int M, const
                                const void* svh, int k, int n, int K, int cb, void* y, int y_dtype, int ldy,
                                void* stream);
 
+/* ---- several EXL3 linears over pointer tables (exl3_mgemm) ----
+ * Slot j (0 <= j < slots) uses matrix q = indices[j] (or j when indices is null); with min_index >= 0 only
+ * q in [min_index, max_index) are kept, rebased to q - min_index; negative or out-of-range q skip the slot.
+ *   C[j][m][n] = lin(A[a_batches == 1 ? 0 : j], matrix q)                 (weights null; skipped slots untouched)
+ *   C[t][m][n] = sum over slots j of token t of weights[j] * lin(...)     (weights given; slots / num_tokens per
+ *                                                                          token, summed in slot order in fp32)
+ * A [a_batches][m][k] fp16/bf16 (row stride lda); trellis_ptrs / suh_ptrs / svh_ptrs: device arrays of n_mats device
+ * addresses (trellis packed by exl3_pack; a zero suh entry means no input signs), K_per_mat device int32 [n_mats];
+ * indices device int32 [slots] or null; weights device fp32 [slots] or null; C fp16/bf16/fp32 (row stride ldc).
+ * k % 128 == 0, n % 128 == 0. Unweighted fp16 C follows the fp16 linear's rounding; weighted sums accumulate in
+ * fp32 (the reference accumulates fp16 C with fp16 additions). workspace >= exl3_mgemm_workspace_size(...),
+ * 256-byte aligned. Replaces exllamav3 exl3_mgemm (glm/docs/ext-op-inventory.md:664-688,1104-1120), without its
+ * sliced mode (size_n_list / c_ptrs, used only by attention). */
+EXL3_API size_t exl3_mgemm_workspace_size(int slots, int m, int k, int n, int n_mats);
+EXL3_API int exl3_mgemm(const void* A, int a_dtype, int a_batches, int lda, int m, int k, int n,
+                        const uint64_t* trellis_ptrs, const uint64_t* suh_ptrs, const uint64_t* svh_ptrs,
+                        const int32_t* K_per_mat, int n_mats, const int32_t* indices, int slots, const float* weights,
+                        int num_tokens, int min_index, int max_index, void* C, int c_dtype, int ldc, void* workspace,
+                        size_t ws_bytes, void* stream);
+
 /* ---- activation ----
  * z = fp16(min(silu(g), L) * clamp(u, -L, L)), L = act_limit (0 disables the clamps); fp32 math.
  * g, u, z fp16 [count]; z may alias u. Replaces silu_mul (glm/xpu/glm_xpu/ops.py:147-154). */

@@ -64,6 +64,18 @@ def test_argument_validation_returns_status_codes():
     assert lib.exl3_moe_decode(16, 0, 128, 1, 16, 16, 2, 16, 4, 0, 128, 128, 0.0, 16, 2, None, 0, 0, None) == \
         L.EXL3_ERR_WORKSPACE
     assert lib.exl3_moe_gateup(1, 2, 16, 4, 0, 128, 128, 0.0, None, 0, 0, None) == L.EXL3_ERR_WORKSPACE
+    # exl3_mgemm: k not a multiple of 128, A batches neither 1 nor the slot count, weighted slots not splitting
+    # over the tokens, missing workspace
+
+    def mgemm(k=128, a_batches=1, slots=2, weights=None, tokens=1, ws=None, ws_bytes=0):
+        return lib.exl3_mgemm(16, 0, a_batches, k, 1, k, 128, 16, 16, 16, 16, 2, None, slots, weights, tokens, -1, -1,
+                              16, 2, 128, ws, ws_bytes, None)
+    assert mgemm(k=100) == L.EXL3_ERR_ARG
+    assert mgemm(a_batches=3) == L.EXL3_ERR_ARG
+    assert mgemm(weights=16, slots=3, tokens=2) == L.EXL3_ERR_ARG
+    assert mgemm() == L.EXL3_ERR_WORKSPACE
+    assert mgemm(slots=0) == L.EXL3_OK
+    assert lib.exl3_mgemm_workspace_size(4, 8, 128, 128, 2) > lib.exl3_mgemm_workspace_size(2, 8, 128, 128, 2) > 0
     # negative group count
     assert gemv(groups=-1) == L.EXL3_ERR_ARG
     # zero rows is a no-op
