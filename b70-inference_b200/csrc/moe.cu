@@ -94,19 +94,30 @@ __device__ __forceinline__ float route_score(float v, int kind) {
 // One warp per row: scores in fp64 rounded once to fp32 and 64-bit selection keys in shared memory; k argmax passes
 // (lane-local scan + warp reduction, ties -> lowest index) with no block-wide barriers; the picks' weights are
 // evaluated in parallel, one lane per pick, and summed in slot order.
-__global__ void __launch_bounds__(kRouteWarps * 32) k_route(const float* __restrict__ logits, int ld, int R, int E,
-                                                            int kind, int k, const float* bias, const float* res,
-                                                            const float* mul, float scale, int renorm, void* ids,
-                                                            int ids64, float* w, void* want) {
-    __shared__ float s_score[kRouteWarps][kRouteMaxE];
-    __shared__ uint64_t s_key[kRouteWarps][kRouteMaxE];
-    pdl_wait();                                               // logits may come from the previous kernel
-    const int lane = threadIdx.x & 31, wr = threadIdx.x >> 5;
-    const int row = blockIdx.x * kRouteWarps + wr;
-    if (row >= R) return;
-    const float* l = logits + (size_t)row * ld;
-    float* sc = s_score[wr];
-    uint64_t* key = s_key[wr];
+struct RouteParams {
+    int E, kind, k;
+    const float* bias;
+    const float* res;
+    const float* mul;
+    float scale;
+    int renorm;
+    void* ids;
+    int ids64;
+    float* w;
+    void* want;
+};
+
+__device__ void route_row(const float* __restrict__ l, int row, const RouteParams& rp, float* sc, uint64_t* key,
+                          int lane) {
+    const int E = rp.E, kind = rp.kind, k = rp.k;
+    const float* bias = rp.bias;
+    const float* res = rp.res;
+    const float* mul = rp.mul;
+    const float scale = rp.scale;
+    const int renorm = rp.renorm, ids64 = rp.ids64;
+    void* ids = rp.ids;
+    float* w = rp.w;
+    void* want = rp.want;
 
     // logits: every load of the row issued before any is used (one memory round trip), then the scores
     float lmax = -INFINITY;
@@ -173,6 +184,78 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route(const float* __restr
         }
         __syncwarp();
     }
+}
+
+__global__ void __launch_bounds__(kRouteWarps * 32) k_route(const float* __restrict__ logits, int ld, int R,
+                                                            const RouteParams rp) {
+    __shared__ float s_score[kRouteWarps][kRouteMaxE];
+    __shared__ uint64_t s_key[kRouteWarps][kRouteMaxE];
+    pdl_wait();                                               // logits may come from the previous kernel
+    const int lane = threadIdx.x & 31, wr = threadIdx.x >> 5;
+    const int row = blockIdx.x * kRouteWarps + wr;
+    if (row >= R) return;
+    route_row(logits + (size_t)row * ld, row, rp, s_score[wr], s_key[wr], lane);
+}
+
+// Router from the hidden states (the router GEMV fused into the launch): CTAs split the experts, one warp per expert
+// computes its logits for every row (fp32 FMA dot over fp16 pairs, lane-strided, then a warp reduction; rounded to
+// fp16 as the reference's routing GEMV does, glm/docs/ext-op-inventory.md:980-1004) into the workspace; the CTA that
+// finishes last (atomic ticket, left at zero for the next call) routes every row.
+constexpr int kRhWarps = 8;
+constexpr int kRhRouteWarps = 3;                      // routing warps of the last CTA (static shared memory: 36 KB)
+constexpr int kRhMaxRows = 64;
+
+template <typename T>
+__global__ void __launch_bounds__(kRhWarps * 32) k_route_hidden(const T* __restrict__ hidden, int ldh, int R, int H,
+                                                                const __half* __restrict__ gate_t, float* lg,
+                                                                __half* logits_out, unsigned int* ticket,
+                                                                const RouteParams rp) {
+    __shared__ float s_score[kRhRouteWarps][kRouteMaxE];
+    __shared__ uint64_t s_key[kRhRouteWarps][kRouteMaxE];
+    __shared__ int s_last;
+    pdl_wait();                                               // hidden states come from the previous kernel
+    const int lane = threadIdx.x & 31, wr = threadIdx.x >> 5;
+    const int E = rp.E;
+    for (int e = blockIdx.x * kRhWarps + wr; e < E; e += gridDim.x * kRhWarps) {
+        const __half2* g = reinterpret_cast<const __half2*>(gate_t + (size_t)e * H);
+        for (int r0 = 0; r0 < R; r0 += 8) {
+            float acc[8];
+#pragma unroll
+            for (int rr = 0; rr < 8; ++rr) acc[rr] = 0.f;
+            for (int c = lane; c < H / 2; c += 32) {
+                const float2 gv = __half22float2(g[c]);
+#pragma unroll
+                for (int rr = 0; rr < 8; ++rr) {
+                    if (r0 + rr < R) {
+                        const T* xp = hidden + (size_t)(r0 + rr) * ldh + 2 * c;
+                        acc[rr] = fmaf(to_f32<T>(xp[0]), gv.x, acc[rr]);
+                        acc[rr] = fmaf(to_f32<T>(xp[1]), gv.y, acc[rr]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int rr = 0; rr < 8; ++rr) {
+                float v = acc[rr];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+                if (lane == 0 && r0 + rr < R) {
+                    const __half h = __float2half_rn(v);
+                    lg[(size_t)(r0 + rr) * E + e] = __half2float(h);
+                    if (logits_out) logits_out[(size_t)(r0 + rr) * E + e] = h;
+                }
+            }
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicInc(ticket, gridDim.x - 1) == gridDim.x - 1;
+    __syncthreads();
+    pdl_trigger();
+    if (!s_last) return;
+    __threadfence();
+    if (wr >= kRhRouteWarps) return;
+    for (int row = wr; row < R; row += kRhRouteWarps)
+        route_row(lg + (size_t)row * E, row, rp, s_score[wr], s_key[wr], lane);
 }
 
 // ------------------------------------------------------------------------------------------------ align
@@ -779,10 +862,52 @@ int exl3_route(const float* logits, int ld, int R, int E, int kind, int k, const
     EXL3_REQUIRE(k >= 1 && k <= kRouteMaxK && k <= E, EXL3_ERR_ARG, "exl3_route: k=%d", k);
     EXL3_REQUIRE(kind >= 0 && kind <= 2, EXL3_ERR_ARG, "exl3_route: kind=%d", kind);
     if (R == 0) return EXL3_OK;
+    const RouteParams rp = {E, kind, k, bias, res, mul, scale, renorm, ids, ids64, w, want};
     cudaError_t e = launch_pdl(k_route, dim3((R + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), 0,
-                               static_cast<cudaStream_t>(stream), logits, ld, R, E, kind, k, bias, res, mul, scale,
-                               renorm, ids, ids64, w, want);
+                               static_cast<cudaStream_t>(stream), logits, ld, R, rp);
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_route: launch failed: %s", cudaGetErrorString(e));
+    return EXL3_OK;
+}
+
+size_t exl3_route_hidden_workspace_size(int R, int E) {
+    if (R <= 0 || E <= 0) return 0;
+    return 256 + align_up((size_t)R * E * 4, 256);
+}
+
+int exl3_route_hidden(const void* hidden, int h_dtype, int ldh, int R, int H, const void* gate_t, int E, int kind,
+                      int k, const float* bias, const float* res, const float* mul, float scale, int renorm, void* ids,
+                      int ids64, float* w, void* want, void* logits_out, void* workspace, size_t ws_bytes,
+                      void* stream) {
+    EXL3_REQUIRE(hidden && gate_t && ids && w && R >= 0 && E > 0 && H > 0 && H % 2 == 0 && ldh >= H, EXL3_ERR_ARG,
+                 "exl3_route_hidden: bad arguments");
+    EXL3_REQUIRE(E <= kRouteMaxE, EXL3_ERR_UNSUPPORTED, "exl3_route_hidden: E=%d > %d", E, kRouteMaxE);
+    EXL3_REQUIRE(R <= kRhMaxRows, EXL3_ERR_UNSUPPORTED,
+                 "exl3_route_hidden: R=%d > %d rows (compute the logits with a GEMM and call exl3_route)", R,
+                 kRhMaxRows);
+    EXL3_REQUIRE(k >= 1 && k <= kRouteMaxK && k <= E, EXL3_ERR_ARG, "exl3_route_hidden: k=%d", k);
+    EXL3_REQUIRE(kind >= 0 && kind <= 2, EXL3_ERR_ARG, "exl3_route_hidden: kind=%d", kind);
+    EXL3_REQUIRE(h_dtype == EXL3_F16 || h_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "exl3_route_hidden: dtype %d",
+                 h_dtype);
+    EXL3_REQUIRE((reinterpret_cast<uintptr_t>(gate_t) & 3) == 0, EXL3_ERR_ARG,
+                 "exl3_route_hidden: gate_t must be 4-byte aligned");
+    if (R == 0) return EXL3_OK;
+    EXL3_REQUIRE(workspace && ws_bytes >= exl3_route_hidden_workspace_size(R, E), EXL3_ERR_WORKSPACE,
+                 "exl3_route_hidden: workspace %zu < %zu bytes", ws_bytes, exl3_route_hidden_workspace_size(R, E));
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    unsigned int* ticket = reinterpret_cast<unsigned int*>(ws);
+    float* lg = reinterpret_cast<float*>(ws + 256);
+    const RouteParams rp = {E, kind, k, bias, res, mul, scale, renorm, ids, ids64, w, want};
+    const dim3 grid((E + kRhWarps - 1) / kRhWarps);
+    cudaError_t e;
+    if (h_dtype == EXL3_BF16)
+        e = launch_pdl(k_route_hidden<__nv_bfloat16>, grid, dim3(kRhWarps * 32), 0, static_cast<cudaStream_t>(stream),
+                       static_cast<const __nv_bfloat16*>(hidden), ldh, R, H, static_cast<const __half*>(gate_t), lg,
+                       static_cast<__half*>(logits_out), ticket, rp);
+    else
+        e = launch_pdl(k_route_hidden<__half>, grid, dim3(kRhWarps * 32), 0, static_cast<cudaStream_t>(stream),
+                       static_cast<const __half*>(hidden), ldh, R, H, static_cast<const __half*>(gate_t), lg,
+                       static_cast<__half*>(logits_out), ticket, rp);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_route_hidden: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }
 

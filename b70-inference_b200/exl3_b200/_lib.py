@@ -46,6 +46,9 @@ _PROTOS = [
                          i32, vp, sz, vp]),
     ("exl3_silu_mul", i32, [vp, vp, vp, i64, f32, vp]),
     ("exl3_route", i32, [vp, i32, i32, i32, i32, i32, vp, vp, vp, f32, i32, vp, i32, vp, vp, vp]),
+    ("exl3_route_hidden_workspace_size", sz, [i32, i32]),
+    ("exl3_route_hidden", i32, [vp, i32, i32, i32, i32, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, i32, vp, vp, vp,
+                                vp, sz, vp]),
     ("exl3_moe_workspace_size", sz, [i32, i32, i32, i32, i32, i32]),
     ("exl3_moe_decode", i32, [vp, i32, i32, i32, vp, vp, i32, vp, i32, i32, i32, i32, f32, vp, i32, vp, sz, i32,
                               vp]),
@@ -107,6 +110,17 @@ def dtype_code(dt: torch.dtype) -> int:
 
 
 _WS: dict = {}
+
+
+def zeroed_workspace(device, nbytes: int, key: str) -> torch.Tensor:
+    """A cached device buffer zeroed when (re)allocated, for entry points that need zeroed scratch on their first
+    use and leave it zeroed (exl3_route_hidden's ticket)."""
+    k = (str(device), "zeroed:" + key)
+    buf = _WS.get(k)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.zeros(max(int(nbytes), 1 << 16), dtype=torch.uint8, device=device)
+        _WS[k] = buf
+    return buf
 
 
 def workspace(device, nbytes: int, key: str = "ws") -> torch.Tensor:

@@ -13,7 +13,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib as L
-from .ops import pack, pack_gateup, route
+from .ops import pack, pack_gateup, route, route_hidden
 
 ROUTE_SIGMOID, ROUTE_SOFTMAX, ROUTE_SQRT_SOFTPLUS = L.ROUTE_SIGMOID, L.ROUTE_SOFTMAX, L.ROUTE_SQRT_SOFTPLUS
 
@@ -272,8 +272,13 @@ class BlockSparseMLP:
         if logits is None:
             if self.gate is None:
                 raise L.Exl3Error("BlockSparseMLP.forward: no router weight; pass logits")
-            logits = torch.matmul(y.half(), self.gate[:, :self.num_experts]).float()
-        ids, w = self.route_logits(logits)
+            if getattr(self, "_gate_t", None) is None:
+                self._gate_t = self.gate[:, :self.num_experts].t().contiguous().half()
+            ids, w, _ = route_hidden(y, self._gate_t, self.router_kind, self.num_experts_per_tok, bias=self.bias,
+                                     res=self.res, mul=self.mul, scale=self.routed_scaling_factor,
+                                     renorm=self.renormalize)
+        else:
+            ids, w = self.route_logits(logits)
         out = moe_forward(y, ids, w, self.table, self.act_limit, torch.float32)
         out = out.view(x.shape[:-1] + (self.hidden_size,))
         if out_dtype is not None:

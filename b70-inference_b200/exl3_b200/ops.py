@@ -335,23 +335,62 @@ def route(logits: torch.Tensor, kind: int, k: int, bias=None, res=None, mul=None
     return ids, w, wt
 
 
+ROUTE_HIDDEN_MAX_ROWS = 64
+
+
+def route_hidden(hidden: torch.Tensor, gate_t: torch.Tensor, kind: int, k: int, bias=None, res=None, mul=None,
+                 scale: float = 1.0, renorm: bool = True, want: bool = False, ids_dtype=torch.int32,
+                 logits_out: torch.Tensor | None = None):
+    """Top-k routing from hidden states [R, H] fp16/bf16 and the router weight transposed gate_t fp16 [E, H]:
+    logits = fp16(hidden @ gate_t^T) then `route`. Up to ROUTE_HIDDEN_MAX_ROWS rows: one fused launch (C ABI
+    exl3_route_hidden); more rows: a library GEMM for the logits, then exl3_route. logits_out (optional, fp16 [R, E])
+    receives the logits. Returns (ids, w, want or None)."""
+    L.require_cuda(hidden, gate_t)
+    h = _f16(hidden.reshape(-1, hidden.shape[-1]))
+    R, H = h.shape
+    E = gate_t.shape[0]
+    g = gate_t.half().contiguous()
+    if R > ROUTE_HIDDEN_MAX_ROWS:
+        logits = torch.matmul(h.float(), g.float().t()).half()
+        if logits_out is not None:
+            logits_out.copy_(logits)
+        return route(logits.float(), kind, k, bias, res, mul, scale, renorm, want, ids_dtype)
+    dev = h.device
+    ids = torch.empty((R, k), dtype=ids_dtype, device=dev)
+    w = torch.empty((R, k), dtype=torch.float32, device=dev)
+    wt = torch.empty((R, k), dtype=ids_dtype, device=dev) if want else None
+    b = bias.float().contiguous() if bias is not None else None
+    r = res.float().contiguous() if res is not None else None
+    m = mul.float().contiguous() if mul is not None else None
+    lo = logits_out
+    if lo is not None and (lo.dtype != torch.float16 or not lo.is_contiguous() or lo.numel() != R * E):
+        raise L.Exl3Error("route_hidden: logits_out must be a contiguous fp16 [R, E] tensor")
+    lib = L.lib()
+    ws = L.zeroed_workspace(dev, lib.exl3_route_hidden_workspace_size(R, E), "route_hidden")
+    rc = lib.exl3_route_hidden(h.data_ptr(), L.dtype_code(h.dtype), h.stride(0), R, H, g.data_ptr(), E, int(kind),
+                               int(k), L.ptr(b), L.ptr(r), L.ptr(m), float(scale), int(bool(renorm)), ids.data_ptr(),
+                               int(ids_dtype == torch.int64), w.data_ptr(), L.ptr(wt), L.ptr(lo), ws.data_ptr(),
+                               ws.numel(), L.stream_of(h))
+    L.check(rc, "exl3_route_hidden")
+    return ids, w, wt
+
+
 def routing_ds3_nogroup(hidden, gate, scores, bias, topk_indices, topk_weights, scaling_factor, gate_t, act_fn,
                         gate_i8, gate_sb, res=None):
     """Sigmoid / noaux_tc top-k routing (glm/xpu/glm_xpu/ops.py:177-193): logits = hidden @ gate rounded to fp16
-    (written to scores); selection by sigmoid + bias (+ residency bias `res`, glm/xpu/glm_xpu/block_graphs.py:
+    (written to scores; the routing GEMV runs in the router's launch, `route_hidden`); selection by sigmoid + bias (+ residency bias `res`, glm/xpu/glm_xpu/block_graphs.py:
     164-167); weights from the unbiased sigmoid, normalised over the picks and scaled. Writes scores, topk_indices,
     topk_weights in place."""
     if act_fn != 0:
         raise L.Exl3Error("routing_ds3_nogroup: sigmoid routing only (act_fn 0)")
     E = scores.shape[-1]
     k = topk_indices.shape[-1]
-    if hidden.dtype == gate.dtype == torch.half:
-        logits = torch.matmul(hidden, gate[:, :E])
-    else:
-        logits = torch.matmul(hidden.float(), gate[:, :E].float()).half()
-    scores.copy_(logits)
-    ids, w, _ = route(logits.float(), L.ROUTE_SIGMOID, k, bias=bias, res=res, scale=scaling_factor,
-                      ids_dtype=torch.int64 if topk_indices.dtype == torch.int64 else torch.int32)
+    gt = gate_t[:E] if gate_t is not None else gate[:, :E].t()
+    lo = torch.empty(scores.shape, dtype=torch.float16, device=scores.device)
+    ids, w, _ = route_hidden(hidden, gt, L.ROUTE_SIGMOID, k, bias=bias, res=res, scale=scaling_factor,
+                             ids_dtype=torch.int64 if topk_indices.dtype == torch.int64 else torch.int32,
+                             logits_out=lo)
+    scores.copy_(lo)
     topk_indices.copy_(ids)
     topk_weights.copy_(w)
 

@@ -167,6 +167,20 @@ EXL3_API int exl3_route(const float* logits, int ld, int R, int E, int kind, int
                const float* mul, float scale, int renorm, void* ids, int ids64, float* w, void* want,
                void* stream);
 
+/* Router from the hidden states: logits[r][e] = fp16(hidden[r] . gate_t[e]) (fp32 FMA dot, rounded to fp16 as the
+ * reference's routing GEMV does) computed in the same launch as the routing above (the CTA that finishes the logits
+ * last routes every row). hidden fp16/bf16 [R][H] (row stride ldh), gate_t fp16 [E][H] (the router weight
+ * transposed, as exllamav3's gate_t), R <= 64 (larger batches: a GEMM for the logits, then exl3_route).
+ * logits_out (optional) receives the fp16 logits (the reference's `scores`). workspace >=
+ * exl3_route_hidden_workspace_size(R, E), zeroed before its first use (each call leaves its ticket at zero).
+ * Replaces routing_ds3_nogroup's routing GEMV + top-k (glm/docs/ext-op-inventory.md:958-1004) and the reference's
+ * fused route (dsv41/xpu/csrc/dsv_moe_glue.sycl:442-520). */
+EXL3_API size_t exl3_route_hidden_workspace_size(int R, int E);
+EXL3_API int exl3_route_hidden(const void* hidden, int h_dtype, int ldh, int R, int H, const void* gate_t, int E,
+                               int kind, int k, const float* bias, const float* res, const float* mul, float scale,
+                               int renorm, void* ids, int ids64, float* w, void* want, void* logits_out,
+                               void* workspace, size_t ws_bytes, void* stream);
+
 /* ---- MoE decode ----
  * Routed MoE layer for decode batches: out[M][H] (fp32 or fp16) = sum_j w[m][j] * expert_{ids[m][j]}(x[m])
  * (+ expert E, the shared expert, with weight 1 when shared != 0), summed in slot order.

@@ -58,6 +58,37 @@ def test_route_bitexact(kind, R, E, k):
         np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("kind", [O.ROUTE_SIGMOID, O.ROUTE_SOFTMAX, O.ROUTE_SQRT_SOFTPLUS])
+@pytest.mark.parametrize("R,H,E,k,dt", [(1, 2048, 512, 10, torch.float16), (4, 6144, 160, 8, torch.bfloat16),
+                                        (37, 256, 1024, 32, torch.float16), (64, 512, 9, 3, torch.float16)])
+def test_route_hidden_fused(kind, R, H, E, k, dt):
+    """The router GEMV fused into the routing launch: fp16 logits within one ulp of the fp32 product, then ids
+    bit-exact and weights as the oracle router gives for those logits; repeated calls reuse the zeroed ticket."""
+    rng = np.random.default_rng(R + H + E + kind)
+    hid = torch.from_numpy(rng.standard_normal((R, H)).astype(np.float32)).to(DEV, dt)
+    gate_t = torch.from_numpy((rng.standard_normal((E, H)) / np.sqrt(H) * 3).astype(np.float16)).to(DEV)
+    bias = (rng.standard_normal(E) * 0.1).astype(np.float32)
+    res = np.zeros(E, dtype=np.float32)
+    res[rng.random(E) < 0.25] = 0.1
+    for _ in range(2):
+        lo = torch.empty((R, E), dtype=torch.float16, device=DEV)
+        ids, w, want = ops.route_hidden(hid, gate_t, kind, k, bias=to_dev(bias), res=to_dev(res), scale=2.5,
+                                        want=True, logits_out=lo)
+        # faithful fp16 rounding of the exact (fp64) product: one of its two fp16 neighbours (an fp32 sum in any
+        # order may land on either side of a rounding midpoint, as the reference's own GEMV may)
+        # plus the fp32 accumulation error, which dominates for logits that cancel to near zero
+        hd, gd = hid.double().cpu().numpy(), gate_t.double().cpu().numpy()
+        exact = hd @ gd.T
+        mag = np.abs(hd) @ np.abs(gd).T
+        got = lo.cpu().numpy().astype(np.float64)
+        ulp = np.abs(np.spacing(np.abs(exact).astype(np.float16))).astype(np.float64)
+        assert np.all(np.abs(got - exact) <= ulp + 64 * 2.0 ** -24 * mag), "logits are not a faithful fp16 rounding"
+        rid, rw, rwant = O.route(got, kind, k, bias=bias, res=res, scale=2.5, want=True)
+        assert np.array_equal(ids.cpu().numpy(), rid), "routed ids must be bit-exact"
+        assert np.array_equal(want.cpu().numpy(), rwant)
+        np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+
+
 def test_route_prefill_rows_and_int64():
     rng = np.random.default_rng(11)
     lg = rng.standard_normal((8192, 256)).astype(np.float32)
