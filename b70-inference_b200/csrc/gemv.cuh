@@ -175,7 +175,8 @@ __device__ __forceinline__ void rotated_block(const TIn* x, const __half* suh, i
 }
 
 // One consumer warp over one segment: its TPW tiles of one matrix on every tile-row of the stages its sub-group owns
-// (ring sequence numbers it with it % kSub == sub), continuing the CTA's ring sequence at `it`. The ring couples the
+// (ring sequence numbers it with it % kSub == sub, visited directly), continuing the CTA's ring sequence at `it` and
+// leaving it at the segment's end. The ring couples the
 // sub-groups: one that falls behind holds the producer back, and the others then wait and leave it the issue slots.
 // d[t] = D[16 n x 8 rows] of tile t: d[0], d[1] = (n = g, rows 2q, 2q+1), d[2], d[3] = (n = g + 8, rows 2q, 2q+1).
 template <int K, int TPW>
@@ -186,8 +187,10 @@ __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, in
     const int q = lane & 3;
     // B fragment of tile-row r for this lane: 8 bytes at xf_row + r * 16 + q * 4
     const uint2* bp = reinterpret_cast<const uint2*>(xf_row + q * 4);
-    for (int r0 = 0; r0 < n_rows; r0 += rps, ++it) {
-        if (it % kSub != sub) continue;
+    const int nst = (n_rows + rps - 1) / rps, it_begin = it;
+    for (int j = (sub - it % kSub + kSub) % kSub; j < nst; j += kSub) {
+        it = it_begin + j;
+        const int r0 = j * rps;
         const int s = it % kStages;
         const int rows = min(rps, n_rows - r0);
         uint2 bn = make_uint2(0, 0);
@@ -211,6 +214,7 @@ __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, in
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
+    it = it_begin + nst;
 }
 
 template <int TPW>

@@ -91,9 +91,12 @@ __device__ __forceinline__ float route_score(float v, int kind) {
     return v;
 }
 
-// One warp per row: scores in fp64 rounded once to fp32 and 64-bit selection keys in shared memory; k argmax passes
-// (lane-local scan + warp reduction, ties -> lowest index) with no block-wide barriers; the picks' weights are
-// evaluated in parallel, one lane per pick, and summed in slot order.
+// One warp per row. Scores in fp64 rounded once to fp32; selection key = order-preserving bits of the biased
+// score, ties to the lowest expert index. Each lane keeps its four best keys (experts lane, lane + 32, ...) sorted in
+// registers; a pick is the row's best head by two warp max reductions (key bits, then the negated index among the
+// lanes holding that key), and only the lane that owned it pops its head (rescanning its experts for the next four
+// once its list runs out). The picks' weights are evaluated in parallel, one lane per pick, and summed in slot order.
+// Code stays compact (loops, not unrolled expert scans): a router runs once per layer from a cold instruction cache.
 struct RouteParams {
     int E, kind, k;
     const float* bias;
@@ -107,94 +110,171 @@ struct RouteParams {
     void* want;
 };
 
-__device__ void route_row(const float* __restrict__ l, int row, const RouteParams& rp, float* sc, uint64_t* key,
-                          int lane) {
-    const int E = rp.E, kind = rp.kind, k = rp.k;
-    const float* bias = rp.bias;
-    const float* res = rp.res;
-    const float* mul = rp.mul;
-    const float scale = rp.scale;
-    const int renorm = rp.renorm, ids64 = rp.ids64;
-    void* ids = rp.ids;
-    float* w = rp.w;
-    void* want = rp.want;
+// A lane's best keys, best first; key 0 (below every real key: ordered_bits(-inf) > 0) = empty slot.
+struct LaneTop4 {
+    uint32_t c0, c1, c2, c3;
+    int e0, e1, e2, e3;
+};
 
-    // logits: every load of the row issued before any is used (one memory round trip), then the scores
-    float lmax = -INFINITY;
-    {
-        float v[kRouteMaxE / 32];
+// Insert (kv, e) scanned in ascending e: a key equal to a listed one goes after it (the lower index wins the tie).
+__device__ __forceinline__ void top4_insert(LaneTop4& t, uint32_t kv, int e) {
+    if (kv <= t.c3) return;
+    if (kv > t.c2) {
+        t.c3 = t.c2; t.e3 = t.e2;
+        if (kv > t.c1) {
+            t.c2 = t.c1; t.e2 = t.e1;
+            if (kv > t.c0) { t.c1 = t.c0; t.e1 = t.e0; t.c0 = kv; t.e0 = e; }
+            else { t.c1 = kv; t.e1 = e; }
+        } else {
+            t.c2 = kv; t.e2 = e;
+        }
+    } else {
+        t.c3 = kv; t.e3 = e;
+    }
+}
+
+// The lane's four best keys among its experts (bit j of `live`: expert lane + 32 j) that rank below (kl, el) when
+// `below`.
+template <int NPL>
+__device__ __forceinline__ LaneTop4 top4_fill(const uint32_t (&kh)[NPL], uint32_t live, int lane, bool below,
+                                              uint32_t kl, int el) {
+    LaneTop4 t = {0u, 0u, 0u, 0u, -1, -1, -1, -1};
 #pragma unroll
-        for (int j = 0; j < kRouteMaxE / 32; ++j) v[j] = (lane + 32 * j < E) ? l[lane + 32 * j] : -INFINITY;
-#pragma unroll
-        for (int j = 0; j < kRouteMaxE / 32; ++j) {
-            lmax = fmaxf(lmax, v[j]);
-            sc[lane + 32 * j] = v[j];
+    for (int j = 0; j < NPL; ++j) {
+        const int e = lane + 32 * j;
+        const uint32_t kv = kh[j];
+        if (((live >> j) & 1u) && (!below || kv < kl || (kv == kl && e > el))) top4_insert(t, kv, e);
+    }
+    return t;
+}
+
+// k argmax passes over the lane's keys; lane p < k returns pick p.
+template <int NPL>
+__device__ __forceinline__ int select_topk(const uint32_t (&kh)[NPL], uint32_t live, int k, int lane) {
+    LaneTop4 t = top4_fill<NPL>(kh, live, lane, false, 0u, 0);
+    int pick = -1;
+    for (int p = 0; p < k; ++p) {
+        const uint32_t top = __reduce_max_sync(0xFFFFFFFFu, t.c0);
+        const uint32_t cand = (t.e0 >= 0 && t.c0 == top) ? 0xFFFFFFFFu - (uint32_t)t.e0 : 0u;
+        const int e = (int)(0xFFFFFFFFu - __reduce_max_sync(0xFFFFFFFFu, cand));
+        if (lane == p) pick = e;
+        if ((e & 31) == lane) {                               // the owner pops its head
+            const uint32_t kl = t.c0;
+            t.c0 = t.c1; t.e0 = t.e1; t.c1 = t.c2; t.e1 = t.e2; t.c2 = t.c3; t.e2 = t.e3; t.c3 = 0u; t.e3 = -1;
+            if (t.e0 < 0) t = top4_fill<NPL>(kh, live, lane, true, kl, e);
         }
     }
-    __syncwarp();
-    if (kind != EXL3_ROUTE_SOFTMAX)
-        for (int e = lane; e < E; e += 32) sc[e] = route_score(sc[e], kind);
-    double denom = 1.0, dmax = 0.0;
-    if (kind == EXL3_ROUTE_SOFTMAX) {                         // softmax statistics (fp64), only for the weights
-        dmax = (double)warp_max(lmax);
-        double part = 0.0;
-        for (int e = lane; e < E; e += 32) part += exp((double)sc[e] - dmax);
+    return pick;
+}
+
+__device__ __forceinline__ uint32_t key_bits(float kv) { return ordered_bits(isnan(kv) ? -INFINITY : kv); }
+
+// s_sc: the warp's shared-memory row of kRouteMaxE scores. NPL = experts per lane (E <= 32 NPL).
+template <int NPL>
+__device__ void route_row(const float* __restrict__ l, int row, const RouteParams& rp, int lane,
+                          float* __restrict__ s_sc) {
+    const int E = rp.E, kind = rp.kind, k = rp.k;
+    // every global load of the row issued before any is used
+    float v[NPL], bv[NPL], rv[NPL], mv[NPL];
+    uint32_t valid = 0;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xFFFFFFFFu, part, o);
-        denom = part;
+    for (int j = 0; j < NPL; ++j) {
+        const int e = lane + 32 * j;
+        const bool ok = e < E;
+        valid |= (ok ? 1u : 0u) << j;
+        v[j] = ok ? l[e] : -INFINITY;
+        bv[j] = (ok && rp.bias) ? rp.bias[e] : 0.f;
+        rv[j] = (ok && rp.res) ? rp.res[e] : 0.f;
+        mv[j] = (ok && rp.mul) ? rp.mul[e] : 1.f;
+    }
+    float lmax = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+        lmax = fmaxf(lmax, v[j]);
+        if ((valid >> j) & 1u) s_sc[lane + 32 * j] = v[j];
+    }
+    __syncwarp();
+    float sc[NPL];
+    if (kind != EXL3_ROUTE_SOFTMAX) {                         // fp64 score functions: a compact loop in place
+#pragma unroll 2
+        for (int e = lane; e < E; e += 32) s_sc[e] = route_score(s_sc[e], kind);
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) sc[j] = ((valid >> j) & 1u) ? s_sc[lane + 32 * j] : -INFINITY;
+    } else {
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) sc[j] = v[j];
+    }
+    double denom = 1.0, dmax = 0.0;
+    if (kind == EXL3_ROUTE_SOFTMAX) {
+        // softmax statistics, only for the weights: fp32 exponentials of the fp64 differences, summed in fp64 (a
+        // relative error of a few 1e-8 in the denominator, which renormalised weights do not see)
+        dmax = (double)warp_max(lmax);
+        double part[4] = {0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+        for (int j = 0; j < NPL; ++j)
+            if ((valid >> j) & 1u) part[j & 3] += (double)expf((float)((double)sc[j] - dmax));
+        double tot = (part[0] + part[1]) + (part[2] + part[3]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
+        denom = tot;
     }
 
     for (int pass = 0; pass < 2; ++pass) {
-        if (pass == 1 && !want) break;
-        for (int e = lane; e < E; e += 32) {
-            float kv = sc[e];
-            if (pass == 0 && mul) kv = kv * mul[e];
-            if (bias) kv = kv + bias[e];
-            if (pass == 0 && res) kv = kv + res[e];
-            key[e] = pack_key(kv, e);
+        if (pass == 1 && !rp.want) break;
+        uint32_t kh[NPL];
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) {
+            float kv = sc[j];
+            if (pass == 0 && rp.mul) kv = kv * mv[j];
+            if (rp.bias) kv = kv + bv[j];
+            if (pass == 0 && rp.res) kv = kv + rv[j];
+            kh[j] = key_bits(kv);
         }
-        __syncwarp();
-        int pick = -1;                                        // lane j < k ends up holding pick j
-        for (int j = 0; j < k; ++j) {
-            uint64_t best = 0;
-            for (int e = lane; e < E; e += 32) best = key[e] > best ? key[e] : best;
-            best = warp_max_u64(best);
-            const int e = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFu));
-            if ((e & 31) == lane) key[e] = 0;                 // the owner lane clears the picked key
-            if (lane == j) pick = e;
-            __syncwarp();
-        }
+        const int pick = select_topk<NPL>(kh, valid, k, lane);
         if (pass == 0) {
             // weights from the unbiased score, summed over the picks in slot order
             float wv = 0.f;
-            if (lane < k) wv = kind == EXL3_ROUTE_SOFTMAX ? (float)(exp((double)l[pick] - dmax) / denom) : sc[pick];
+            if (lane < k)
+                wv = kind == EXL3_ROUTE_SOFTMAX ? (float)(exp((double)s_sc[pick] - dmax) / denom) : s_sc[pick];
             float tot = 0.f;
             for (int j = 0; j < k; ++j) tot += __shfl_sync(0xFFFFFFFFu, wv, j);
             if (lane < k) {
                 float o;
-                if (kind == EXL3_ROUTE_SOFTMAX) o = renorm ? wv / (tot + 1e-20f) : wv;
-                else o = wv * scale / (tot + 1e-20f);
-                w[(size_t)row * k + lane] = o;
-                if (ids64) static_cast<int64_t*>(ids)[(size_t)row * k + lane] = pick;
-                else static_cast<int32_t*>(ids)[(size_t)row * k + lane] = pick;
+                if (kind == EXL3_ROUTE_SOFTMAX) o = rp.renorm ? wv / (tot + 1e-20f) : wv;
+                else o = wv * rp.scale / (tot + 1e-20f);
+                rp.w[(size_t)row * k + lane] = o;
+                if (rp.ids64) static_cast<int64_t*>(rp.ids)[(size_t)row * k + lane] = pick;
+                else static_cast<int32_t*>(rp.ids)[(size_t)row * k + lane] = pick;
             }
         } else if (lane < k) {
-            if (ids64) static_cast<int64_t*>(want)[(size_t)row * k + lane] = pick;
-            else static_cast<int32_t*>(want)[(size_t)row * k + lane] = pick;
+            if (rp.ids64) static_cast<int64_t*>(rp.want)[(size_t)row * k + lane] = pick;
+            else static_cast<int32_t*>(rp.want)[(size_t)row * k + lane] = pick;
         }
-        __syncwarp();
     }
+    __syncwarp();
 }
 
+// Experts per lane of a row of E experts (a compiled instance of route_row).
+inline int route_npl(int E) { return E <= 128 ? 4 : E <= 256 ? 8 : E <= 512 ? 16 : 32; }
+
+__device__ __forceinline__ void route_row_any(const float* __restrict__ l, int row, const RouteParams& rp, int lane,
+                                              float* sc) {
+    if (rp.E <= 128) route_row<4>(l, row, rp, lane, sc);
+    else if (rp.E <= 256) route_row<8>(l, row, rp, lane, sc);
+    else if (rp.E <= 512) route_row<16>(l, row, rp, lane, sc);
+    else route_row<32>(l, row, rp, lane, sc);
+}
+
+template <int NPL>
 __global__ void __launch_bounds__(kRouteWarps * 32) k_route(const float* __restrict__ logits, int ld, int R,
                                                             const RouteParams rp) {
     __shared__ float s_score[kRouteWarps][kRouteMaxE];
-    __shared__ uint64_t s_key[kRouteWarps][kRouteMaxE];
     pdl_wait();                                               // logits may come from the previous kernel
     const int lane = threadIdx.x & 31, wr = threadIdx.x >> 5;
     const int row = blockIdx.x * kRouteWarps + wr;
     if (row >= R) return;
-    route_row(logits + (size_t)row * ld, row, rp, s_score[wr], s_key[wr], lane);
+    route_row<NPL>(logits + (size_t)row * ld, row, rp, lane, s_score[wr]);
 }
 
 // Router from the hidden states (the router GEMV fused into the launch): CTAs split the experts, one warp per expert
@@ -202,7 +282,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route(const float* __restr
 // fp16 as the reference's routing GEMV does, glm/docs/ext-op-inventory.md:980-1004) into the workspace; the CTA that
 // finishes last (atomic ticket, left at zero for the next call) routes every row.
 constexpr int kRhWarps = 8;
-constexpr int kRhRouteWarps = 3;                      // routing warps of the last CTA (static shared memory: 36 KB)
+constexpr int kRhRouteWarps = 8;                      // routing warps of the last CTA (static shared memory: 32 KB)
 constexpr int kRhMaxRows = 64;
 
 template <typename T>
@@ -211,7 +291,6 @@ __global__ void __launch_bounds__(kRhWarps * 32) k_route_hidden(const T* __restr
                                                                 __half* logits_out, unsigned int* ticket,
                                                                 const RouteParams rp) {
     __shared__ float s_score[kRhRouteWarps][kRouteMaxE];
-    __shared__ uint64_t s_key[kRhRouteWarps][kRouteMaxE];
     __shared__ int s_last;
     pdl_wait();                                               // hidden states come from the previous kernel
     const int lane = threadIdx.x & 31, wr = threadIdx.x >> 5;
@@ -255,7 +334,7 @@ __global__ void __launch_bounds__(kRhWarps * 32) k_route_hidden(const T* __restr
     __threadfence();
     if (wr >= kRhRouteWarps) return;
     for (int row = wr; row < R; row += kRhRouteWarps)
-        route_row(lg + (size_t)row * E, row, rp, s_score[wr], s_key[wr], lane);
+        route_row_any(lg + (size_t)row * E, row, rp, lane, s_score[wr]);
 }
 
 // ------------------------------------------------------------------------------------------------ align
@@ -395,6 +474,97 @@ __device__ void align_cta(const int32_t* __restrict__ ids, const float* __restri
     place_pairs(ids, w, topk, E, a0, a1, cnt + warp * E, o);
 }
 
+// Alignment of at most kAlignSmallPairs pairs by all warps of the CTA (decode batches): the same tables as
+// align_cta from warp votes, without block-wide scans. Every lane holds the experts of pairs lane and lane + 32; the
+// warp of pair i counts by ballot the valid pairs ranked before it (smaller expert, or the same expert and a smaller
+// index: its position), the pairs of its expert, and whether it is the expert's first pair, which then writes the
+// expert's items after those of all smaller experts. sm: 3 kAlignSmallPairs ints of shared memory.
+constexpr int kAlignSmallPairs = 64;
+
+__device__ void align_small(const int32_t* __restrict__ ids, const float* __restrict__ w, int npairs, int topk, int E,
+                            int M, int shared, int chunk, const AlignOut& o, int* sm) {
+    int* s_nch = sm;
+    int* s_pos = sm + kAlignSmallPairs;
+    int* s_cnt = sm + 2 * kAlignSmallPairs;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    int ej[2];
+    bool vj[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int j = lane + 32 * h;
+        ej[h] = j < npairs ? ids[j] : -1;
+        vj[h] = ej[h] >= 0 && ej[h] < E;
+    }
+    for (int i = warp; i < npairs; i += nw) {
+        const int ei = __shfl_sync(0xFFFFFFFFu, i < 32 ? ej[0] : ej[1], i & 31);
+        const bool vi = ei >= 0 && ei < E;
+        int pos = 0, cnt = 0;
+        bool first = true;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int j = lane + 32 * h;
+            const bool same = vj[h] && ej[h] == ei;
+            pos += __popc(__ballot_sync(0xFFFFFFFFu, vj[h] && (ej[h] < ei || (same && j < i))));
+            cnt += __popc(__ballot_sync(0xFFFFFFFFu, same));
+            if (__ballot_sync(0xFFFFFFFFu, same && j < i)) first = false;
+        }
+        if (lane == 0) {
+            s_nch[i] = (vi && first) ? (cnt + chunk - 1) / chunk : 0;
+            s_pos[i] = vi ? pos : -1;
+            s_cnt[i] = cnt;
+        }
+    }
+    __syncthreads();
+    int nch_j[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) nch_j[h] = lane + 32 * h < npairs ? s_nch[lane + 32 * h] : 0;
+    const int n_valid = __popc(__ballot_sync(0xFFFFFFFFu, vj[0])) + __popc(__ballot_sync(0xFFFFFFFFu, vj[1]));
+    const int n_routed_items = (int)__reduce_add_sync(0xFFFFFFFFu, (unsigned)(nch_j[0] + nch_j[1]));
+    const int shared_items = shared ? (M + chunk - 1) / chunk : 0;
+    for (int i = warp; i < npairs; i += nw) {
+        const int ei = __shfl_sync(0xFFFFFFFFu, i < 32 ? ej[0] : ej[1], i & 31);
+        const int pos = s_pos[i], nch = s_nch[i], cnt = s_cnt[i];
+        if (lane == 0) {
+            o.pair_of[i] = pos;
+            if (pos >= 0) {
+                o.pair_tok[pos] = i / topk;
+                o.pair_expert[pos] = ei;
+                o.pair_w[pos] = w[i];
+                o.pair_src[pos] = i;
+            }
+        }
+        if (nch) {                                            // warp-uniform: the expert's first pair
+            const unsigned below = (vj[0] && ej[0] < ei ? nch_j[0] : 0) + (vj[1] && ej[1] < ei ? nch_j[1] : 0);
+            const int ibase = (int)__reduce_add_sync(0xFFFFFFFFu, below);
+            for (int c = lane; c < nch; c += 32) {
+                o.item_expert[ibase + c] = ei;
+                o.item_start[ibase + c] = pos + c * chunk;
+                o.item_cnt[ibase + c] = min(chunk, cnt - c * chunk);
+            }
+        }
+    }
+    if (warp == 0) {
+        if (lane == 0) {
+            o.ws_i[0] = n_routed_items + shared_items;
+            o.ws_i[1] = n_valid;
+            o.ws_i[2] = n_valid + (shared ? M : 0);
+        }
+        if (shared) {
+            for (int m = lane; m < M; m += 32) {
+                o.pair_tok[n_valid + m] = m;
+                o.pair_expert[n_valid + m] = E;
+                o.pair_w[n_valid + m] = 1.0f;
+                o.pair_src[n_valid + m] = npairs + m;
+            }
+            for (int c = lane; c < shared_items; c += 32) {
+                o.item_expert[n_routed_items + c] = E;
+                o.item_start[n_routed_items + c] = n_valid + c * chunk;
+                o.item_cnt[n_routed_items + c] = min(chunk, M - c * chunk);
+            }
+        }
+    }
+}
+
 // Multi-CTA alignment of large pair counts (prefill), the same tables as align_cta: segments of kAlignSeg pairs,
 // pass 1 counts per (segment, expert), pass 2 gives each segment its offsets from those counts and places its pairs.
 constexpr int kAlignSeg = kAlignSegPairs;
@@ -462,7 +632,11 @@ __global__ void __launch_bounds__(kAlignThreads) k_align(const int32_t* __restri
                                                          const AlignOut o) {
     extern __shared__ int sm[];
     pdl_wait();
-    align_cta(ids, w, npairs, topk, E, M, shared, chunk, o, sm);
+    if (npairs <= kAlignSmallPairs) {
+        align_small(ids, w, npairs, topk, E, M, shared, chunk, o, sm);
+    } else {
+        align_cta(ids, w, npairs, topk, E, M, shared, chunk, o, sm);
+    }
 }
 
 // ------------------------------------------------------------------------------------------------ prepare
@@ -490,7 +664,8 @@ __global__ void __launch_bounds__(kAlignThreads) k_prepare(const PrepareArgs a) 
     const int npairs = a.M * a.topk;
     if (blockIdx.x == 0) {
         for (int i = threadIdx.x; i < a.n_tickets; i += kAlignThreads) a.tickets[i] = 0;
-        align_cta(a.ids, a.w, npairs, a.topk, a.E, a.M, a.shared, a.chunk, a.o, sm);
+        if (npairs <= kAlignSmallPairs) align_small(a.ids, a.w, npairs, a.topk, a.E, a.M, a.shared, a.chunk, a.o, sm);
+        else align_cta(a.ids, a.w, npairs, a.topk, a.E, a.M, a.shared, a.chunk, a.o, sm);
         __threadfence();
         __syncthreads();
         pdl_trigger();
@@ -863,8 +1038,15 @@ int exl3_route(const float* logits, int ld, int R, int E, int kind, int k, const
     EXL3_REQUIRE(kind >= 0 && kind <= 2, EXL3_ERR_ARG, "exl3_route: kind=%d", kind);
     if (R == 0) return EXL3_OK;
     const RouteParams rp = {E, kind, k, bias, res, mul, scale, renorm, ids, ids64, w, want};
-    cudaError_t e = launch_pdl(k_route, dim3((R + kRouteWarps - 1) / kRouteWarps), dim3(kRouteWarps * 32), 0,
-                               static_cast<cudaStream_t>(stream), logits, ld, R, rp);
+    const dim3 grid((R + kRouteWarps - 1) / kRouteWarps), block(kRouteWarps * 32);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e;
+    switch (route_npl(E)) {
+        case 4: e = launch_pdl(k_route<4>, grid, block, 0, st, logits, ld, R, rp); break;
+        case 8: e = launch_pdl(k_route<8>, grid, block, 0, st, logits, ld, R, rp); break;
+        case 16: e = launch_pdl(k_route<16>, grid, block, 0, st, logits, ld, R, rp); break;
+        default: e = launch_pdl(k_route<32>, grid, block, 0, st, logits, ld, R, rp); break;
+    }
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_route: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }

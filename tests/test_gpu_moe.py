@@ -39,10 +39,13 @@ def _status_clean():
 # ------------------------------------------------------------------------------------------------ router
 
 @pytest.mark.parametrize("kind", [O.ROUTE_SIGMOID, O.ROUTE_SOFTMAX, O.ROUTE_SQRT_SOFTPLUS])
-@pytest.mark.parametrize("R,E,k", [(1, 160, 8), (4, 512, 10), (37, 256, 8), (3, 1024, 32)])
-def test_route_bitexact(kind, R, E, k):
+@pytest.mark.parametrize("R,E,k", [(1, 160, 8), (4, 512, 10), (37, 256, 8), (3, 1024, 32), (5, 100, 7)])
+@pytest.mark.parametrize("ties", [False, True])
+def test_route_bitexact(kind, R, E, k, ties):
     rng = np.random.default_rng(R * E + kind)
     lg = rng.standard_normal((R, E)).astype(np.float32) * 3
+    if ties:                                             # many equal scores: the lowest expert index wins a tie
+        lg = np.round(lg * 2).astype(np.float32) / 2
     bias = (rng.standard_normal(E) * 0.1).astype(np.float32)
     res = np.zeros(E, dtype=np.float32)
     res[rng.random(E) < 0.25] = 0.1                      # resident subset preferred
@@ -162,6 +165,36 @@ def test_align_matches_oracle(M, k, E, shared):
         for j in range(0, M, 8):
             exp_items.append((E, nv + j, min(8, M - j)))
         assert np.array_equal(a["pair_tok"].cpu().numpy()[nv:], np.arange(M))
+    got = list(zip(a["item_expert"].tolist(), a["item_start"].tolist(), a["item_cnt"].tolist()))
+    assert got == exp_items
+
+
+@pytest.mark.parametrize("M,k,E,chunk", [(8, 8, 40, 3), (3, 7, 20, 2), (1, 1, 4, 1)])
+@pytest.mark.parametrize("shared", [False, True])
+def test_align_warp_path_hot_expert(M, k, E, chunk, shared):
+    """Decode-sized alignments (<= 64 pairs, one warp): several items per expert, dropped picks, shared rows."""
+    rng = np.random.default_rng(M * k + E + chunk)
+    ids = rng.integers(0, E, size=(M, k)).astype(np.int32)
+    ids[:, 0] = 3                                       # a hot expert picked by every token
+    ids[rng.random((M, k)) < 0.1] = -1
+    ids[0, -1] = E + 5                                  # out of range: dropped as well
+    w = rng.random((M, k)).astype(np.float32)
+    a = moe.moe_align(to_dev(ids), to_dev(w), E, shared=shared, chunk=chunk)
+    ref = O.moe_align(np.where((ids >= 0) & (ids < E), ids, -1), E)
+    nv = len(ref["pair_src"])
+    assert a["n_valid"] == nv
+    assert np.array_equal(a["pair_of"].cpu().numpy(), ref["pair_of"])
+    assert np.array_equal(a["pair_tok"].cpu().numpy()[:nv], ref["pair_tok"])
+    assert np.array_equal(a["pair_src"].cpu().numpy()[:nv], ref["pair_src"])
+    assert np.array_equal(a["pair_w"].cpu().numpy()[:nv], w.reshape(-1)[ref["pair_src"]])
+    exp_items = []
+    for e, s0, c in zip(ref["act_expert"], ref["act_start"], ref["act_cnt"]):
+        for j in range(0, int(c), chunk):
+            exp_items.append((int(e), int(s0) + j, min(chunk, int(c) - j)))
+    if shared:
+        for j in range(0, M, chunk):
+            exp_items.append((E, nv + j, min(chunk, M - j)))
+        assert np.array_equal(a["pair_src"].cpu().numpy()[nv:], M * k + np.arange(M))
     got = list(zip(a["item_expert"].tolist(), a["item_start"].tolist(), a["item_cnt"].tolist()))
     assert got == exp_items
 
