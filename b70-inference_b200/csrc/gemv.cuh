@@ -10,7 +10,7 @@
 // Schedule. A unit is (work item, 128-column block): the dense linear has n/128 units, a MoE launch one per
 // (expert item, column block). The launch's work is units x k-blocks (128 input rows each), laid out unit-major and
 // cut into equal contiguous ranges, one per CTA (one CTA per SM). In a CTA one producer warp streams the range through
-// a 16-stage shared-memory ring to 20 consumer warps: five sub-groups of four warps take the stages in turn, the four
+// a 10-stage shared-memory ring to 20 consumer warps: five sub-groups of four warps take the stages in turn, the four
 // warps of a sub-group covering all tiles of each tile-row; the shared ring keeps the sub-groups within a few
 // stages of each other. At the end of each segment the consumers park their accumulators in one of two shared-memory
 // slots and go on decoding; four epilogue warps sum them, reduce split units and run the epilogue. A CTA that covers a whole unit
@@ -50,12 +50,14 @@ enum { EPI_LINEAR = 0, EPI_GATEUP = 1, EPI_DOWN = 2 };
 constexpr int kTilesPerMat = 8;     // 128 output columns per unit and matrix (one Hadamard block)
 constexpr int kMaxRows = 8;         // MMA N dimension: input rows per unit
 constexpr int kStageBytes = 8192;   // ring stage (one bulk copy)
-constexpr int kStages = 16;         // ring stages per CTA (128 KB in flight)
+constexpr int kStages = 10;         // ring stages per CTA (80 KB in flight; the rest of the 256 KB stays L1 for the
+                                    // activation rows)
 constexpr int kConsumers = 4;       // consumer warps that cover one tile-row (all tiles of all matrices)
 constexpr int kSub = 5;             // consumer sub-groups; sub-group j takes ring stages j, j + kSub, ...
 constexpr int kConsumerWarps = kSub * kConsumers;
 constexpr int kEpilogueWarps = 4;   // reduce and finish units while the consumers decode the next segment
 constexpr int kGemvThreads = (1 + kConsumerWarps + kEpilogueWarps) * 32;   // producer, consumers, epilogue
+static_assert(kMaxRows % kEpilogueWarps == 0, "epilogue rows per warp");
 
 __host__ __device__ constexpr int nmat_of(int epi) { return epi == EPI_GATEUP ? 2 : 1; }
 __host__ __device__ constexpr int tiles_per_warp(int epi) { return nmat_of(epi) * kTilesPerMat / kConsumers; }
@@ -296,11 +298,21 @@ __device__ __forceinline__ UnitInfo<EPI> unit_info(const GemvArgs& a, int u, int
     return ui;
 }
 
-// Epilogue of one unit from its summed accumulators red[nmat][kMaxRows][128] (shared memory), one row per warp.
+// The epilogue operands of a unit for lane `lane` (columns cb * 128 + 4 lane ..+3) of epilogue warp ew: output
+// scales of each matrix, the down projection's input signs (gate|up), the routing weights of the warp's rows (down).
+// Loaded before the epilogue warps wait for the unit's accumulators, so that the dependent loads (expert descriptor,
+// then its vectors) stay off the end of the launch.
 template <int EPI>
-__device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<EPI>& ui, const float* red, int ew,
-                                              int lane) {
+struct EpiOperands {
+    float sv[nmat_of(EPI)][4];
+    float su_dn[4];                                           // gate|up: suh of the down projection
+    float w[kMaxRows / kEpilogueWarps];                       // down: routing weights of rows ew, ew + kEpilogueWarps
+};
+
+template <int EPI>
+__device__ __forceinline__ EpiOperands<EPI> epi_operands(const GemvArgs& a, const UnitInfo<EPI>& ui, int ew, int lane) {
     constexpr int NMAT = nmat_of(EPI);
+    EpiOperands<EPI> op;
     const int col = ui.cb * 128 + 4 * lane;
     const __half* svh[NMAT];
     if constexpr (EPI == EPI_LINEAR) {
@@ -310,11 +322,36 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
         if constexpr (EPI == EPI_GATEUP) {
             svh[0] = ed.svh[0];
             svh[NMAT - 1] = ed.svh[1];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) op.su_dn[j] = __half2float(ed.suh[2][col + j]);
         } else {
             svh[0] = ed.svh[2];
         }
     }
-    for (int row = ew; row < ui.Mi; row += kEpilogueWarps) {
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) op.sv[m][j] = __half2float(svh[m][col + j]);
+    if constexpr (EPI == EPI_DOWN) {
+#pragma unroll
+        for (int i = 0; i < kMaxRows / kEpilogueWarps; ++i) {
+            const int row = ew + i * kEpilogueWarps;
+            op.w[i] = row < ui.Mi ? __ldcg(a.items.pair_w + ui.s0 + row) : 0.f;
+        }
+    }
+    return op;
+}
+
+// Epilogue of one unit from its summed accumulators red[nmat][kMaxRows][128] (shared memory), one row per warp.
+template <int EPI>
+__device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<EPI>& ui, const float* red, int ew,
+                                              int lane, const EpiOperands<EPI>& op) {
+    constexpr int NMAT = nmat_of(EPI);
+    const int col = ui.cb * 128 + 4 * lane;
+#pragma unroll
+    for (int ri = 0; ri < kMaxRows / kEpilogueWarps; ++ri) {
+        const int row = ew + ri * kEpilogueWarps;
+        if (row >= ui.Mi) break;
         float v[NMAT][4];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
@@ -326,7 +363,7 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
             float o[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const float sv = __half2float(svh[0][col + j]);
+                const float sv = op.sv[0][j];
                 if (a.y_dtype == EXL3_F16)
                     o[j] = __half2float(__float2half_rn(__half2float(__float2half_rn(v[0][j] * kRsqrt128)) * sv));
                 else
@@ -348,21 +385,18 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
                 for (int j = 0; j < 4; ++j) yp[j] = __float2bfloat16_rn(o[j]);
             }
         } else if constexpr (EPI == EPI_GATEUP) {
-            const ExpertDesc& ed = a.experts[ui.expert];
             const float Lc = a.act_limit;
             float h[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
                 // gate/up outputs rounded to fp16 as the fp16 linear does: fp16(fp16(H(acc)*r) * svh)
-                float gg = __half2float(__float2half_rn(
-                    __half2float(__float2half_rn(v[0][j] * kRsqrt128)) * __half2float(svh[0][col + j])));
-                float uu = __half2float(__float2half_rn(
-                    __half2float(__float2half_rn(v[NMAT - 1][j] * kRsqrt128)) *
-                    __half2float(svh[NMAT - 1][col + j])));
+                float gg = __half2float(__float2half_rn(__half2float(__float2half_rn(v[0][j] * kRsqrt128)) * op.sv[0][j]));
+                float uu = __half2float(
+                    __float2half_rn(__half2float(__float2half_rn(v[NMAT - 1][j] * kRsqrt128)) * op.sv[NMAT - 1][j]));
                 float sg = silu_f(gg);
                 if (Lc != 0.f) { sg = fminf(sg, Lc); uu = fminf(fmaxf(uu, -Lc), Lc); }
                 const float act = __half2float(__float2half_rn(sg * uu));
-                h[j] = __half2float(__float2half_rn(act * __half2float(ed.suh[2][col + j])));
+                h[j] = __half2float(__float2half_rn(act * op.su_dn[j]));
             }
             fwht128_warp(h, lane);
 #pragma unroll
@@ -370,11 +404,11 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
             // the down projection's input block cb, straight into xf order
             store_xf_block(h, lane, a.xf_out + (size_t)(ui.s0 + row) * a.n + (size_t)ui.cb * 128);
         } else {
-            const float w = __ldcg(a.items.pair_w + ui.s0 + row);
+            const float w = op.w[ri];
             float o[4];
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                const float sv = __half2float(svh[0][col + j]);
+                const float sv = op.sv[0][j];
                 o[j] = a.ybuf_round_f16
                            ? w * __half2float(__float2half_rn(__half2float(__float2half_rn(v[0][j] * kRsqrt128)) * sv))
                            : w * (v[0][j] * kRsqrt128 * sv);
@@ -528,6 +562,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
         const int lo = i == 0 ? (int)(r0 - u * KB) : 0;
         const int hi = (int)min((long long)KB, r1 - u * KB);
         const UnitInfo<EPI> ui = i < kMaxSeg ? descs[i] : unit_info<EPI>(args, (int)u, NB, KB);
+        const EpiOperands<EPI> op = epi_operands<EPI>(args, ui, ew, lane);
         const int buf = i & 1;
         if (!to && !mbar_wait(&acc_full[buf], (i >> 1) & 1)) to = true;
         float* rb = red + (size_t)buf * kSub * UF;
@@ -599,7 +634,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
         }
         if (finish) {
             epilogue_sync();
-            unit_epilogue<EPI>(args, ui, rb, ew, lane);
+            unit_epilogue<EPI>(args, ui, rb, ew, lane, op);
         }
         epilogue_sync();                                      // the flag and red[buf] are read: release them
         if (lane == 0) mbar_arrive(&acc_empty[buf]);

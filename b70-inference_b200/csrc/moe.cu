@@ -158,11 +158,13 @@ __device__ __forceinline__ int select_topk(const uint32_t (&kh)[NPL], uint32_t l
         const uint32_t cand = (t.e0 >= 0 && t.c0 == top) ? 0xFFFFFFFFu - (uint32_t)t.e0 : 0u;
         const int e = (int)(0xFFFFFFFFu - __reduce_max_sync(0xFFFFFFFFu, cand));
         if (lane == p) pick = e;
-        if ((e & 31) == lane) {                               // the owner pops its head
-            const uint32_t kl = t.c0;
+        const bool own = (e & 31) == lane;
+        const uint32_t kl = t.c0;
+        if (own) {                                            // the owner pops its head
             t.c0 = t.c1; t.e0 = t.e1; t.c1 = t.c2; t.e1 = t.e2; t.c2 = t.c3; t.e2 = t.e3; t.c3 = 0u; t.e3 = -1;
-            if (t.e0 < 0) t = top4_fill<NPL>(kh, live, lane, true, kl, e);
         }
+        // rare (a lane held more than four of the picks so far): its next four, behind a warp-uniform branch
+        if (__any_sync(0xFFFFFFFFu, own && t.e0 < 0) && own) t = top4_fill<NPL>(kh, live, lane, true, kl, e);
     }
     return pick;
 }
@@ -174,6 +176,9 @@ template <int NPL>
 __device__ void route_row(const float* __restrict__ l, int row, const RouteParams& rp, int lane,
                           float* __restrict__ s_sc) {
     const int E = rp.E, kind = rp.kind, k = rp.k;
+    const float* __restrict__ bias = rp.bias;
+    const float* __restrict__ res = rp.res;
+    const float* __restrict__ mul = rp.mul;
     // every global load of the row issued before any is used
     float v[NPL], bv[NPL], rv[NPL], mv[NPL];
     uint32_t valid = 0;
@@ -183,9 +188,9 @@ __device__ void route_row(const float* __restrict__ l, int row, const RouteParam
         const bool ok = e < E;
         valid |= (ok ? 1u : 0u) << j;
         v[j] = ok ? l[e] : -INFINITY;
-        bv[j] = (ok && rp.bias) ? rp.bias[e] : 0.f;
-        rv[j] = (ok && rp.res) ? rp.res[e] : 0.f;
-        mv[j] = (ok && rp.mul) ? rp.mul[e] : 1.f;
+        bv[j] = (ok && bias) ? bias[e] : 0.f;
+        rv[j] = (ok && res) ? res[e] : 0.f;
+        mv[j] = (ok && mul) ? mul[e] : 1.f;
     }
     float lmax = -INFINITY;
 #pragma unroll
@@ -207,14 +212,16 @@ __device__ void route_row(const float* __restrict__ l, int row, const RouteParam
     }
     double denom = 1.0, dmax = 0.0;
     if (kind == EXL3_ROUTE_SOFTMAX) {
-        // softmax statistics, only for the weights: fp32 exponentials of the fp64 differences, summed in fp64 (a
-        // relative error of a few 1e-8 in the denominator, which renormalised weights do not see)
-        dmax = (double)warp_max(lmax);
-        double part[4] = {0.0, 0.0, 0.0, 0.0};
+        // softmax denominator, only for the weights: fp32 exponentials of the fp32 differences to the row maximum,
+        // four partial sums per lane, lanes summed in fp64 (relative error a few 1e-7, which renormalised weights do
+        // not see; the picks' own probabilities are evaluated in fp64)
+        const float fmax = warp_max(lmax);
+        dmax = (double)fmax;
+        float part[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int j = 0; j < NPL; ++j)
-            if ((valid >> j) & 1u) part[j & 3] += (double)expf((float)((double)sc[j] - dmax));
-        double tot = (part[0] + part[1]) + (part[2] + part[3]);
+            if ((valid >> j) & 1u) part[j & 3] += expf(sc[j] - fmax);
+        double tot = (double)((part[0] + part[1]) + (part[2] + part[3]));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
         denom = tot;
@@ -226,9 +233,9 @@ __device__ void route_row(const float* __restrict__ l, int row, const RouteParam
 #pragma unroll
         for (int j = 0; j < NPL; ++j) {
             float kv = sc[j];
-            if (pass == 0 && rp.mul) kv = kv * mv[j];
-            if (rp.bias) kv = kv + bv[j];
-            if (pass == 0 && rp.res) kv = kv + rv[j];
+            if (pass == 0 && mul) kv = kv * mv[j];
+            if (bias) kv = kv + bv[j];
+            if (pass == 0 && res) kv = kv + rv[j];
             kh[j] = key_bits(kv);
         }
         const int pick = select_topk<NPL>(kh, valid, k, lane);
