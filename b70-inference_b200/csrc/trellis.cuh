@@ -56,11 +56,13 @@ __device__ __forceinline__ void lane_states(uint32_t w0, uint32_t w1, uint32_t w
             const int r = s - 32, sh = r & 7, b = (r - sh) >> 3;
             v = __byte_perm(sh ? hi >> sh : hi, 0u, (uint32_t)(b | ((b + 1) << 4) | 0x4400));
         } else if (s >= 32) {
-            v = (s - 32 == 16) ? (hi >> 16) : ((hi >> (s - 32)) & 0xFFFFu);
+            // window at bit r = s - 32 of hi: shifted up against bit 31 (a constant left shift, which issues on its
+            // own pipe), then down by 16 (one ALU op instead of a shift and a mask)
+            v = (s - 32 == 16) ? (hi >> 16) : ((hi << (48 - s)) >> 16);
         } else if (s >= 16) {
             v = __funnelshift_r(mid, hi, s) & 0xFFFFu;
         } else if (s >= 0) {
-            v = (mid >> s) & 0xFFFFu;
+            v = (mid << (16 - s)) >> 16;
         } else {
             const uint32_t lo3 = w2 << off;                  // bits [b + 64, b + 96) (only the top ones are used)
             v = __funnelshift_r(lo3, mid, s + 32) & 0xFFFFu;
@@ -75,7 +77,8 @@ __device__ __forceinline__ uint32_t mul1_pair(uint32_t sa, uint32_t sb) {
     const uint32_t xb = sb * kMul1;
     const uint32_t ha = __dp4a(xa, 0x01010101u, 0x6400u);   // fp16 bits of 1024 + bytesum (< 2048: exact)
     const uint32_t hb = __dp4a(xb, 0x01010101u, 0x6400u);
-    uint32_t h2 = __byte_perm(ha, hb, 0x5410);               // {lo: ha, hi: hb}
+    // {lo: ha, hi: hb}: both < 2^16, so a shift-and-add (off the ALU pipe) packs them
+    const uint32_t h2 = ha + (hb << 16);
     uint32_t r;
     // fma in fp16x2 with the fp16 constants 0x1EEE (0.00676727294921875) and 0xC931 (-10.3828125): single rounding
     asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(h2), "r"(0x1EEE1EEEu), "r"(0xC931C931u));
