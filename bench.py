@@ -594,7 +594,7 @@ def run_ours(args, cfg):
 
 # DRAM bytes (read + write) per gate|up launch from the committed ncu capture
 # (profiles/k_gemv_moe_qwen_next_full.md), per workload; None where no capture was made.
-TRAFFIC_PER_LAUNCH: dict = {"qwen_next_decode": 31220224 + 33024}
+TRAFFIC_PER_LAUNCH: dict = {"qwen_next_decode": 31216384 + 39680}
 
 
 def main():
