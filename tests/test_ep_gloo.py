@@ -1,4 +1,4 @@
-"""Expert-parallel dispatch/combine on CPU gloo ranks (world size 2), with the oracle as each rank's local expert
+"""Expert-parallel dispatch/combine on CPU gloo ranks (world sizes 2 and 4), with the oracle as each rank's local expert
 compute, against the single-process oracle; and a rank that fails before the exchange surfaces as an error on its
 peer (short process-group timeout) instead of a hang. No GPU involved."""
 import os
@@ -86,15 +86,15 @@ def _worker(rank, world, port, mode, q):
             pass
 
 
-def _run(mode):
+def _run(mode, world=2):
     ctx = tmp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, mode, q)) for r in range(world)]
     for p in ps:
         p.start()
     res = {}
-    for _ in range(2):
+    for _ in range(world):
         r, st, v = q.get(timeout=180)
         res[r] = (st, v)
     for p in ps:
@@ -130,6 +130,22 @@ def test_ep_shared_expert_counted_once():
         x, ids, w = _tokens(r)
         ref = O.moe_forward(x, ids, w, experts, 10.0, shared=shared)
         assert_close(out, ref, what=f"EP rank {r} with shared expert")
+
+
+def test_ep_four_ranks_with_shared_expert():
+    """Four ranks (two experts each): every token's picks reach the owners of their experts and come back summed in
+    slot order, the shared expert once per token: the exchange pattern of the 4- and 8-GPU runs."""
+    from oracle import oracle as O
+    from tests.tolerance import assert_close
+    res = _run("shared", world=4)
+    experts = _experts()
+    shared = _experts(1, seed=7)[0]
+    for r in range(4):
+        st, out = res[r]
+        assert st == "ok", out
+        x, ids, w = _tokens(r)
+        ref = O.moe_forward(x, ids, w, experts, 10.0, shared=shared)
+        assert_close(out, ref, what=f"EP rank {r} of 4")
 
 
 def test_ep_rank_failure_is_reported_not_hung():
