@@ -564,8 +564,13 @@ __device__ __forceinline__ void fwht128_quad(float v[32], int lane) {
 // xh = fp16(H(fp16(v * s)) / sqrt(128)) for the quad's block (v: the lane's 32 values, s: its 32 signs), stored at
 // dst (the lane's 32 elements, 16-byte aligned) in the operand's k order: inside each 16-element group, k pair p goes
 // to pair slot p < 4 ? 2p : 2p - 7, i.e. the group's pair words in the order 0 4 1 5 2 6 3 7. `store` is per lane;
-// every lane of the warp must call this (the transform shuffles).
-__device__ __forceinline__ void rotate_store32(float v[32], const uint2 sraw[8], int lane, __half* dst, bool store) {
+// every lane of the warp must call this (the transform shuffles). The lanes' destinations are consecutive (lane l at
+// lane 0's + 64 l bytes, lane 0 storing): the warp's 2 KB go through `stage` (the warp's 128 uint4 of shared memory,
+// 16-byte chunks swizzled against bank conflicts) and out as four 512-byte contiguous stores.
+__device__ __forceinline__ int stage_slot(int src, int c) { return 4 * src + (c ^ ((src >> 1) & 3)); }
+
+__device__ __forceinline__ void rotate_store32(float v[32], const uint2 sraw[8], int lane, __half* dst, bool store,
+                                               uint4* stage) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
         float sg[4];
@@ -574,26 +579,34 @@ __device__ __forceinline__ void rotate_store32(float v[32], const uint2 sraw[8],
         for (int j = 0; j < 4; ++j) v[4 * c + j] = __half2float(__float2half_rn(v[4 * c + j] * sg[j]));
     }
     fwht128_quad(v, lane);
-    if (!store) return;
     uint32_t w[16];
 #pragma unroll
     for (int pp = 0; pp < 16; ++pp) {
         const __half2 h = __floats2half2_rn(v[2 * pp] * kRsqrt128, v[2 * pp + 1] * kRsqrt128);
         w[pp] = *reinterpret_cast<const uint32_t*>(&h);
     }
-    uint4* d = reinterpret_cast<uint4*>(dst);
 #pragma unroll
     for (int g = 0; g < 2; ++g) {
         const uint32_t* P = w + 8 * g;
-        d[2 * g] = make_uint4(P[0], P[4], P[1], P[5]);
-        d[2 * g + 1] = make_uint4(P[2], P[6], P[3], P[7]);
+        stage[stage_slot(lane, 2 * g)] = make_uint4(P[0], P[4], P[1], P[5]);
+        stage[stage_slot(lane, 2 * g + 1)] = make_uint4(P[2], P[6], P[3], P[7]);
     }
+    __syncwarp();
+    const unsigned long long base = __shfl_sync(0xFFFFFFFFu, reinterpret_cast<unsigned long long>(dst), 0);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const int src = 8 * g + (lane >> 2);                  // chunk 32 g + lane: chunk lane & 3 of lane src
+        if (__shfl_sync(0xFFFFFFFFu, store, src))
+            reinterpret_cast<uint4*>(base)[32 * g + lane] = stage[stage_slot(src, lane & 3)];
+    }
+    __syncwarp();                                             // the stage is reused by the warp's next job
 }
 
 // Rotated input rows of the dense linear, in the operand's k order: xh[m][k]. One warp per (row, 8 blocks).
 template <typename T>
 static __global__ void __launch_bounds__(256, 2) k_rotate_rows(const T* x, int ldx, int M, int k, const __half* suh,
                                                                __half* xh) {
+    __shared__ uint4 s_stage[8][128];
     pdl_wait();
     pdl_trigger();
     const int KB = k / 128, lane = threadIdx.x & 31, i = lane & 3;
@@ -610,7 +623,7 @@ static __global__ void __launch_bounds__(256, 2) k_rotate_rows(const T* x, int l
         float v[32];
 #pragma unroll
         for (int c = 0; c < 8; ++c) unpack4<T>(xr[c], v + 4 * c);
-        rotate_store32(v, sr, lane, xh + (size_t)row * k + off, act);
+        rotate_store32(v, sr, lane, xh + (size_t)row * k + off, act, s_stage[threadIdx.x >> 5]);
     }
 }
 
@@ -621,6 +634,7 @@ template <typename T>
 static __global__ void __launch_bounds__(256, 2) k_rotate_pairs(const T* x, int ldx, int H, int P, const int* n_pos,
                                                                 const int* pair_tok, const int* pair_expert,
                                                                 const ExpertDesc* experts, __half* a_gu) {
+    __shared__ uint4 s_stage[8][128];
     pdl_wait();
     pdl_trigger();
     const int KB = H / 128, lane = threadIdx.x & 31, i = lane & 3;
@@ -641,10 +655,10 @@ static __global__ void __launch_bounds__(256, 2) k_rotate_pairs(const T* x, int 
         float v[32];
 #pragma unroll
         for (int c = 0; c < 8; ++c) unpack4<T>(xr[c], v + 4 * c);
-        rotate_store32(v, gr, lane, a_gu + (size_t)pos * H + off, act);
+        rotate_store32(v, gr, lane, a_gu + (size_t)pos * H + off, act, s_stage[threadIdx.x >> 5]);
 #pragma unroll
         for (int c = 0; c < 8; ++c) unpack4<T>(xr[c], v + 4 * c);
-        rotate_store32(v, ur, lane, a_gu + ((size_t)P + pos) * H + off, act);
+        rotate_store32(v, ur, lane, a_gu + ((size_t)P + pos) * H + off, act, s_stage[threadIdx.x >> 5]);
     }
 }
 
@@ -654,6 +668,7 @@ static __global__ void __launch_bounds__(256, 2) k_rotate_pairs(const T* x, int 
 static __global__ void __launch_bounds__(256, 2) k_act(const __half* gu, int I, int P, const int* n_pos,
                                                        const int* pair_expert, const ExpertDesc* experts,
                                                        float act_limit, __half* a_dn) {
+    __shared__ uint4 s_stage[8][128];
     pdl_wait();
     pdl_trigger();
     const int KB = I / 128, lane = threadIdx.x & 31, i = lane & 3;
@@ -685,7 +700,7 @@ static __global__ void __launch_bounds__(256, 2) k_act(const __half* gu, int I, 
                 v[4 * c + j] = __half2float(__float2half_rn(sg * uu));
             }
         }
-        rotate_store32(v, sr, lane, a_dn + (size_t)pos * I + off, act);
+        rotate_store32(v, sr, lane, a_dn + (size_t)pos * I + off, act, s_stage[threadIdx.x >> 5]);
     }
 }
 
