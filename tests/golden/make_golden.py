@@ -2,13 +2,17 @@
 
 Run in a container where the reference tree is mounted (default /root/reference, or $B70_REFERENCE):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py            # every fixture
+    python tests/golden/make_golden.py softmax    # only route_softmax.npz
 
 What runs (all from horvay/b70-inference, unmodified, imported or exec'd from its files):
   * glm/xpu/tests/units.py:42-89  -- mul1_lut, w_hat, H128, ref_linear (the reference's own torch restatement of
     the EXL3 linear, fp64); the module body needs an XPU, so only that line range is exec'd;
   * glm/xpu/glm_xpu/ops.py        -- routing_ds3_nogroup (sigmoid router), silu_mul, had_r_128;
-  * dsv41/xpu/dsv_xpu/moe.py      -- route() (sqrt-softplus router with the residency bias), its torch path.
+  * dsv41/xpu/dsv_xpu/moe.py      -- route() (sqrt-softplus router with the residency bias), its torch path;
+  * trellis-serve.patch            -- fused_xpu.py's Triton `_router_kernel` / `router` (the Qwen-Next softmax router
+    with the cold-tier bias and the RAM margin), cut out of the patch text and run on CPU under Triton's interpreter
+    (TRITON_INTERPRET=1).
 The outputs are small .npz files with seeded inputs and the reference's outputs; tests compare the oracle and the
 CUDA path against them. Nothing here runs at test time.
 """
@@ -18,6 +22,9 @@ import json
 import os
 import sys
 import types
+
+# the softmax router is a Triton kernel: run it with Triton's CPU interpreter (must be set before triton loads)
+os.environ.setdefault("TRITON_INTERPRET", "1")
 
 import numpy as np
 import torch
@@ -37,7 +44,69 @@ def load_units_slice():
     return ns
 
 
+def load_fused_router():
+    """The reference's softmax router: trellis-serve.patch adds xpu/exl3xpu/fused_xpu.py as a new file; its
+    `_router_kernel` (Triton) and `router` wrapper are cut out of the patch text (lines starting with '+') and exec'd
+    with their own imports. Nothing of them is changed."""
+    path = os.path.join(REF, "trellis-serve.patch")
+    lines = open(path).read().splitlines()
+    start = next(i for i, l in enumerate(lines) if l.startswith("+++ ") and l.endswith("xpu/exl3xpu/fused_xpu.py"))
+    end = next(i for i in range(start + 1, len(lines)) if lines[i].startswith("diff --git"))
+    src = "\n".join(l[1:] for l in lines[start + 1:end] if l.startswith("+"))
+    i0 = src.index("@triton.jit\ndef _router_kernel")
+    i1 = src.index("@triton.jit", i0 + 10)
+    body = src[i0:i1]
+    assert "def router(logits" in body and "tl.argmax" in body, "fused_xpu.py layout changed"
+    ns = {}
+    exec(compile("import os\nimport torch\nimport triton\nimport triton.language as tl\n" + body, path, "exec"), ns)
+    return ns["router"]
+
+
+def make_softmax():
+    """route_softmax.npz: the reference's fused softmax router (Triton, CPU interpreter) on seeded logits, with and
+    without the cold-tier bias / RAM margin, with and without renormalisation, on tie-heavy logits and on an expert
+    count that is not a power of two."""
+    router = load_fused_router()
+    rng = np.random.default_rng(20261202)
+    cases = {}
+    # (R, E, k, renorm, bias?, margin?, quantised logits for ties?)
+    specs = [("plain", 8, 512, 10, True, False, False, False),
+             ("cold_margin", 8, 512, 10, True, True, True, False),
+             ("cold_only", 4, 512, 10, True, True, False, False),
+             ("norenorm", 4, 512, 10, False, True, True, False),
+             ("ties", 6, 512, 10, True, True, True, True),
+             ("e160", 4, 160, 8, True, True, True, False)]
+    for name, R, E, k, renorm, has_cold, has_margin, ties in specs:
+        lg = rng.standard_normal((R, E)).astype(np.float32)
+        if ties:
+            lg = (np.round(lg * 4) / 4).astype(np.float32)          # many equal logits
+        cold = slot = margin = None
+        if has_cold:
+            cold = np.zeros(E, dtype=np.float32)
+            cold[rng.random(E) < 0.15] = -1e4                       # NVMe-only experts
+        if has_margin:
+            slot = np.where(rng.random(E) < 0.6, np.arange(E), -1).astype(np.int32)   # -1: not in a VRAM slot
+            margin = np.array([0.5], dtype=np.float32)
+        w, ids = router(torch.from_numpy(lg), k, renorm,
+                        cold=None if cold is None else torch.from_numpy(cold),
+                        slot_of=None if slot is None else torch.from_numpy(slot),
+                        margin=None if margin is None else torch.from_numpy(margin))
+        d = {"logits": lg, "k": k, "renorm": int(renorm), "ids": ids.numpy(), "w": w.numpy()}
+        if cold is not None:
+            d["cold"] = cold
+        if slot is not None:
+            d["slot_of"] = slot
+            d["margin"] = margin
+        for kk, v in d.items():
+            cases[f"{name}__{kk}"] = np.asarray(v)
+    np.savez_compressed(os.path.join(HERE, "route_softmax.npz"), **cases)
+
+
 def main():
+    if sys.argv[1:] == ["softmax"]:
+        make_softmax()
+        print("route_softmax.npz written to", HERE)
+        return
     sys.path.insert(0, os.path.join(REF, "glm/xpu"))
     sys.path.insert(0, os.path.join(REF, "dsv41/xpu"))
     from glm_xpu import ops as glm_ops            # noqa: E402
@@ -152,6 +221,8 @@ def main():
             out[m] += float(wsel[m, j]) * d
     np.savez_compressed(os.path.join(HERE, "moe_expert.npz"), x=x, sel=sel, w=wsel, out=out, Ks=np.array(Ks),
                         H=H, I=I, act_limit=L, **ex)
+
+    make_softmax()
 
     with open(os.path.join(HERE, "known_answers.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)

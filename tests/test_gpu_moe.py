@@ -111,6 +111,18 @@ def test_route_golden_sigmoid():
     np.testing.assert_allclose(w.cpu().numpy(), d["w"], rtol=2e-6, atol=1e-7)
 
 
+@pytest.mark.parametrize("name", ["plain", "cold_margin", "cold_only", "norenorm", "ties", "e160"])
+def test_route_golden_softmax(name):
+    # the reference's own softmax router (trellis-serve.patch:394-441, run by make_golden.py under Triton's CPU
+    # interpreter): cold-tier bias as the key bias, the RAM margin as the residency bias on slotless experts
+    from tests.test_oracle_golden import softmax_case
+    lg, k, renorm, bias, res, ids_ref, w_ref = softmax_case(name)
+    ids, w, _ = ops.route(to_dev(lg), O.ROUTE_SOFTMAX, k, bias=None if bias is None else to_dev(bias),
+                          res=None if res is None else to_dev(res), renorm=renorm)
+    assert np.array_equal(ids.cpu().numpy(), ids_ref.astype(np.int32)), "routed ids must be bit-exact"
+    np.testing.assert_allclose(w.cpu().numpy(), w_ref, rtol=2e-6, atol=1e-9)
+
+
 def test_routing_ds3_nogroup_api():
     """The reference op's signature: logits from hidden @ gate (fp16), outputs written in place."""
     rng = np.random.default_rng(4)

@@ -103,6 +103,31 @@ def test_softmax_router_semantics():
         np.testing.assert_allclose(w[r], pw / pw.sum(), rtol=1e-6)
 
 
+SOFTMAX_CASES = ["plain", "cold_margin", "cold_only", "norenorm", "ties", "e160"]
+
+
+def softmax_case(name):
+    """One case of route_softmax.npz (the reference's Triton router run under the CPU interpreter) as exl3_route
+    arguments: the cold-tier bias is the key bias, the RAM margin becomes the residency bias -margin on experts
+    without a device slot (trellis-serve.patch:404-407)."""
+    d = load("route_softmax.npz")
+    g = {kk.split("__", 1)[1]: d[kk] for kk in d.files if kk.startswith(name + "__")}
+    bias = g.get("cold")
+    res = None
+    if "slot_of" in g:
+        res = np.where(g["slot_of"] < 0, -np.float32(g["margin"][0]), np.float32(0.0)).astype(np.float32)
+    return g["logits"], int(g["k"]), bool(g["renorm"]), bias, res, g["ids"], g["w"]
+
+
+@pytest.mark.parametrize("name", SOFTMAX_CASES)
+def test_softmax_router_matches_reference(name):
+    lg, k, renorm, bias, res, ids_ref, w_ref = softmax_case(name)
+    ids, w, _ = O.route(lg, O.ROUTE_SOFTMAX, k, bias=bias, res=res, renorm=renorm)
+    assert np.array_equal(ids, ids_ref.astype(ids.dtype))
+    # the reference evaluates the softmax in fp32 (exp, sum, divide); the oracle in fp64 rounded once
+    np.testing.assert_allclose(w, w_ref, rtol=2e-6, atol=1e-9)
+
+
 def test_router_ties_go_to_lowest_index():
     lg = np.zeros((2, 64), dtype=np.float32)
     ids, _, _ = O.route(lg, O.ROUTE_SOFTMAX, 4)
