@@ -48,8 +48,10 @@ int* device_status_ptr();
 
 constexpr uint32_t kMul1 = 0x83DCD12Du;
 constexpr float kRsqrt128 = 0.08838834764831845f;
-// Upper bound on polling iterations of any device-side wait (mbarrier try_wait already suspends in hardware between
-// polls); a wait that runs out records EXL3_ERR_TIMEOUT in the kernel's status word and the kernel returns.
+// Every device-side wait is bounded in time: a wait that has not completed after kWaitLimitNs of the global timer
+// (100 ms; no wait of a healthy launch comes near it) gives up, the kernel records EXL3_ERR_TIMEOUT in its status
+// word, lets its own copies in flight land and returns. kSpinLimit caps the polls as well, in case the timer stalls.
+constexpr uint64_t kWaitLimitNs = 100ull * 1000 * 1000;
 constexpr uint32_t kSpinLimit = 1u << 24;
 
 __device__ __forceinline__ float h2f(__half h) { return __half2float(h); }
@@ -83,10 +85,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: returns false when the limit ran out.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i)
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait: returns false when limit_ns of global time (or kSpinLimit polls) passed without completion. The
+// fast path is one try_wait; the timer is read once per 32 polls after that.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = kWaitLimitNs) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1; i < kSpinLimit; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 31) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
+    }
     return false;
 }
 __device__ __forceinline__ void fence_barrier_init() {

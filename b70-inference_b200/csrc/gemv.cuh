@@ -129,14 +129,6 @@ __host__ __device__ __forceinline__ Smem smem_layout(int epi) {
     return s;
 }
 
-// Optional per-CTA timeline for performance investigation: a harness that defines EXL3_TRACE before including this
-// file provides `exl3_trace_point(slot)`, which records the global timer; otherwise the hooks compile to nothing.
-#ifdef EXL3_TRACE
-#define EXL3_TRACE_POINT(slot) exl3_trace_point(slot)
-#else
-#define EXL3_TRACE_POINT(slot)
-#endif
-
 // ---- programmatic dependent launch ----
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -437,7 +429,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
     constexpr int UF = unit_floats(EPI);
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x == 0) EXL3_TRACE_POINT(0);
     pdl_trigger();
     const int NB = args.n / 128, KB = args.k / 128;
     const long long G = gridDim.x;
@@ -491,7 +482,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
                     bulk_g2s(ring + (size_t)s * kStageBytes, src + (size_t)r * ui.row_stride, bytes, &full[s]);
                 }
             }
-            EXL3_TRACE_POINT(7);
             if (to) report(args.status, EXL3_ERR_TIMEOUT);
             // every issued copy has landed before the CTA can retire its shared memory: stage s last held sequence
             // number s + kStages * floor((it - 1 - s) / kStages)
@@ -510,7 +500,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
         const int m = (cq * TPW) / kTilesPerMat, tile0 = (cq * TPW) % kTilesPerMat;
         const int g = lane >> 2, q = lane & 3;
         pdl_wait();                                           // activations come from earlier kernels
-        if (threadIdx.x == 32) EXL3_TRACE_POINT(1);
         bool to = false;
         int it = 0;
         for (int i = 0; i < n_seg; ++i) {
@@ -548,7 +537,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
             if (lane == 0) mbar_arrive(&acc_full[buf]);
         }
         if (to) report(args.status, EXL3_ERR_TIMEOUT);
-        if (threadIdx.x == 32) EXL3_TRACE_POINT(6);
         return;
     }
 

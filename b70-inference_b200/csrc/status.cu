@@ -45,9 +45,30 @@ int* device_status_ptr() {
     return cache[dev];
 }
 
+// A wait nothing completes: one thread initialises an mbarrier that expects one arrival and waits on it with the
+// library's bounded wait and the given limit. The wait runs out, the kernel records EXL3_ERR_TIMEOUT and returns.
+static __global__ void k_wait_probe(uint64_t limit_ns, int* status) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x != 0) return;
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+    if (!mbar_wait(&bar, 0, limit_ns)) report(status, EXL3_ERR_TIMEOUT);
+}
+
 }  // namespace exl3
 
 extern "C" {
+
+int exl3_wait_probe(uint64_t limit_ns, void* stream) {
+    EXL3_REQUIRE(limit_ns > 0 && limit_ns <= exl3::kWaitLimitNs, EXL3_ERR_ARG,
+                 "exl3_wait_probe: limit %llu ns outside (0, %llu]", (unsigned long long)limit_ns,
+                 (unsigned long long)exl3::kWaitLimitNs);
+    int* status = exl3::device_status_ptr();
+    EXL3_REQUIRE(status, EXL3_ERR_CUDA, "exl3_wait_probe: status word lookup failed");
+    exl3::k_wait_probe<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, status);
+    EXL3_LAUNCH_CHECK("exl3_wait_probe");
+    return EXL3_OK;
+}
 
 int exl3_version(void) { return 100; }
 

@@ -1,7 +1,7 @@
 """Routed-expert MoE on B200: expert pointer tables, the decode-path moe_forward, and a BlockSparseMLP module with the
 reference's load/forward API.
 
-Reference: glm/xpu/glm_xpu/moe_patch.py:541-620 (BlockSparseMLP forward = router + routed sum + shared expert),
+Reference: glm/xpu/glm_xpu/moe_patch.py:15-94 (BlockSparseMLP load/forward = router + routed sum + shared expert),
 glm/xpu/csrc/exl3_moe.n128.sycl:1338-1439 (moe_forward over expert pointer tables), dsv41/xpu/dsv_xpu/moe.py:
 914-994,1563-1630 (router with residency bias, per-pick expert math, module forward).
 """
@@ -235,7 +235,7 @@ def moe_align(topk_ids: torch.Tensor, topk_w: torch.Tensor, E: int, shared: bool
 
 
 class BlockSparseMLP:
-    """Routed-expert MLP block with the reference's module API (glm/xpu/glm_xpu/moe_patch.py:541-620):
+    """Routed-expert MLP block with the reference's module API (glm/xpu/glm_xpu/moe_patch.py:66-94):
     forward(x, params, out_dtype) = router (with residency bias) -> routed sum on the MoE kernels + shared expert.
 
     router_kind: ROUTE_SIGMOID (GLM / DeepSeek-V3 noaux_tc), ROUTE_SOFTMAX (Qwen-Next), ROUTE_SQRT_SOFTPLUS

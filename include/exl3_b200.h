@@ -63,6 +63,12 @@ EXL3_API int exl3_version(void);
 EXL3_API const char* exl3_last_error(void);
 /* Device status word (sticky EXL3_ERR_TIMEOUT from bounded device waits); reset != 0 clears it. Synchronous. */
 EXL3_API int exl3_device_status(int reset);
+/* Failure-path check of the bounded device waits: launches one thread that waits, with the library's wait and a
+ * limit of limit_ns (0 < limit_ns <= 100 ms, the library's own limit), on an mbarrier that nothing completes. The
+ * wait runs out, EXL3_ERR_TIMEOUT is recorded in the device status word and the kernel returns; the context stays
+ * usable. Every kernel's waits (TMA stages, accumulator hand-offs, tensor-memory stages) use the same wait with the
+ * 100 ms limit. No reference counterpart: the reference's SYCL kernels do not wait on one another. */
+EXL3_API int exl3_wait_probe(uint64_t limit_ns, void* stream);
 
 /* ---- dequantisation ----
  * W_hat[:, n0 : n0 + n_slice] -> w (fp16 [k][n_slice], row stride ldw elements), Hadamard domain, no scales.
@@ -118,11 +124,11 @@ EXL3_API int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void
                           void* workspace, size_t ws_bytes, void* stream);
 
 /* No-allocation variant of exl3_gemv: same arguments minus the workspace and n_ctas; its scratch is a fixed
- * file-scope device array (about 2.3 MB per device), for callers that cannot allocate device memory. Limits: M <= 8,
- * k <= 32768, n <= 65536 (larger shapes return EXL3_ERR_UNSUPPORTED). Calls on one device that may overlap race on
- * the shared scratch: order them on one stream. Make the first call on each device outside stream capture (it looks
- * up the scratch's address). No reference counterpart: the reference allocates its scratch per call
- * (glm/xpu/csrc/exl3_ops.sycl:286-300). */
+ * file-scope device array (1,837,056 bytes per device that loads the library: the rotated input rows, the split
+ * tickets and the partial slots, sized from the limits below), for callers that cannot allocate device memory.
+ * Limits: M <= 8, k <= 32768, n <= 65536 (larger shapes return EXL3_ERR_UNSUPPORTED). Calls on one device that may
+ * overlap race on the shared scratch: order them on one stream. Make the first call on each device outside stream
+ * capture (it looks up the scratch's address). No reference counterpart. */
 EXL3_API int exl3_gemv_noalloc(const void* x, int x_dtype, int ldx, int M, const void* packed, const void* suh,
                                const void* svh, int k, int n, int K, int cb, void* y, int y_dtype, int ldy,
                                void* stream);
