@@ -76,11 +76,20 @@ def trellis_words(trellis: np.ndarray) -> np.ndarray:
 
 
 def tile_states(trellis: np.ndarray, K: int) -> np.ndarray:
-    """uint16 states [tk, tn, 256] in ring-position order."""
-    words = trellis_words(trellis).astype(np.uint64)
+    """uint16 states [tk, tn, 256] in ring-position order: state(t) = ((word[il] << 32 | word[ih]) >> sh) & 0xFFFF,
+    evaluated position by position on whole [tk, tn] word planes in uint32 arithmetic (the high word contributes
+    word[il] << (32 - sh) when sh > 0 and nothing when sh == 0)."""
+    words = trellis_words(trellis)
     il, ih, sh, _, _ = tile_tables(K)
-    st = (((words[..., il] << np.uint64(32)) | words[..., ih]) >> sh.astype(np.uint64)) & np.uint64(0xFFFF)
-    return st.astype(np.uint16)
+    tk, tn, _ = words.shape
+    st = np.empty((tk, tn, 256), dtype=np.uint16)
+    for t in range(256):
+        s_ = int(sh[t])
+        v = words[..., ih[t]] >> np.uint32(s_)
+        if s_ > 0:
+            v = v | (words[..., il[t]] << np.uint32(32 - s_))
+        st[..., t] = (v & np.uint32(0xFFFF)).astype(np.uint16)
+    return st
 
 
 def w_hat(trellis: np.ndarray, K: int) -> np.ndarray:

@@ -33,11 +33,11 @@ def _experts(n=E, seed=42):
     return ex
 
 
-def _tokens(rank):
+def _tokens(rank, b=B):
     rng = np.random.default_rng(100 + rank)
-    x = rng.standard_normal((B, H)).astype(np.float16)
-    ids = np.stack([rng.permutation(E)[:TOPK] for _ in range(B)]).astype(np.int32)
-    w = rng.random((B, TOPK)).astype(np.float32)
+    x = rng.standard_normal((b, H)).astype(np.float16)
+    ids = np.stack([rng.permutation(E)[:TOPK] for _ in range(b)]).astype(np.int32)
+    w = rng.random((b, TOPK)).astype(np.float32)
     return x, ids, w
 
 
@@ -71,11 +71,23 @@ def _worker(rank, world, port, mode, q):
             def shared_fn(x):
                 return torch.from_numpy(O.expert_forward(x.numpy(), shared, 10.0).astype(np.float32))
 
-        m = ep.ExpertParallelMoE(E, H, TOPK, local_fn=local_fn, shared_fn=shared_fn)
-        x, ids, w = _tokens(rank)
+        cap = 4 if mode == "uneven" else None
+        m = ep.ExpertParallelMoE(E, H, TOPK, local_fn=local_fn, shared_fn=shared_fn, capacity=cap)
+        x, ids, w = _tokens(rank, _batch(mode, rank))
         if mode == "fail" and rank == 1:
             raise RuntimeError("rank 1 fails before the dispatch")
         out = m.forward(torch.from_numpy(x), torch.from_numpy(ids), torch.from_numpy(w))
+        if mode == "uneven":                     # a second call with a smaller batch on the same layer
+            x2, ids2, w2 = _tokens(rank + 10, 1)
+            out2 = m.forward(torch.from_numpy(x2), torch.from_numpy(ids2), torch.from_numpy(w2))
+            try:
+                x3, ids3, w3 = _tokens(rank, 5)
+                m.forward(torch.from_numpy(x3), torch.from_numpy(ids3), torch.from_numpy(w3))
+                over = "no error"
+            except ValueError as exc:            # raised before any collective: the ranks stay in step
+                over = str(exc)
+            q.put((rank, "ok", (out.numpy(), out2.numpy(), over)))
+            return
         q.put((rank, "ok", out.numpy()))
     except Exception as exc:      # reported to the parent, which decides pass/fail
         q.put((rank, "error", repr(exc)))
@@ -84,6 +96,11 @@ def _worker(rank, world, port, mode, q):
             dist.destroy_process_group()
         except Exception:
             pass
+
+
+def _batch(mode, rank):
+    """Rows per rank: B everywhere, or uneven batches below the capacity of 4."""
+    return (3, 2, 4, 1)[rank] if mode == "uneven" else B
 
 
 def _run(mode, world=2):
@@ -146,6 +163,26 @@ def test_ep_four_ranks_with_shared_expert():
         x, ids, w = _tokens(r)
         ref = O.moe_forward(x, ids, w, experts, 10.0, shared=shared)
         assert_close(out, ref, what=f"EP rank {r} of 4")
+
+
+def test_ep_uneven_batches_under_a_fixed_capacity():
+    """Ranks with different batch sizes (3, 2, 4, 1 rows) under one capacity (4): padding rows carry no picks, each
+    rank gets its own rows' routed sums; a second call with one row reuses the layer; a batch above the capacity
+    raises before any collective."""
+    from oracle import oracle as O
+    from tests.tolerance import assert_close
+    res = _run("uneven", world=4)
+    experts = _experts()
+    for r in range(4):
+        st, v = res[r]
+        assert st == "ok", v
+        out, out2, over = v
+        x, ids, w = _tokens(r, _batch("uneven", r))
+        assert out.shape == (x.shape[0], H)
+        assert_close(out, O.moe_forward(x, ids, w, experts, 10.0), what=f"EP uneven rank {r}")
+        x2, ids2, w2 = _tokens(r + 10, 1)
+        assert_close(out2, O.moe_forward(x2, ids2, w2, experts, 10.0), what=f"EP second call rank {r}")
+        assert "exceeds the capacity" in over
 
 
 def test_ep_rank_failure_is_reported_not_hung():

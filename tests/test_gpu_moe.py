@@ -344,3 +344,47 @@ def test_block_sparse_mlp_forward():
     ids, w, _ = O.route(logits, O.ROUTE_SIGMOID, topk, bias=bias, res=res, scale=2.5)
     ref = O.moe_forward(x.reshape(-1, H), ids, w, np_exp, 10.0, sh_np)
     assert_close(out.view(-1, H).cpu().numpy(), ref, what="BlockSparseMLP")
+
+
+def test_decode_step_graph_replay_matches_oracle():
+    """A two-layer decode step (router with residency bias -> moe_forward per layer) captured in one CUDA graph and
+    replayed twice with new inputs copied into its static buffers, as a serving loop does (the reference captures
+    per-block graphs, glm/xpu/glm_xpu/block_graphs.py:275-312): each replay equals the oracle."""
+    rng = np.random.default_rng(77)
+    E, H, I, topk, M, Lc, layers = 16, 256, 128, 4, 3, 10.0, 2
+    nets = [make_experts(rng, E, H, I, [(2, 3, 3)] * E, 3) for _ in range(layers)]
+    tables = [moe.ExpertTable(n[1], n[3]) for n in nets]
+    res = np.where(rng.random(E) < 0.25, 0.1, 0.0).astype(np.float32)
+    res_d = to_dev(res)
+    x = torch.zeros((layers, M, H), dtype=torch.half, device=DEV)
+    lg = torch.zeros((layers, M, E), dtype=torch.float32, device=DEV)
+    out = torch.zeros((layers, M, H), dtype=torch.float32, device=DEV)
+
+    def step():
+        for l in range(layers):
+            ids, w, _ = ops.route(lg[l], O.ROUTE_SIGMOID, topk, res=res_d, scale=2.5)
+            moe.moe_forward(x[l], ids, w, tables[l], Lc, out=out[l])
+
+    step()                                               # eager warm-up: attributes, workspaces
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for rep in range(2):
+        xn = rng.standard_normal((layers, M, H)).astype(np.float16)
+        ln = rng.standard_normal((layers, M, E)).astype(np.float32)
+        x.copy_(to_dev(xn))
+        lg.copy_(to_dev(ln))
+        out.fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        for l in range(layers):
+            rid, rw, _ = O.route(ln[l], O.ROUTE_SIGMOID, topk, res=res, scale=2.5)
+            ref = O.moe_forward(xn[l], rid, rw, nets[l][0], Lc, nets[l][2])
+            assert_close(out[l].cpu().numpy(), ref, what=f"graph replay {rep} layer {l}")
+    del graph
