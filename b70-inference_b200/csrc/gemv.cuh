@@ -23,11 +23,15 @@
 // a = fp16(H(fp16(x*suh))/sqrt(128)) (exllamav3's roundings), stored per (row, 16-input tile-row) as 4 quads x 4 fp16
 // {a[2q], a[2q+1], a[2q+8], a[2q+9]}: exactly the two registers of the m16n8k16 MMA B fragment of lane quad q.
 //
-// Decode (glm/docs/ext-op-inventory.md:559-574): the weight's 16-bit state times 0x83DCD12D, byte sum + 0x6400 by
-// dp4a = fp16 bits of 1024 + bytesum, then fma.rn.f16x2 with the fp16 constants 0x1EEE / 0xC931: the reference's fp16
-// weight, bit for bit, written straight into the MMA A fragment (the EXL3 position order is that fragment's layout:
-// lane 4g+q owns positions 8l..8l+7, so no shuffles). One m16n8k16 MMA per 16x16 tile accumulates in fp32; batch
-// rows ride in the MMA's 8 columns, so rows 1..8 cost the same decode.
+// Decode (glm/docs/ext-op-inventory.md:559-574), fold form (glm/xpu/csrc/exl3_esimd.h:82-91): the weight's 16-bit
+// state times 0x83DCD12D, byte sum + 0x6400 by dp4a = the fp16 bits of h = 1024 + bytesum (exact), packed two per
+// register straight into the MMA A fragment (the EXL3 position order is that fragment's layout: lane 4g+q owns
+// positions 8l..8l+7, so no shuffles). One m16n8k16 MMA per 16x16 tile accumulates D = sum_k h_k a_k in fp32; batch
+// rows ride in the MMA's 8 columns, so rows 1..8 cost the same decode. The codebook's affine w = h c1 + c2 (fp16
+// constants 0x1EEE / 0xC931) is applied once per output in the epilogue, D' = c1 D + c2 S with S = sum_k a_k from the
+// per-128-block activation sums the rotation kernels write: the product is the one of the unrounded affine
+// (|w' - w| <= half an fp16 ulp of the reference's fp16 weight), one fp16 FMA per weight pair less than applying it to
+// every weight. exl3_dequant keeps the rounded fp16 weights, bit for bit.
 //
 // Epilogues: the output Hadamard x svh (linear), the gated-MLP activation + the down projection's input rotation
 // (MoE gate|up), or Hadamard x svh x routing weight (MoE down).
@@ -55,7 +59,7 @@ constexpr int kStages = 10;         // ring stages per CTA (80 KB in flight; the
 constexpr int kConsumers = 4;       // consumer warps that cover one tile-row (all tiles of all matrices)
 constexpr int kSub = 5;             // consumer sub-groups; sub-group j takes ring stages j, j + kSub, ...
 constexpr int kConsumerWarps = kSub * kConsumers;
-constexpr int kEpilogueWarps = 4;   // reduce and finish units while the consumers decode the next segment
+constexpr int kEpilogueWarps = 2;   // reduce and finish units while the consumers decode the next segment
 constexpr int kGemvThreads = (1 + kConsumerWarps + kEpilogueWarps) * 32;   // producer, consumers, epilogue
 static_assert(kMaxRows % kEpilogueWarps == 0, "epilogue rows per warp");
 
@@ -102,7 +106,10 @@ struct GemvArgs {
     float act_limit;
     // activations in xf order: linear: [M][k]; gate|up: [rows][2][k] (row = pair_src of a position); down: [pos][k]
     const __half* xf;
+    // sums of the fp16 activations per 128-block, in the same row order: [row][nmat][k / 128] fp32 (the fold's S)
+    const float* xsum;
     __half* xf_out;         // gate|up only: the down input in xf order [positions][I]
+    float* xsum_out;        // gate|up only: its block sums [positions][I / 128]
     // shape of the matrices this launch runs (gate|up: k = H, n = I; down: k = I, n = H)
     int k, n;
     float* partial;         // [2 gridDim.x][unit_floats] split-unit partial sums
@@ -155,6 +162,24 @@ __device__ __forceinline__ void store_xf_block(const float v[4], int lane, __hal
     }
 }
 
+// Sum of one 128-block's values (lane l holds 4l..4l+3, already fp16-rounded) in a fixed association order; every
+// lane gets lane 0's total.
+__device__ __forceinline__ float xf_block_sum(const float v[4]) {
+    float t = (v[0] + v[1]) + (v[2] + v[3]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xFFFFFFFFu, t, o);
+    return __shfl_sync(0xFFFFFFFFu, t, 0);
+}
+
+// Sum of n per-block sums p[0..n) (lane-strided partial sums, then a fixed xor tree; lane 0's total to every lane).
+__device__ __forceinline__ float xsum_total(const float* p, int n, int lane) {
+    float t = 0.f;
+    for (int b = lane; b < n; b += 32) t += __ldcg(p + b);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xFFFFFFFFu, t, o);
+    return __shfl_sync(0xFFFFFFFFu, t, 0);
+}
+
 // The lane's 4 rotated activations of one 128-block, as the fp16 values the reference computes (returned widened).
 template <typename TIn>
 __device__ __forceinline__ void rotated_block(const TIn* x, const __half* suh, int lane, float v[4]) {
@@ -170,13 +195,16 @@ __device__ __forceinline__ void rotated_block(const TIn* x, const __half* suh, i
 
 // One consumer warp over one segment: its TPW tiles of one matrix on every tile-row of the stages its sub-group owns
 // (ring sequence numbers it with it % kSub == sub, visited directly), continuing the CTA's ring sequence at `it` and
-// leaving it at the segment's end. The ring couples the
-// sub-groups: one that falls behind holds the producer back, and the others then wait and leave it the issue slots.
+// leaving it at the segment's end. The ring couples the sub-groups: one that falls behind holds the producer back, and
+// the others then wait and leave it the issue slots. The B fragments of a stage's first kBatch tile-rows are loaded
+// before the stage's full barrier is waited on, and each further row's fragment kBatch rows ahead.
 // d[t] = D[16 n x 8 rows] of tile t: d[0], d[1] = (n = g, rows 2q, 2q+1), d[2], d[3] = (n = g + 8, rows 2q, 2q+1).
 template <int K, int TPW>
 __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, int row_stride, int mat_off, int tile0,
                                         int n_rows, int rps, int sub, uint64_t* full, uint64_t* empty,
                                         const __half* xf_row, bool has_row, int lane, int& it, bool& timed_out) {
+    constexpr int kBatch = TPW >= 4 ? 2 : 4;             // B fragments in flight (registers: the 4-tile warps hold
+                                                          // twice the accumulators)
     const LaneWords lw = lane_words<K>(lane);
     const int q = lane & 3;
     // B fragment of tile-row r for this lane: 8 bytes at xf_row + r * 16 + q * 4
@@ -187,21 +215,28 @@ __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, in
         const int r0 = j * rps;
         const int s = it % kStages;
         const int rows = min(rps, n_rows - r0);
-        uint2 bn = make_uint2(0, 0);
-        if (has_row) bn = __ldg(bp + (size_t)r0 * 4);
+        uint2 bq[kBatch];
+#pragma unroll
+        for (int b = 0; b < kBatch; ++b)
+            bq[b] = (has_row && b < rows) ? __ldg(bp + (size_t)(r0 + b) * 4) : make_uint2(0, 0);
         if (!timed_out && !mbar_wait(&full[s], (it / kStages) & 1)) timed_out = true;
         if (!timed_out) {
             const uint8_t* base = ring + (size_t)s * kStageBytes + mat_off + tile0 * 32 * K;
-            for (int rr = 0; rr < rows; ++rr, base += row_stride) {
-                const int r = r0 + rr;
-                const uint2 b = bn;
-                if (has_row && rr + 1 < rows) bn = __ldg(bp + (size_t)(r + 1) * 4);             // next row's
-                if (has_row && r + kSub * rps < n_rows) prefetch_l1(bp + (size_t)(r + kSub * rps) * 4);
+            for (int rb = 0; rb < rows; rb += kBatch) {
 #pragma unroll
-                for (int t = 0; t < TPW; ++t) {
-                    uint32_t a[4];
-                    decode_frag<K>(reinterpret_cast<const uint32_t*>(base + t * 32 * K), lw, a);
-                    mma_16816(d[t], a, b.x, b.y);
+                for (int b = 0; b < kBatch; ++b) {
+                    if (rb + b < rows) {
+                        const uint2 bv = bq[b];
+                        const int nx = rb + kBatch + b;            // the row this slot holds next
+                        if (has_row && nx < rows) bq[b] = __ldg(bp + (size_t)(r0 + nx) * 4);
+#pragma unroll
+                        for (int t = 0; t < TPW; ++t) {
+                            uint32_t a[4];
+                            decode_frag_raw<K>(reinterpret_cast<const uint32_t*>(base + t * 32 * K), lw, a);
+                            mma_16816(d[t], a, bv.x, bv.y);
+                        }
+                        base += row_stride;
+                    }
                 }
             }
         }
@@ -347,8 +382,14 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
         float v[NMAT][4];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
+            // the codebook affine on the product: c1 * sum h a + c2 * sum a (S: the row's activation sum)
+            const float c2s = kMul1C2 * xsum_total(a.xsum + ((size_t)ui.xrow[row] * NMAT + m) * (a.k / 128),
+                                                   a.k / 128, lane);
             const float4 t = *reinterpret_cast<const float4*>(red + ((size_t)m * kMaxRows + row) * 128 + 4 * lane);
-            v[m][0] = t.x; v[m][1] = t.y; v[m][2] = t.z; v[m][3] = t.w;
+            v[m][0] = fmaf(kMul1C1, t.x, c2s);
+            v[m][1] = fmaf(kMul1C1, t.y, c2s);
+            v[m][2] = fmaf(kMul1C1, t.z, c2s);
+            v[m][3] = fmaf(kMul1C1, t.w, c2s);
             fwht128_warp(v[m], lane);
         }
         if constexpr (EPI == EPI_LINEAR) {
@@ -392,9 +433,11 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
             }
             fwht128_warp(h, lane);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) h[j] = h[j] * kRsqrt128;
-            // the down projection's input block cb, straight into xf order
+            for (int j = 0; j < 4; ++j) h[j] = __half2float(__float2half_rn(h[j] * kRsqrt128));
+            // the down projection's input block cb, straight into xf order, and its block sum
             store_xf_block(h, lane, a.xf_out + (size_t)(ui.s0 + row) * a.n + (size_t)ui.cb * 128);
+            const float bs = xf_block_sum(h);
+            if (lane == 0) a.xsum_out[(size_t)(ui.s0 + row) * (a.n / 128) + ui.cb] = bs;
         } else {
             const float w = op.w[ri];
             float o[4];
@@ -640,6 +683,7 @@ struct PrepArgs {
     int rows, k;
     const __half* suh;
     __half* xf;                   // [rows][k] in xf order
+    float* xsum;                  // [rows][k / 128] block sums of the rotated rows
     int* zero;                    // tickets of the following GEMV
     int n_zero;
 };
@@ -662,6 +706,8 @@ static __global__ void __launch_bounds__(256) k_prep(const PrepArgs a) {
         else
             rotated_block<__half>(reinterpret_cast<const __half*>(a.x) + (size_t)row * a.ldx + kb * 128, su, lane, v);
         store_xf_block(v, lane, a.xf + (size_t)row * a.k + (size_t)kb * 128);
+        const float bs = xf_block_sum(v);
+        if (lane == 0) a.xsum[(size_t)row * KB + kb] = bs;
     }
 }
 

@@ -145,12 +145,14 @@ int exl3_pack_gateup(const void* gate, const void* up, int H, int I, int Kg, int
 
 // Workspace of exl3_gemv: rotated input rows [M][k] fp16 | tickets [n/128] int32 | split-unit partial slots.
 struct GemvWs {
-    size_t xf, tickets, partial, total;
+    size_t xf, xsum, tickets, partial, total;
 };
+// rotated rows [M][k] fp16 | their block sums [M][k / 128] fp32 | tickets [n / 128] | split-unit partial slots
 static GemvWs gemv_ws(int M, int k, int n) {
     GemvWs w;
     w.xf = 0;
-    w.tickets = align_up((size_t)M * k * 2, 256);
+    w.xsum = align_up((size_t)M * k * 2, 256);
+    w.tickets = align_up(w.xsum + (size_t)M * (k / 128) * 4, 256);
     w.partial = align_up(w.tickets + (size_t)(n / 128) * 4, 256);
     w.total = w.partial + partial_bytes(EPI_LINEAR);
     return w;
@@ -255,6 +257,7 @@ int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* packed, co
     pa.k = k;
     pa.suh = static_cast<const __half*>(suh);
     pa.xf = xf;
+    pa.xsum = reinterpret_cast<float*>(ws + W.xsum);
     pa.zero = tickets;
     pa.n_zero = n / 128;
     int rc = launch_prep(pa, st, "exl3_gemv");
@@ -269,6 +272,7 @@ int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* packed, co
     a.y_dtype = y_dtype;
     a.M = M;
     a.xf = xf;
+    a.xsum = reinterpret_cast<const float*>(ws + W.xsum);
     a.k = k;
     a.n = n;
     a.partial = reinterpret_cast<float*>(ws + W.partial);

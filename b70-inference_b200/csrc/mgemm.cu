@@ -8,7 +8,8 @@
 // sums each token's slots in slot order.
 //
 // Workspace: counters (8 ints) | descriptors [n_mats] | items [max_items] x 3 | row weights [P] | tickets
-// [max_items][n/128] | xf rows [P][k] fp16 | fp32 rows [P][n] | split-unit partial slots, P = slots * m.
+// [max_items][n/128] | xf rows [P][k] fp16 | their block sums [P][k/128] fp32 | fp32 rows [P][n] | split-unit
+// partial slots, P = slots * m.
 #include <type_traits>
 
 #include "gemv.cuh"
@@ -16,7 +17,7 @@
 namespace exl3 {
 
 struct MgLayout {
-    size_t desc, item_expert, item_start, item_cnt, pair_w, tickets, xf, ybuf, partial, total;
+    size_t desc, item_expert, item_start, item_cnt, pair_w, tickets, xf, xsum, ybuf, partial, total;
     int max_items, P, n_tickets;
 };
 
@@ -35,6 +36,7 @@ inline MgLayout mg_layout(int slots, int m, int k, int n, int n_mats) {
     L.tickets = o; o += (size_t)L.n_tickets * 4;
     o = align_up(o, 256);
     L.xf = o; o += align_up((size_t)L.P * k * 2, 256);
+    L.xsum = o; o += align_up((size_t)L.P * (k / 128) * 4, 256);
     L.ybuf = o; o += align_up((size_t)L.P * n * 4, 256);
     L.partial = o; o += partial_bytes(EPI_DOWN);
     L.total = o;
@@ -134,6 +136,8 @@ static __global__ void __launch_bounds__(kMgThreads) k_mg_prep(const MgPrep p) {
         else
             rotated_block<__half>(static_cast<const __half*>(p.A) + xrow, su, lane, v);
         store_xf_block(v, lane, xf + (size_t)pos * p.k + (size_t)kb * 128);
+        const float bs = xf_block_sum(v);
+        if (lane == 0) reinterpret_cast<float*>(p.ws + p.L.xsum)[(size_t)pos * KB + kb] = bs;
     }
 }
 
@@ -247,6 +251,7 @@ int exl3_mgemm(const void* A, int a_dtype, int a_batches, int lda, int m, int k,
     a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
     a.ybuf_round_f16 = !weights && c_dtype == EXL3_F16;   // the fp16 linear's rounding for unweighted fp16 C
     a.xf = reinterpret_cast<const __half*>(ws + L.xf);
+    a.xsum = reinterpret_cast<const float*>(ws + L.xsum);
     a.k = k;
     a.n = n;
     a.partial = reinterpret_cast<float*>(ws + L.partial);

@@ -7,8 +7,8 @@
 //   pair_tok[P] pair_expert[P] pair_of[pairs] pair_w[P] (fp32) pair_src[P]
 //   tickets[max_items * max(H, I) / 128] (GEMV split-unit counters)
 //   then, 256-byte aligned: gate|up input rows in xf order fp16 [P][2][H] (row = routed pair index, or pairs + m for
-//   the shared expert's row of token m), down input rows in xf order fp16 [P][I] (by position), ybuf fp32 [P][H],
-//   GEMV split-unit partial slots.
+//   the shared expert's row of token m), down input rows in xf order fp16 [P][I] (by position), the block sums of
+//   both (fp32 [P][2][H/128], [P][I/128]), ybuf fp32 [P][H], GEMV split-unit partial slots.
 #include "gemv.cuh"
 #include "tc.cuh"
 
@@ -19,7 +19,7 @@ inline int item_rows(int M) { return M < 8 ? (M > 0 ? M : 1) : 8; }
 
 struct WsLayout {
     size_t item_expert, item_start, item_cnt, pair_tok, pair_expert, pair_of, pair_w, pair_src, tickets, seg_cnt,
-        xf_gu, xf_dn, ybuf, partial, total;
+        xf_gu, xf_dn, xsum_gu, xsum_dn, ybuf, partial, total;
     int max_items, p_max, n_tickets;
 };
 
@@ -47,6 +47,8 @@ inline WsLayout ws_layout(int M, int topk, int E, int H, int I, int shared, int 
     o = align_up(o, 256);
     L.xf_gu = o; o += align_up((size_t)L.p_max * 2 * H * 2, 256);
     L.xf_dn = o; o += align_up((size_t)L.p_max * I * 2, 256);
+    L.xsum_gu = o; o += align_up((size_t)L.p_max * 2 * (H / 128) * 4, 256);
+    L.xsum_dn = o; o += align_up((size_t)L.p_max * (I / 128) * 4, 256);
     L.ybuf = o; o += align_up((size_t)L.p_max * H * 4, 256);
     L.partial = o; o += partial_bytes(EPI_GATEUP);
     L.total = o;
@@ -663,6 +665,7 @@ struct PrepareArgs {
     int* tickets;
     int n_tickets;
     __half* xf;                  // [P][2][H]
+    float* xsum;                 // [P][2][H / 128] block sums of the rotated rows
 };
 
 __global__ void __launch_bounds__(kAlignThreads) k_prepare(const PrepareArgs a) {
@@ -704,6 +707,8 @@ __global__ void __launch_bounds__(kAlignThreads) k_prepare(const PrepareArgs a) 
         else
             rotated_block<__half>(reinterpret_cast<const __half*>(a.x) + (size_t)tok * a.ldx + kb * 128, su, lane, v);
         store_xf_block(v, lane, a.xf + ((size_t)row * 2 + mat) * a.H + (size_t)kb * 128);
+        const float bs = xf_block_sum(v);
+        if (lane == 0) a.xsum[((size_t)row * 2 + mat) * KB + kb] = bs;
     }
 }
 
@@ -859,6 +864,7 @@ static int run_prepare(const void* x, int x_dtype, int ldx, int M, const int32_t
     a.tickets = reinterpret_cast<int*>(ws + L.tickets);
     a.n_tickets = L.n_tickets;
     a.xf = reinterpret_cast<__half*>(ws + L.xf_gu);
+    a.xsum = reinterpret_cast<float*>(ws + L.xsum_gu);
     const long jobs = (long)L.p_max * 2 * (H / 128);
     long ctas = (jobs + kAlignWarps - 1) / kAlignWarps;
     if (ctas > 2 * num_sms()) ctas = 2 * num_sms();
@@ -894,7 +900,9 @@ static int run_gateup(int M, int topk, const exl3_expert* experts, int E, int sh
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     GemvArgs a = moe_args(experts, act_limit, ws, L);
     a.xf = reinterpret_cast<const __half*>(ws + L.xf_gu);
+    a.xsum = reinterpret_cast<const float*>(ws + L.xsum_gu);
     a.xf_out = reinterpret_cast<__half*>(ws + L.xf_dn);
+    a.xsum_out = reinterpret_cast<float*>(ws + L.xsum_dn);
     a.k = H;
     a.n = I;
     const GemvPlan pl = plan_gemv(EPI_GATEUP, (long long)L.max_items * (I / 128) * (H / 128), n_ctas);
@@ -911,6 +919,7 @@ static int run_down(int M, int topk, const exl3_expert* experts, int E, int shar
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     GemvArgs a = moe_args(experts, 0.f, ws, L);
     a.xf = reinterpret_cast<const __half*>(ws + L.xf_dn);
+    a.xsum = reinterpret_cast<const float*>(ws + L.xsum_dn);
     a.k = I;
     a.n = H;
     const GemvPlan pl = plan_gemv(EPI_DOWN, (long long)L.max_items * (H / 128) * (I / 128), n_ctas);

@@ -3,8 +3,9 @@
 // runtime that forbids allocation on its hot path). The kernels are exl3_gemv's (k_prep + k_gemv<EPI_LINEAR>); only
 // where the scratch lives differs.
 //
-// Scratch (kNoAllocBytes, 256-byte aligned): rotated input rows [8][kNoAllocMaxK] fp16 | tickets
-// [kNoAllocMaxN / 128] int32 | split-unit partial slots [2 * kNoAllocMaxCtas][8][128] fp32.
+// Scratch (kNoAllocBytes = 1,845,248 bytes, 256-byte aligned): rotated input rows [8][kNoAllocMaxK] fp16 | their
+// block sums [8][kNoAllocMaxK / 128] fp32 | tickets [kNoAllocMaxN / 128] int32 | split-unit partial slots
+// [2 * kNoAllocMaxCtas][8][128] fp32.
 // * Limits: M <= 8, k <= kNoAllocMaxK, n <= kNoAllocMaxN; the launch uses at most kNoAllocMaxCtas CTAs. Larger
 //   shapes are rejected with EXL3_ERR_UNSUPPORTED.
 // * Zero state: the tickets must be zero when the GEMV starts; the prep kernel of the same call zeroes them (and the
@@ -21,10 +22,12 @@ constexpr int kNoAllocMaxK = 32768;
 constexpr int kNoAllocMaxN = 65536;
 constexpr int kNoAllocMaxCtas = 160;
 constexpr size_t kNoAllocXf = (size_t)kMaxRows * kNoAllocMaxK * 2;
+constexpr size_t kNoAllocXsum = (size_t)kMaxRows * (kNoAllocMaxK / 128) * 4;
 constexpr size_t kNoAllocTickets = (size_t)(kNoAllocMaxN / 128) * 4;
 constexpr size_t kNoAllocPartial = (size_t)2 * kNoAllocMaxCtas * unit_floats(EPI_LINEAR) * 4;
-constexpr size_t kNoAllocBytes = kNoAllocXf + kNoAllocTickets + kNoAllocPartial;
-static_assert(kNoAllocXf % 256 == 0 && kNoAllocTickets % 256 == 0, "region alignment");
+constexpr size_t kNoAllocBytes = kNoAllocXf + kNoAllocXsum + kNoAllocTickets + kNoAllocPartial;
+static_assert(kNoAllocXf % 256 == 0 && kNoAllocXsum % 256 == 0 && kNoAllocTickets % 256 == 0, "region alignment");
+static_assert(kNoAllocBytes == 1845248, "the documented scratch size");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
@@ -73,7 +76,8 @@ int exl3_gemv_noalloc(const void* x, int x_dtype, int ldx, int M, const void* pa
                  cudaGetErrorString(cudaGetLastError()));
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     __half* xf = reinterpret_cast<__half*>(ws);
-    int* tickets = reinterpret_cast<int*>(ws + kNoAllocXf);
+    float* xsum = reinterpret_cast<float*>(ws + kNoAllocXf);
+    int* tickets = reinterpret_cast<int*>(ws + kNoAllocXf + kNoAllocXsum);
 
     PrepArgs pa = {};
     pa.x = x;
@@ -83,6 +87,7 @@ int exl3_gemv_noalloc(const void* x, int x_dtype, int ldx, int M, const void* pa
     pa.k = k;
     pa.suh = static_cast<const __half*>(suh);
     pa.xf = xf;
+    pa.xsum = xsum;
     pa.zero = tickets;
     pa.n_zero = n / 128;
     int rc = launch_prep(pa, st, "exl3_gemv_noalloc");
@@ -97,9 +102,10 @@ int exl3_gemv_noalloc(const void* x, int x_dtype, int ldx, int M, const void* pa
     a.y_dtype = y_dtype;
     a.M = M;
     a.xf = xf;
+    a.xsum = xsum;
     a.k = k;
     a.n = n;
-    a.partial = reinterpret_cast<float*>(ws + kNoAllocXf + kNoAllocTickets);
+    a.partial = reinterpret_cast<float*>(ws + kNoAllocXf + kNoAllocXsum + kNoAllocTickets);
     a.counters = tickets;
     a.status = device_status_ptr();
     GemvPlan pl = plan_gemv(EPI_LINEAR, (long long)(n / 128) * (k / 128), 0);

@@ -90,6 +90,20 @@ __device__ __forceinline__ __half mul1_one(uint32_t s) {
     return __ushort_as_half(static_cast<unsigned short>(r & 0xFFFFu));
 }
 
+// The codebook without its affine ("fold" form, the reference's decode_mul1_raw, glm/xpu/csrc/exl3_esimd.h:82-91):
+// h = fp16 bits of 1024 + bytesum(state * 0x83DCD12D), exact in fp16, for two states packed as half2. The affine
+// w = fp16(h * c1 + c2) is then applied to the dot product instead of to every weight:
+//   sum_k a_k * (h_k * c1 + c2) = c1 * sum_k a_k h_k + c2 * sum_k a_k,
+// i.e. the product uses the unrounded w' = h c1 + c2 (|w' - w| <= half an fp16 ulp of w) and needs the sum of the
+// activations, which the kernels that rotate the activations provide per 128-block. Saves the fp16 FMA per pair.
+constexpr float kMul1C1 = 0.00676727294921875f;     // fp16 0x1EEE
+constexpr float kMul1C2 = -10.3828125f;             // fp16 0xC931
+__device__ __forceinline__ uint32_t mul1_raw_pair(uint32_t sa, uint32_t sb) {
+    const uint32_t ha = __dp4a(sa * kMul1, 0x01010101u, 0x6400u);
+    const uint32_t hb = __dp4a(sb * kMul1, 0x01010101u, 0x6400u);
+    return ha + (hb << 16);
+}
+
 // Decode the lane's A fragment (4 x half2) of one tile from its three words (tile words lw.i0, lw.i1, lw.i2).
 // Register order follows the m16n8k16 A layout: {pos0,pos1} {pos4,pos5} {pos2,pos3} {pos6,pos7}.
 template <int K>
@@ -100,6 +114,17 @@ __device__ __forceinline__ void decode_frag_words(uint32_t w0, uint32_t w1, uint
     a[1] = mul1_pair(st[4], st[5]);
     a[2] = mul1_pair(st[2], st[3]);
     a[3] = mul1_pair(st[6], st[7]);
+}
+
+// The same fragment in the fold form: h values (1024 + bytesum) instead of weights.
+template <int K>
+__device__ __forceinline__ void decode_frag_raw(const uint32_t* tile, const LaneWords& lw, uint32_t a[4]) {
+    uint32_t st[8];
+    lane_states<K>(tile[lw.i0], tile[lw.i1], tile[lw.i2], lw.off, st);
+    a[0] = mul1_raw_pair(st[0], st[1]);
+    a[1] = mul1_raw_pair(st[4], st[5]);
+    a[2] = mul1_raw_pair(st[2], st[3]);
+    a[3] = mul1_raw_pair(st[6], st[7]);
 }
 
 // Decode the lane's A fragment of one tile whose words start at `tile` (shared or global memory).

@@ -101,8 +101,9 @@ EXL3_API int exl3_pack_gateup(const void* gate, const void* up, int H, int I, in
  * packed = the weights in the packed layout (exl3_pack). k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2.
  * workspace >= exl3_gemv_workspace_size(M, k, n) bytes (rotated input rows, split-unit reduction state; calls that
  * share a workspace must be ordered on one stream). n_ctas = CTAs of the persistent launch (0 = one per SM).
- * Weights are decoded to the reference's fp16 values bit for bit and multiplied with fp32 accumulation; results
- * differ from the reference only by summation order, and are identical from call to call for one n_ctas.
+ * Weights are decoded bit for bit up to the codebook's final fp16 affine, which is applied to the fp32-accumulated
+ * dot product instead (the reference's fold form, glm/xpu/csrc/exl3_esimd.h:82-91: the product uses the unrounded
+ * affine, within half an fp16 ulp of each weight); results are identical from call to call for one n_ctas.
  * Replaces exl3_gemm_small (glm/xpu/csrc/exl3_ops.sycl:258-321) / exllamav3 exl3_gemm
  * (glm/docs/ext-op-inventory.md:498-557) as called by BC_LinearEXL3.run (glm/xpu/glm_xpu/ops.py:60-80). */
 EXL3_API size_t exl3_gemv_workspace_size(int M, int k, int n);
@@ -124,8 +125,8 @@ EXL3_API int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void
                           void* workspace, size_t ws_bytes, void* stream);
 
 /* No-allocation variant of exl3_gemv: same arguments minus the workspace and n_ctas; its scratch is a fixed
- * file-scope device array (1,837,056 bytes per device that loads the library: the rotated input rows, the split
- * tickets and the partial slots, sized from the limits below), for callers that cannot allocate device memory.
+ * file-scope device array (1,845,248 bytes per device that loads the library: the rotated input rows and their
+ * block sums, the split tickets and the partial slots, sized from the limits below), for callers that cannot allocate device memory.
  * Limits: M <= 8, k <= 32768, n <= 65536 (larger shapes return EXL3_ERR_UNSUPPORTED). Calls on one device that may
  * overlap race on the shared scratch: order them on one stream. Make the first call on each device outside stream
  * capture (it looks up the scratch's address). No reference counterpart. */
