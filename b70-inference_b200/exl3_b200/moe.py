@@ -16,6 +16,9 @@ from . import _lib as L
 from .ops import pack, pack_gateup, route, route_hidden
 
 ROUTE_SIGMOID, ROUTE_SOFTMAX, ROUTE_SQRT_SOFTPLUS = L.ROUTE_SIGMOID, L.ROUTE_SOFTMAX, L.ROUTE_SQRT_SOFTPLUS
+# Rows from which a MoE layer runs on the tcgen05 grouped GEMMs instead of the decode GEMVs (the decode kernels read a
+# picked expert once per 8 rows; a 320-row tensor-core tile pays off once experts see tens of rows each)
+PREFILL_MIN_ROWS = 256
 
 
 @dataclass
@@ -236,7 +239,8 @@ def moe_align(topk_ids: torch.Tensor, topk_w: torch.Tensor, E: int, shared: bool
 
 class BlockSparseMLP:
     """Routed-expert MLP block with the reference's module API (glm/xpu/glm_xpu/moe_patch.py:66-94):
-    forward(x, params, out_dtype) = router (with residency bias) -> routed sum on the MoE kernels + shared expert.
+    forward(x, params, out_dtype) = router (with residency bias) -> routed sum on the MoE kernels (the decode GEMVs,
+    or the tcgen05 grouped GEMMs from PREFILL_MIN_ROWS rows) + shared expert.
 
     router_kind: ROUTE_SIGMOID (GLM / DeepSeek-V3 noaux_tc), ROUTE_SOFTMAX (Qwen-Next), ROUTE_SQRT_SOFTPLUS
     (DeepSeek-V4). gate: router weight fp16 [H, E] (exllamav3 stores it in x out). bias: e_score_correction_bias
@@ -279,7 +283,8 @@ class BlockSparseMLP:
                                      renorm=self.renormalize)
         else:
             ids, w = self.route_logits(logits)
-        out = moe_forward(y, ids, w, self.table, self.act_limit, torch.float32)
+        fn = moe_prefill if y.shape[0] >= PREFILL_MIN_ROWS else moe_forward
+        out = fn(y, ids, w, self.table, self.act_limit, torch.float32)
         out = out.view(x.shape[:-1] + (self.hidden_size,))
         if out_dtype is not None:
             out = out.to(out_dtype)

@@ -4,6 +4,7 @@ Run in a container where the reference tree is mounted (default /root/reference,
 
     python tests/golden/make_golden.py            # every fixture
     python tests/golden/make_golden.py softmax    # only route_softmax.npz
+    python tests/golden/make_golden.py stores     # only the expert blob / piece store / checkpoint fixtures
 
 What runs (all from horvay/b70-inference, unmodified, imported or exec'd from its files):
   * glm/xpu/tests/units.py:42-89  -- mul1_lut, w_hat, H128, ref_linear (the reference's own torch restatement of
@@ -12,7 +13,11 @@ What runs (all from horvay/b70-inference, unmodified, imported or exec'd from it
   * dsv41/xpu/dsv_xpu/moe.py      -- route() (sqrt-softplus router with the residency bias), its torch path;
   * trellis-serve.patch            -- fused_xpu.py's Triton `_router_kernel` / `router` (the Qwen-Next softmax router
     with the cold-tier bias and the RAM margin), cut out of the patch text and run on CPU under Triton's interpreter
-    (TRITON_INTERPRET=1).
+    (TRITON_INTERPRET=1);
+  * glm/xpu/exl3xpu/moe_offload.py -- pack_expert / planar4 (the GLM / Qwen-Next expert blob), cross-checked against
+    the record permutation blob_perm of glm/xpu/pack_store.py;
+  * dsv41/xpu/dsv_xpu/pack_store.py -- main(): the DeepSeek-V4 piece store written from a small EXL3 safetensors
+    checkpoint (its module constants H, I set to the fixture's sizes).
 The outputs are small .npz files with seeded inputs and the reference's outputs; tests compare the oracle and the
 CUDA path against them. Nothing here runs at test time.
 """
@@ -102,10 +107,77 @@ def make_softmax():
     np.savez_compressed(os.path.join(HERE, "route_softmax.npz"), **cases)
 
 
+def make_stores():
+    """expert_blob.npz: experts (H 256, I 128; K 3, 4, 5) and their blobs by the reference's pack_expert, which must
+    agree with its record permutation blob_perm. dsv_store/: an EXL3 checkpoint of two MoE layers x 4 experts (K 1-3
+    per projection, DeepSeek-V4 key names) and the piece store the reference's pack_store.main writes from it."""
+    import importlib
+    import shutil
+    import tempfile
+    from safetensors.torch import save_file
+    sys.path.insert(0, os.path.join(REF, "glm/xpu"))
+    mo = importlib.import_module("exl3xpu.moe_offload")
+    ps = importlib.import_module("pack_store")
+    rng = np.random.default_rng(20261203)
+    H, I = 256, 128
+    blobs = {}
+    for K in (3, 4, 5):
+        mats = {}
+        for nm, (k, n) in (("gate", (H, I)), ("up", (H, I)), ("down", (I, H))):
+            mats[nm] = {"trellis": torch.from_numpy(rng.integers(-32768, 32768, (k // 16, n // 16, 16 * K),
+                                                                 dtype=np.int16)),
+                        "suh": torch.from_numpy(np.where(rng.random(k) < 0.5, 1.0, -1.0).astype(np.float16)),
+                        "svh": torch.from_numpy((rng.standard_normal(n) * 0.1).astype(np.float16))}
+        blob = mo.pack_expert(mats["gate"], mats["up"], mats["down"], K).numpy()
+        # the same bytes through blob_perm: the raw record is gate | up | down trellis words, then g_suh g_svh u_suh
+        # u_svh d_suh d_svh as fp16 pairs
+        raw = np.concatenate([mats[m]["trellis"].numpy().view(np.uint32).reshape(-1) for m in ("gate", "up", "down")]
+                             + [np.ascontiguousarray(mats[m][v].numpy()).view(np.uint32)
+                                for m, v in (("gate", "suh"), ("gate", "svh"), ("up", "suh"), ("up", "svh"),
+                                             ("down", "suh"), ("down", "svh"))])
+        perm = ps.blob_perm(H, I, K)
+        assert np.array_equal(raw[perm].view(np.uint8), blob), f"pack_expert and blob_perm disagree at K={K}"
+        blobs[f"K{K}_blob"] = blob
+        for m in mats:
+            for v in mats[m]:
+                blobs[f"K{K}_{m}_{v}"] = mats[m][v].numpy()
+    np.savez_compressed(os.path.join(HERE, "expert_blob.npz"), H=H, I=I, **blobs)
+
+    # DeepSeek-V4 piece store from a small checkpoint
+    sys.path.insert(0, os.path.join(REF, "dsv41/xpu"))
+    dps = importlib.import_module("dsv_xpu.pack_store")
+    dps.H, dps.I = H, I
+    dps.UNIT = H * I // 8
+    dps.VEC = 2 * H + 2 * I + I + H
+    out = os.path.join(HERE, "dsv_store")
+    shutil.rmtree(out, ignore_errors=True)
+    with tempfile.TemporaryDirectory() as ck:
+        tens = {}
+        for L in range(2):
+            for e in range(4):
+                for p, (k, n) in (("w1", (H, I)), ("w3", (H, I)), ("w2", (I, H))):
+                    K = int(rng.integers(1, 4))
+                    key = f"layers.{L}.ffn.experts.{e}.{p}"
+                    tens[f"{key}.trellis"] = torch.from_numpy(
+                        rng.integers(-32768, 32768, (k // 16, n // 16, 16 * K), dtype=np.int16))
+                    tens[f"{key}.suh"] = torch.from_numpy(np.where(rng.random(k) < 0.5, 1.0, -1.0).astype(np.float16))
+                    tens[f"{key}.svh"] = torch.from_numpy((rng.standard_normal(n) * 0.1).astype(np.float16))
+        save_file(tens, os.path.join(ck, "model-00001-of-00001.safetensors"))
+        with open(os.path.join(ck, "model.safetensors.index.json"), "w") as f:
+            json.dump({"weight_map": {k: "model-00001-of-00001.safetensors" for k in tens}}, f)
+        dps.main(ck, out, n_layers=2, n_experts=4)
+        os.makedirs(out, exist_ok=True)
+        shutil.copy(os.path.join(ck, "model-00001-of-00001.safetensors"), os.path.join(out, "checkpoint.safetensors"))
+
+
 def main():
     if sys.argv[1:] == ["softmax"]:
         make_softmax()
         print("route_softmax.npz written to", HERE)
+        return
+    if sys.argv[1:] == ["stores"]:
+        make_stores()
+        print("expert_blob.npz and dsv_store/ written to", HERE)
         return
     sys.path.insert(0, os.path.join(REF, "glm/xpu"))
     sys.path.insert(0, os.path.join(REF, "dsv41/xpu"))
@@ -223,6 +295,7 @@ def main():
                         H=H, I=I, act_limit=L, **ex)
 
     make_softmax()
+    make_stores()
 
     with open(os.path.join(HERE, "known_answers.json"), "w") as f:
         json.dump(meta, f, indent=1, sort_keys=True)
