@@ -209,12 +209,40 @@ __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, in
     const int q = lane & 3;
     // B fragment of tile-row r for this lane: 8 bytes at xf_row + r * 16 + q * 4
     const uint2* bp = reinterpret_cast<const uint2*>(xf_row + q * 4);
+    // a stage of a segment whose matrices share K holds RPS whole tile-rows of a compile-time stride: that case
+    // runs fully unrolled with every row's B fragment loaded before the stage's barrier
+    constexpr int RS = (TPW / 2) * kTilesPerMat * 32 * K;
+    constexpr int RPS = kStageBytes / RS;
+    constexpr int UNR = RPS <= (TPW >= 4 ? 5 : 10) ? RPS : 0;
     const int nst = (n_rows + rps - 1) / rps, it_begin = it;
     for (int j = (sub - it % kSub + kSub) % kSub; j < nst; j += kSub) {
         it = it_begin + j;
         const int r0 = j * rps;
         const int s = it % kStages;
         const int rows = min(rps, n_rows - r0);
+        if constexpr (UNR > 0) {
+            if (row_stride == RS && rows == RPS) {
+                uint2 bf[UNR > 0 ? UNR : 1];
+#pragma unroll
+                for (int r = 0; r < UNR; ++r) bf[r] = has_row ? __ldg(bp + (size_t)(r0 + r) * 4) : make_uint2(0, 0);
+                if (!timed_out && !mbar_wait(&full[s], (it / kStages) & 1)) timed_out = true;
+                if (!timed_out) {
+                    const uint8_t* base = ring + (size_t)s * kStageBytes + mat_off + tile0 * 32 * K;
+#pragma unroll
+                    for (int r = 0; r < UNR; ++r) {
+#pragma unroll
+                        for (int t = 0; t < TPW; ++t) {
+                            uint32_t a[4];
+                            decode_frag_raw<K>(reinterpret_cast<const uint32_t*>(base + r * RS + t * 32 * K), lw, a);
+                            mma_16816(d[t], a, bf[r].x, bf[r].y);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+                continue;
+            }
+        }
         uint2 bq[kBatch];
 #pragma unroll
         for (int b = 0; b < kBatch; ++b)
