@@ -60,6 +60,16 @@ _PROTOS = [
     ("exl3_moe_gateup", i32, [i32, i32, vp, i32, i32, i32, i32, f32, vp, sz, i32, vp]),
     ("exl3_moe_down", i32, [i32, i32, vp, i32, i32, i32, i32, vp, sz, i32, vp]),
     ("exl3_moe_combine", i32, [i32, i32, i32, i32, i32, i32, vp, i32, vp, sz, vp]),
+    ("exl3_ep_buffer_bytes", sz, [i32, i32, i32, i32]),
+    ("exl3_ep_recv_offsets", i32, [i32, i32, i32, i32, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t),
+                                   C.POINTER(C.c_size_t)]),
+    ("exl3_ep_buffer_create", i32, [sz, C.POINTER(vp), vp]),
+    ("exl3_ep_buffer_open", i32, [vp, C.POINTER(vp)]),
+    ("exl3_ep_buffer_close", i32, [vp]),
+    ("exl3_ep_buffer_free", i32, [vp]),
+    ("exl3_ep_dispatch", i32, [vp, i32, i32, i32, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp]),
+    ("exl3_ep_combine", i32, [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp]),
+    ("exl3_ep_reduce", i32, [vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp]),
 ]
 
 _lib = None

@@ -1,27 +1,31 @@
 """Expert parallelism over the GPUs of one box: rank r holds experts [r*E/W, (r+1)*E/W) of every MoE layer in its HBM
 (the reference's VRAM/RAM/NVMe tiers, glm/xpu/glm_xpu/tier.py:1-20, collapse to this residency), tokens stay
-data-parallel, and two NCCL all-to-alls over NVLink move the routed tokens:
+data-parallel, and each layer exchanges the routed rows in three steps:
 
-  dispatch: every rank sends each peer one chunk of `capacity` rows: its token rows (fp16/bf16) with their routed
-            expert ids (already rebased to that peer's expert range, -1 for picks of other ranks' experts) and
-            weights; rows past the rank's batch are padding with no picks. Every token row goes to every peer (the
-            chunk size is fixed so that the step needs no host synchronisation and can be graph-captured): the
-            exchange moves W * capacity rows per rank whatever the routing, and a row without a pick on a peer
-            costs that peer nothing but its bytes;
+  dispatch: every rank hands each peer its rows (fp16/bf16) with their routed expert ids rebased to that peer's
+            expert range (-1 for picks of other ranks' experts) and weights; rows past the rank's batch are padding
+            with no picks;
   local:    each rank runs the grouped MoE kernels on the W * capacity received rows (picks of other ranks' experts
             are -1 and skipped), producing one fp32 partial row per received row (decode kernels for small batches,
             the tcgen05 prefill path from PREFILL_MIN_PAIRS picks on);
-  combine:  the partial rows go back to their source rank, which sums the W partials in rank order (fixed order:
+  combine:  the partial rows go back to their source rank, which sums them in rank order (fixed order:
             bit-reproducible for a given world size) and adds the shared expert of its own rows (every rank holds
             the shared expert; it runs once per token, on the token's rank).
 
-Every rank must call forward with a batch of at most `capacity` rows (the capacity is fixed at construction, or by
-the first call); batches may differ between ranks. NCCL's all-to-all is the only data-path collective. The local
-step is pluggable so that the exchange logic is tested on CPU gloo ranks with the oracle standing in for the GPU
-kernels.
+Two exchanges implement dispatch / combine:
+  "p2p" (GPUs, the default there): this package's kernels write straight into the peers' exchange buffers over
+        NVLink (exl3_ep_dispatch / exl3_ep_combine / exl3_ep_reduce; buffers shared once through CUDA IPC handles):
+        a row's activations go only to the ranks it picked, a partial row comes back only from the ranks it picked,
+        no host synchronisation, no collective launch, graph-capturable (the calls count themselves on the device);
+  "nccl": two NCCL (or gloo) all_to_all_single calls per layer on fixed-size chunks (every row to every rank), and
+        the summation on the host side's tensors; the path the CPU gloo tests exercise with the oracle as the local
+        step.
+Every rank must call forward with a batch of at most `capacity` rows (fixed at construction, or by the first call);
+batches may differ between ranks; every rank makes the same calls in the same order.
 """
 from __future__ import annotations
 
+import ctypes as C
 from typing import Callable
 
 import torch
@@ -45,6 +49,84 @@ def localize_ids(ids: torch.Tensor, e0: int, e1: int) -> torch.Tensor:
 PREFILL_MIN_PAIRS = 4096          # received picks from which the local step uses the tcgen05 prefill kernels
 
 
+class PeerExchange:
+    """One exchange buffer per rank for (W, capacity, H, topk), mapped on every peer through CUDA IPC handles
+    (exchanged with all_gather_object on the group). Shared by every layer of that shape: layers run one after
+    another, and the buffer's device-side call counters keep the ranks in step."""
+
+    _cache: dict = {}
+
+    @classmethod
+    def get(cls, group, W: int, rank: int, cap: int, H: int, k: int, device):
+        key = (id(group), W, cap, H, k, str(device))
+        ex = cls._cache.get(key)
+        if ex is None:
+            ex = cls._cache[key] = cls(group, W, rank, cap, H, k, device)
+        return ex
+
+    def __init__(self, group, W, rank, cap, H, k, device):
+        from . import _lib as L
+        self.L = L
+        lib = L.lib()
+        self.W, self.rank, self.cap, self.H, self.k, self.device = W, rank, cap, H, k, device
+        nbytes = lib.exl3_ep_buffer_bytes(W, cap, H, k)
+        if nbytes == 0:
+            raise L.Exl3Error("PeerExchange: unsupported shape")
+        with torch.cuda.device(device):
+            ptr = C.c_void_p()
+            handle = (C.c_ubyte * 64)()
+            L.check(lib.exl3_ep_buffer_create(nbytes, C.byref(ptr), handle), "exl3_ep_buffer_create")
+            self.ptr = ptr.value
+            handles = [None] * W
+            dist.all_gather_object(handles, bytes(handle), group=group)
+            addrs, self.opened = [], []
+            for r, h in enumerate(handles):
+                if r == rank:
+                    addrs.append(self.ptr)
+                    continue
+                pp = C.c_void_p()
+                hb = (C.c_ubyte * 64).from_buffer_copy(h)
+                L.check(lib.exl3_ep_buffer_open(hb, C.byref(pp)), "exl3_ep_buffer_open")
+                addrs.append(pp.value)
+                self.opened.append(pp.value)
+        self.peers = torch.tensor([a if a < (1 << 63) else a - (1 << 64) for a in addrs], dtype=torch.int64,
+                                  device=device)
+        ox, oi, ow = C.c_size_t(), C.c_size_t(), C.c_size_t()
+        L.check(lib.exl3_ep_recv_offsets(W, cap, H, k, C.byref(ox), C.byref(oi), C.byref(ow)), "exl3_ep_recv_offsets")
+        self.off = (ox.value, oi.value, ow.value)
+        dist.barrier(group=group)
+
+    def recv_views(self, x_dtype):
+        """The receive region as tensors: x [W*cap, H], ids int32 [W*cap, k], w fp32 [W*cap, k] (views of the
+        library's buffer, valid while this object lives)."""
+        W, cap, H, k = self.W, self.cap, self.H, self.k
+
+        def view(off, numel, dt):
+            n = numel * torch.tensor([], dtype=dt).element_size()
+            return _device_view(self.ptr + off, n, self.device).view(dt)
+
+        return (view(self.off[0], W * cap * H, x_dtype).view(W * cap, H),
+                view(self.off[1], W * cap * k, torch.int32).view(W * cap, k),
+                view(self.off[2], W * cap * k, torch.float32).view(W * cap, k))
+
+    def close(self):
+        lib = self.L.lib()
+        for p in self.opened:
+            lib.exl3_ep_buffer_close(p)
+        self.opened = []
+        if self.ptr:
+            lib.exl3_ep_buffer_free(self.ptr)
+            self.ptr = 0
+
+
+def _device_view(addr: int, nbytes: int, device) -> torch.Tensor:
+    """A uint8 tensor over device memory the library owns (no copy; the owner keeps it alive)."""
+    class _Arr:
+        __cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (addr, False), "version": 3,
+                                    "strides": None}
+    return torch.as_tensor(_Arr(), device=device)
+
+
 class ExpertParallelMoE:
     """One MoE layer's routed experts sharded over a process group.
 
@@ -54,9 +136,11 @@ class ExpertParallelMoE:
     shared expert, if any)."""
 
     def __init__(self, E: int, H: int, topk: int, group=None, table=None, act_limit: float = 0.0,
-                 local_fn: Callable | None = None, shared_fn: Callable | None = None, capacity: int | None = None):
+                 local_fn: Callable | None = None, shared_fn: Callable | None = None, capacity: int | None = None,
+                 exchange: str | None = None):
         self.group = group
         self.capacity = capacity
+        self.exchange = exchange
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.E, self.H, self.topk = E, H, topk
@@ -95,6 +179,9 @@ class ExpertParallelMoE:
         cap = self.capacity
         if B > cap:
             raise ValueError(f"expert parallelism: batch of {B} rows exceeds the capacity {cap} of this layer")
+        exchange = self.exchange or ("p2p" if x.is_cuda else "nccl")
+        if exchange == "p2p":
+            return self._forward_p2p(x, ids, w)
         k = ids.shape[1]
         ids = ids.to(torch.int32)
         if B < cap:                                     # padding rows: no picks anywhere
@@ -127,4 +214,30 @@ class ExpertParallelMoE:
             out += back[r, :B]
         if self.shared_fn is not None:
             out += self.shared_fn(x[:B])
+        return out
+
+    def _forward_p2p(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """dispatch / local experts / combine / reduce on this package's peer-memory kernels."""
+        from . import _lib as L
+        B, H = x.shape
+        W, cap, k = self.world, self.capacity, ids.shape[1]
+        ex = PeerExchange.get(self.group, W, self.rank, cap, H, k, x.device)
+        lib = L.lib()
+        st = L.stream_of(x)
+        xc = x if x.dtype in (torch.float16, torch.bfloat16) else x.half()
+        xc = xc.contiguous()
+        idc = ids.to(torch.int32).contiguous()
+        wc = w.to(torch.float32).contiguous()
+        L.check(lib.exl3_ep_dispatch(xc.data_ptr(), L.dtype_code(xc.dtype), xc.stride(0), B, idc.data_ptr(),
+                                     wc.data_ptr(), k, self.E, H, W, self.rank, cap, ex.peers.data_ptr(), ex.ptr, st),
+                "exl3_ep_dispatch")
+        xr, rid, rw = ex.recv_views(xc.dtype)
+        part = self.local_fn(xr, rid, rw)
+        part = part.contiguous()
+        L.check(lib.exl3_ep_combine(part.data_ptr(), k, self.E, H, W, self.rank, cap, ex.peers.data_ptr(), ex.ptr,
+                                    st), "exl3_ep_combine")
+        shared = self.shared_fn(xc) if self.shared_fn is not None else None
+        out = torch.empty((B, H), dtype=torch.float32, device=x.device)
+        L.check(lib.exl3_ep_reduce(idc.data_ptr(), B, k, self.E, H, W, self.rank, cap, L.ptr(shared), ex.ptr,
+                                   out.data_ptr(), st), "exl3_ep_reduce")
         return out

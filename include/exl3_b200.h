@@ -239,6 +239,38 @@ EXL3_API int exl3_moe_prefill(const void* x, int x_dtype, int ldx, int M, const 
 EXL3_API int exl3_moe_align(const int32_t* ids, const float* w, int M, int topk, int E, int shared, int chunk,
                    void* workspace, size_t ws_bytes, void* stream);
 
+/* ---- expert-parallel exchange over peer memory ----
+ * The dispatch and combine of an expert-parallel MoE layer (rank r holds experts [r E/W, (r+1) E/W)) as kernels that
+ * write straight into the peers' memory over NVLink, in place of two all-to-all collectives per layer (the reference
+ * runs on one GPU and has no exchange; it has no counterpart there). Every rank owns one
+ * exchange buffer of exl3_ep_buffer_bytes(W, cap, H, topk) bytes, allocated by exl3_ep_buffer_create (cudaMalloc,
+ * zeroed, exported as a 64-byte CUDA IPC handle that the caller passes to its peers, e.g. through torch.distributed)
+ * and mapped on every peer with exl3_ep_buffer_open. peers = device array of W uint64 buffer addresses (this rank's
+ * own at [rank]). Per call, on one stream, in the same order on every rank:
+ *   exl3_ep_dispatch  rank r's rows x [B][H] (B <= cap), global ids int32 [B][topk] and weights [B][topk] into every
+ *                     peer's receive region (picks rebased to that peer's experts, -1 for others; activations only
+ *                     for rows with a pick there), then it waits for every peer's rows (bounded: 100 ms, then
+ *                     EXL3_ERR_TIMEOUT in the device status word);
+ *   (the caller runs its local experts on the W * cap received rows: recv_x / recv_ids / recv_w at the offsets
+ *    exl3_ep_recv_offsets gives, producing part fp32 [W][cap][H])
+ *   exl3_ep_combine   every received row that had a pick here goes back to its rank; waits for every peer's rows;
+ *   exl3_ep_reduce    out[i] = sum over the ranks row i picked, in rank order, of their partial rows (+ shared[i]).
+ * The calls count themselves on the device, so a captured sequence replays. exl3_ep_buffer_create allocates device
+ * memory; no other entry point here does. */
+EXL3_API size_t exl3_ep_buffer_bytes(int W, int cap, int H, int topk);
+EXL3_API int exl3_ep_recv_offsets(int W, int cap, int H, int topk, size_t* recv_x, size_t* recv_ids, size_t* recv_w);
+EXL3_API int exl3_ep_buffer_create(size_t bytes, void** ptr, void* ipc_handle);
+EXL3_API int exl3_ep_buffer_open(const void* ipc_handle, void** peer_ptr);
+EXL3_API int exl3_ep_buffer_close(void* peer_ptr);
+EXL3_API int exl3_ep_buffer_free(void* ptr);
+EXL3_API int exl3_ep_dispatch(const void* x, int x_dtype, int ldx, int B, const int32_t* ids, const float* w,
+                              int topk, int E, int H, int W, int rank, int cap, const uint64_t* peers, void* local,
+                              void* stream);
+EXL3_API int exl3_ep_combine(const float* part, int topk, int E, int H, int W, int rank, int cap,
+                             const uint64_t* peers, void* local, void* stream);
+EXL3_API int exl3_ep_reduce(const int32_t* ids, int B, int topk, int E, int H, int W, int rank, int cap,
+                            const float* shared, void* local, float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
