@@ -99,6 +99,8 @@ __device__ __forceinline__ bool row_picks_rank(const int32_t* ids, int i, int k,
 
 // grid (chunks, W): CTA (c, p) sends rows [c * rpc, ...) of this rank to peer p.
 __global__ void __launch_bounds__(kEpThreads) k_ep_dispatch(const EpArgs a) {
+    pdl_wait();                                                 // ids and rows come from earlier kernels
+    pdl_trigger();
     EpCtl* ctl = reinterpret_cast<EpCtl*>(a.local);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&ctl->dispatch_epoch) + 1;
     const int p = blockIdx.y, per = a.E / a.W;
@@ -144,6 +146,8 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_dispatch(const EpArgs a) {
 
 // grid (chunks, W): CTA (c, r) returns the rows [c * rpc, ...) received from rank r that had a pick here.
 __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpArgs a) {
+    pdl_wait();
+    pdl_trigger();
     EpCtl* ctl = reinterpret_cast<EpCtl*>(a.local);
     const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&ctl->combine_epoch) + 1;
     const int r = blockIdx.y;
@@ -180,6 +184,8 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpArgs a) {
 
 // out[i][:] = sum over ranks p (in order) that row i picked of back[p][i][:] (+ shared[i][:]); one float4 per thread.
 __global__ void __launch_bounds__(kEpThreads) k_ep_reduce(const EpArgs a, const float* shared, float* out) {
+    pdl_wait();
+    pdl_trigger();
     const int vec = a.H / 4, per = a.E / a.W;
     const long total = (long)a.B * vec;
     const float4* back = reinterpret_cast<const float4*>(a.local + a.L.back);
@@ -298,8 +304,9 @@ int exl3_ep_dispatch(const void* x, int x_dtype, int ldx, int B, const int32_t* 
     a.ldx = ldx;
     a.ids = ids;
     a.w = w;
-    k_ep_dispatch<<<dim3(ep_chunks(cap, W), W), kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-    EXL3_LAUNCH_CHECK("exl3_ep_dispatch");
+    cudaError_t e = launch_pdl(k_ep_dispatch, dim3(ep_chunks(cap, W), W), dim3(kEpThreads), 0,
+                               static_cast<cudaStream_t>(stream), a);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_ep_dispatch: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }
 
@@ -311,8 +318,9 @@ int exl3_ep_combine(const float* part, int topk, int E, int H, int W, int rank, 
     EXL3_REQUIRE(part && (reinterpret_cast<uintptr_t>(part) & 15) == 0 && H % 4 == 0, EXL3_ERR_ARG,
                  "exl3_ep_combine: part must be 16-byte aligned");
     a.part = part;
-    k_ep_combine<<<dim3(ep_chunks(cap, W), W), kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
-    EXL3_LAUNCH_CHECK("exl3_ep_combine");
+    cudaError_t e = launch_pdl(k_ep_combine, dim3(ep_chunks(cap, W), W), dim3(kEpThreads), 0,
+                               static_cast<cudaStream_t>(stream), a);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_ep_combine: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }
 
@@ -328,8 +336,9 @@ int exl3_ep_reduce(const int32_t* ids, int B, int topk, int E, int H, int W, int
     const long total = (long)B * (H / 4);
     long blocks = (total + kEpThreads - 1) / kEpThreads;
     if (blocks > 4 * num_sms()) blocks = 4 * num_sms();
-    k_ep_reduce<<<(unsigned)blocks, kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, shared, out);
-    EXL3_LAUNCH_CHECK("exl3_ep_reduce");
+    cudaError_t e = launch_pdl(k_ep_reduce, dim3((unsigned)blocks), dim3(kEpThreads), 0,
+                               static_cast<cudaStream_t>(stream), a, shared, out);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_ep_reduce: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }
 

@@ -9,6 +9,8 @@
 //   then, 256-byte aligned: gate|up input rows in xf order fp16 [P][2][H] (row = routed pair index, or pairs + m for
 //   the shared expert's row of token m), down input rows in xf order fp16 [P][I] (by position), the block sums of
 //   both (fp32 [P][2][H/128], [P][I/128]), ybuf fp32 [P][H], GEMV split-unit partial slots.
+#include <type_traits>
+
 #include "gemv.cuh"
 #include "tc.cuh"
 
@@ -289,23 +291,28 @@ __global__ void __launch_bounds__(kRouteWarps * 32) k_route(const float* __restr
 // Router from the hidden states (the router GEMV fused into the launch): CTAs split the experts, one warp per expert
 // computes its logits for every row (fp32 FMA dot over fp16 pairs, lane-strided, then a warp reduction; rounded to
 // fp16 as the reference's routing GEMV does, glm/docs/ext-op-inventory.md:980-1004) into the workspace; the CTA that
-// finishes last (atomic ticket, left at zero for the next call) routes every row.
+// finishes last (atomic ticket, left at zero for the next call) routes every row. With a second router (gate_t1, the
+// next layer's), one GEMV computes both layers' logits over the same hidden states, [R][E0 + E1], and the last CTA also
+// routes the next layer's rows: the reference's layer-ahead prediction in one launch
+// (dsv41/xpu/csrc/dsv_moe_glue.sycl:442-520 route_fused / GemvH; glm/xpu/glm_xpu/moe_patch.py:74-84).
 constexpr int kRhWarps = 8;
 constexpr int kRhRouteWarps = 8;                      // routing warps of the last CTA (static shared memory: 32 KB)
 constexpr int kRhMaxRows = 64;
 
 template <typename T>
 __global__ void __launch_bounds__(kRhWarps * 32) k_route_hidden(const T* __restrict__ hidden, int ldh, int R, int H,
-                                                                const __half* __restrict__ gate_t, float* lg,
+                                                                const __half* __restrict__ gate_t,
+                                                                const __half* __restrict__ gate_t1, float* lg,
                                                                 __half* logits_out, unsigned int* ticket,
-                                                                const RouteParams rp) {
+                                                                const RouteParams rp, const RouteParams rp1) {
     __shared__ float s_score[kRhRouteWarps][kRouteMaxE];
     __shared__ int s_last;
     pdl_wait();                                               // hidden states come from the previous kernel
     const int lane = threadIdx.x & 31, wr = threadIdx.x >> 5;
-    const int E = rp.E;
+    const int E0 = rp.E, E = rp.E + (gate_t1 ? rp1.E : 0);   // logits row stride: both routers' experts
     for (int e = blockIdx.x * kRhWarps + wr; e < E; e += gridDim.x * kRhWarps) {
-        const __half2* g = reinterpret_cast<const __half2*>(gate_t + (size_t)e * H);
+        const __half2* g = reinterpret_cast<const __half2*>(e < E0 ? gate_t + (size_t)e * H
+                                                                   : gate_t1 + (size_t)(e - E0) * H);
         for (int r0 = 0; r0 < R; r0 += 8) {
             float acc[8];
 #pragma unroll
@@ -329,7 +336,7 @@ __global__ void __launch_bounds__(kRhWarps * 32) k_route_hidden(const T* __restr
                 if (lane == 0 && r0 + rr < R) {
                     const __half h = __float2half_rn(v);
                     lg[(size_t)(r0 + rr) * E + e] = __half2float(h);
-                    if (logits_out) logits_out[(size_t)(r0 + rr) * E + e] = h;
+                    if (logits_out && e < E0) logits_out[(size_t)(r0 + rr) * E0 + e] = h;
                 }
             }
         }
@@ -342,8 +349,111 @@ __global__ void __launch_bounds__(kRhWarps * 32) k_route_hidden(const T* __restr
     if (!s_last) return;
     __threadfence();
     if (wr >= kRhRouteWarps) return;
-    for (int row = wr; row < R; row += kRhRouteWarps)
+    for (int row = wr; row < R; row += kRhRouteWarps) {
         route_row_any(lg + (size_t)row * E, row, rp, lane, s_score[wr]);
+        if (gate_t1) route_row_any(lg + (size_t)row * E + E0, row, rp1, lane, s_score[wr]);
+    }
+}
+
+// Router logits for many rows (prefill batches): logits[r][e] = fp16(hidden[r] . gate_t[e]) on the tensor cores
+// (mma.sync m16n8k16, fp16 operands, fp32 accumulation; bf16 hidden states converted to fp16 while staged), the same
+// faithful fp16 rounding as the fused router's GEMV. CTA tile 64 rows x 64 experts, four warps of 32 x 32, 32-deep
+// k chunks staged through shared memory (padded rows: conflict-free ldmatrix), the next chunk loaded into registers
+// while the current one is multiplied.
+constexpr int kRlTile = 64, kRlK = 32, kRlPad = 40;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t r[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(smem_u32(p)));
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 rl_load(const T* src, bool ok) {
+    if (!ok) return make_uint4(0, 0, 0, 0);
+    const uint4 v = *reinterpret_cast<const uint4*>(src);
+    if constexpr (sizeof(T) == 2 && !std::is_same<T, __half>::value) {   // bf16 -> fp16, 8 values
+        const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&v);
+        uint4 o;
+        __half2* h = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h[j] = __float22half2_rn(__bfloat1622float2(b[j]));
+        return o;
+    }
+    return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) k_router_logits(const T* __restrict__ hidden, int ldh, int R, int H,
+                                                       const __half* __restrict__ gate_t, int E, float* logits,
+                                                       __half* logits_f16) {
+    __shared__ __align__(16) __half As[kRlTile][kRlPad];
+    __shared__ __align__(16) __half Bs[kRlTile][kRlPad];
+    pdl_wait();
+    pdl_trigger();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int m_blk = blockIdx.x * kRlTile, n_blk = blockIdx.y * kRlTile;
+    const int wm = (warp >> 1) * 32, wn = (warp & 1) * 32;
+    float acc[2][4][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[i][j][e] = 0.f;
+    // staging: 64 rows x 4 uint4 per tile, two uint4 per thread for each of A and B
+    uint4 ra[2], rb[2];
+    auto load = [&](int k0) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int idx = tid + j * 128, row = idx >> 2, c = (idx & 3) * 8;
+            ra[j] = rl_load<T>(hidden + (size_t)(m_blk + row) * ldh + k0 + c, m_blk + row < R);
+            rb[j] = rl_load<__half>(gate_t + (size_t)(n_blk + row) * H + k0 + c, n_blk + row < E);
+        }
+    };
+    auto store = [&]() {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const int idx = tid + j * 128, row = idx >> 2, c = (idx & 3) * 8;
+            *reinterpret_cast<uint4*>(&As[row][c]) = ra[j];
+            *reinterpret_cast<uint4*>(&Bs[row][c]) = rb[j];
+        }
+    };
+    load(0);
+    for (int k0 = 0; k0 < H; k0 += kRlK) {
+        __syncthreads();
+        store();
+        __syncthreads();
+        if (k0 + kRlK < H) load(k0 + kRlK);
+#pragma unroll
+        for (int kk = 0; kk < kRlK; kk += 16) {
+            uint32_t a[2][4], b[2][4];
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+                ldsm_x4(a[i], &As[wm + i * 16 + (lane & 15)][kk + (lane >> 4) * 8]);
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                ldsm_x4(b[j], &Bs[wn + j * 16 + (lane & 7) + ((lane >> 4) << 3)][kk + ((lane >> 3) & 1) * 8]);
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) mma_16816(acc[i][j], a[i], b[j >> 1][(j & 1) * 2], b[j >> 1][(j & 1) * 2 + 1]);
+        }
+    }
+    const int g = lane >> 2, q = lane & 3;
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int m = m_blk + wm + i * 16 + g + ((e >> 1) << 3), n = n_blk + wn + j * 8 + 2 * q + (e & 1);
+                if (m < R && n < E) {
+                    const __half h = __float2half_rn(acc[i][j][e]);
+                    logits[(size_t)m * E + n] = __half2float(h);
+                    if (logits_f16) logits_f16[(size_t)m * E + n] = h;
+                }
+            }
 }
 
 // ------------------------------------------------------------------------------------------------ align
@@ -1072,41 +1182,91 @@ size_t exl3_route_hidden_workspace_size(int R, int E) {
     return 256 + align_up((size_t)R * E * 4, 256);
 }
 
-int exl3_route_hidden(const void* hidden, int h_dtype, int ldh, int R, int H, const void* gate_t, int E, int kind,
-                      int k, const float* bias, const float* res, const float* mul, float scale, int renorm, void* ids,
-                      int ids64, float* w, void* want, void* logits_out, void* workspace, size_t ws_bytes,
-                      void* stream) {
-    EXL3_REQUIRE(hidden && gate_t && ids && w && R >= 0 && E > 0 && H > 0 && H % 2 == 0 && ldh >= H, EXL3_ERR_ARG,
-                 "exl3_route_hidden: bad arguments");
-    EXL3_REQUIRE(E <= kRouteMaxE, EXL3_ERR_UNSUPPORTED, "exl3_route_hidden: E=%d > %d", E, kRouteMaxE);
+static int route_hidden_launch(const void* hidden, int h_dtype, int ldh, int R, int H, const void* gate_t,
+                               const void* gate_t1, const RouteParams& rp, const RouteParams& rp1, void* logits_out,
+                               void* workspace, size_t ws_bytes, void* stream, const char* what) {
+    const int E = rp.E + (gate_t1 ? rp1.E : 0);
+    EXL3_REQUIRE(hidden && gate_t && rp.ids && rp.w && R >= 0 && rp.E > 0 && H > 0 && H % 2 == 0 && ldh >= H,
+                 EXL3_ERR_ARG, "%s: bad arguments", what);
+    EXL3_REQUIRE(rp.E <= kRouteMaxE && (!gate_t1 || rp1.E <= kRouteMaxE), EXL3_ERR_UNSUPPORTED, "%s: E > %d", what,
+                 kRouteMaxE);
     EXL3_REQUIRE(R <= kRhMaxRows, EXL3_ERR_UNSUPPORTED,
-                 "exl3_route_hidden: R=%d > %d rows (compute the logits with a GEMM and call exl3_route)", R,
+                 "%s: R=%d > %d rows (compute the logits with exl3_router_logits and call exl3_route)", what, R,
                  kRhMaxRows);
-    EXL3_REQUIRE(k >= 1 && k <= kRouteMaxK && k <= E, EXL3_ERR_ARG, "exl3_route_hidden: k=%d", k);
-    EXL3_REQUIRE(kind >= 0 && kind <= 2, EXL3_ERR_ARG, "exl3_route_hidden: kind=%d", kind);
-    EXL3_REQUIRE(h_dtype == EXL3_F16 || h_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "exl3_route_hidden: dtype %d",
-                 h_dtype);
-    EXL3_REQUIRE((reinterpret_cast<uintptr_t>(gate_t) & 3) == 0, EXL3_ERR_ARG,
-                 "exl3_route_hidden: gate_t must be 4-byte aligned");
+    EXL3_REQUIRE(rp.k >= 1 && rp.k <= kRouteMaxK && rp.k <= rp.E, EXL3_ERR_ARG, "%s: k=%d", what, rp.k);
+    EXL3_REQUIRE(rp.kind >= 0 && rp.kind <= 2, EXL3_ERR_ARG, "%s: kind=%d", what, rp.kind);
+    if (gate_t1) {
+        EXL3_REQUIRE(rp1.ids && rp1.w && rp1.E > 0 && rp1.k >= 1 && rp1.k <= kRouteMaxK && rp1.k <= rp1.E &&
+                         rp1.kind >= 0 && rp1.kind <= 2 && (reinterpret_cast<uintptr_t>(gate_t1) & 3) == 0,
+                     EXL3_ERR_ARG, "%s: bad next-layer router arguments", what);
+    }
+    EXL3_REQUIRE(h_dtype == EXL3_F16 || h_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "%s: dtype %d", what, h_dtype);
+    EXL3_REQUIRE((reinterpret_cast<uintptr_t>(gate_t) & 3) == 0, EXL3_ERR_ARG, "%s: gate_t must be 4-byte aligned",
+                 what);
     if (R == 0) return EXL3_OK;
     EXL3_REQUIRE(workspace && ws_bytes >= exl3_route_hidden_workspace_size(R, E), EXL3_ERR_WORKSPACE,
-                 "exl3_route_hidden: workspace %zu < %zu bytes", ws_bytes, exl3_route_hidden_workspace_size(R, E));
+                 "%s: workspace %zu < %zu bytes", what, ws_bytes, exl3_route_hidden_workspace_size(R, E));
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     unsigned int* ticket = reinterpret_cast<unsigned int*>(ws);
     float* lg = reinterpret_cast<float*>(ws + 256);
-    const RouteParams rp = {E, kind, k, bias, res, mul, scale, renorm, ids, ids64, w, want};
     const dim3 grid((E + kRhWarps - 1) / kRhWarps);
     cudaError_t e;
     if (h_dtype == EXL3_BF16)
         e = launch_pdl(k_route_hidden<__nv_bfloat16>, grid, dim3(kRhWarps * 32), 0, static_cast<cudaStream_t>(stream),
-                       static_cast<const __nv_bfloat16*>(hidden), ldh, R, H, static_cast<const __half*>(gate_t), lg,
-                       static_cast<__half*>(logits_out), ticket, rp);
+                       static_cast<const __nv_bfloat16*>(hidden), ldh, R, H, static_cast<const __half*>(gate_t),
+                       static_cast<const __half*>(gate_t1), lg, static_cast<__half*>(logits_out), ticket, rp, rp1);
     else
         e = launch_pdl(k_route_hidden<__half>, grid, dim3(kRhWarps * 32), 0, static_cast<cudaStream_t>(stream),
-                       static_cast<const __half*>(hidden), ldh, R, H, static_cast<const __half*>(gate_t), lg,
-                       static_cast<__half*>(logits_out), ticket, rp);
-    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_route_hidden: launch failed: %s", cudaGetErrorString(e));
+                       static_cast<const __half*>(hidden), ldh, R, H, static_cast<const __half*>(gate_t),
+                       static_cast<const __half*>(gate_t1), lg, static_cast<__half*>(logits_out), ticket, rp, rp1);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
     return EXL3_OK;
+}
+
+int exl3_router_logits(const void* hidden, int h_dtype, int ldh, int R, int H, const void* gate_t, int E,
+                       float* logits, void* logits_f16, void* stream) {
+    EXL3_REQUIRE(hidden && gate_t && logits && R >= 0 && E > 0 && H > 0 && H % kRlK == 0 && ldh >= H && ldh % 8 == 0,
+                 EXL3_ERR_ARG, "exl3_router_logits: bad arguments (H %% 32 == 0, ldh %% 8 == 0)");
+    EXL3_REQUIRE(h_dtype == EXL3_F16 || h_dtype == EXL3_BF16, EXL3_ERR_UNSUPPORTED, "exl3_router_logits: dtype %d",
+                 h_dtype);
+    EXL3_REQUIRE(aligned16(hidden) && aligned16(gate_t), EXL3_ERR_ARG,
+                 "exl3_router_logits: hidden and gate_t must be 16-byte aligned");
+    if (R == 0) return EXL3_OK;
+    const dim3 grid((R + kRlTile - 1) / kRlTile, (E + kRlTile - 1) / kRlTile);
+    cudaError_t e;
+    if (h_dtype == EXL3_BF16)
+        e = launch_pdl(k_router_logits<__nv_bfloat16>, grid, dim3(128), 0, static_cast<cudaStream_t>(stream),
+                       static_cast<const __nv_bfloat16*>(hidden), ldh, R, H, static_cast<const __half*>(gate_t), E,
+                       logits, static_cast<__half*>(logits_f16));
+    else
+        e = launch_pdl(k_router_logits<__half>, grid, dim3(128), 0, static_cast<cudaStream_t>(stream),
+                       static_cast<const __half*>(hidden), ldh, R, H, static_cast<const __half*>(gate_t), E, logits,
+                       static_cast<__half*>(logits_f16));
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_router_logits: launch failed: %s", cudaGetErrorString(e));
+    return EXL3_OK;
+}
+
+int exl3_route_hidden(const void* hidden, int h_dtype, int ldh, int R, int H, const void* gate_t, int E, int kind,
+                      int k, const float* bias, const float* res, const float* mul, float scale, int renorm, void* ids,
+                      int ids64, float* w, void* want, void* logits_out, void* workspace, size_t ws_bytes,
+                      void* stream) {
+    const RouteParams rp = {E, kind, k, bias, res, mul, scale, renorm, ids, ids64, w, want};
+    const RouteParams none = {};
+    return route_hidden_launch(hidden, h_dtype, ldh, R, H, gate_t, nullptr, rp, none, logits_out, workspace, ws_bytes,
+                               stream, "exl3_route_hidden");
+}
+
+int exl3_route_hidden_pair(const void* hidden, int h_dtype, int ldh, int R, int H, const void* gate_t, int E,
+                           int kind, int k, const float* bias, const float* res, const float* mul, float scale,
+                           int renorm, void* ids, int ids64, float* w, void* want, void* logits_out,
+                           const void* gate_t1, int E1, int kind1, int k1, const float* bias1, const float* mul1,
+                           float scale1, int renorm1, void* ids1, int ids1_64, float* w1, void* workspace,
+                           size_t ws_bytes, void* stream) {
+    EXL3_REQUIRE(gate_t1, EXL3_ERR_ARG, "exl3_route_hidden_pair: gate_t1 is null");
+    const RouteParams rp = {E, kind, k, bias, res, mul, scale, renorm, ids, ids64, w, want};
+    const RouteParams rp1 = {E1, kind1, k1, bias1, nullptr, mul1, scale1, renorm1, ids1, ids1_64, w1, nullptr};
+    return route_hidden_launch(hidden, h_dtype, ldh, R, H, gate_t, gate_t1, rp, rp1, logits_out, workspace, ws_bytes,
+                               stream, "exl3_route_hidden_pair");
 }
 
 size_t exl3_moe_workspace_size(int M, int topk, int E, int H, int I, int shared) {

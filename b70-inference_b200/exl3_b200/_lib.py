@@ -50,6 +50,9 @@ _PROTOS = [
     ("exl3_route_hidden_workspace_size", sz, [i32, i32]),
     ("exl3_route_hidden", i32, [vp, i32, i32, i32, i32, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, i32, vp, vp, vp,
                                 vp, sz, vp]),
+    ("exl3_route_hidden_pair", i32, [vp, i32, i32, i32, i32, vp, i32, i32, i32, vp, vp, vp, f32, i32, vp, i32, vp,
+                                     vp, vp, vp, i32, i32, i32, vp, vp, f32, i32, vp, i32, vp, vp, sz, vp]),
+    ("exl3_router_logits", i32, [vp, i32, i32, i32, i32, vp, i32, vp, vp, vp]),
     ("exl3_moe_workspace_size", sz, [i32, i32, i32, i32, i32, i32]),
     ("exl3_moe_decode", i32, [vp, i32, i32, i32, vp, vp, i32, vp, i32, i32, i32, i32, f32, vp, i32, vp, sz, i32,
                               vp]),

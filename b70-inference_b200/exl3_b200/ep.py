@@ -164,16 +164,21 @@ class ExpertParallelMoE:
         self.local_fn = local_fn
         self.shared_fn = shared_fn
 
-    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None
+                ) -> torch.Tensor:
         """x [B, H] fp16/bf16 (this rank's tokens, B <= capacity), ids int32 [B, k] global expert ids, w fp32 [B, k]
-        -> fp32 [B, H]: the routed sum over all ranks' experts (+ the shared expert)."""
+        -> fp32 [B, H]: the routed sum over all ranks' experts (+ the shared expert), written into `out` (fp32,
+        contiguous) when given."""
         B, H = x.shape
         W = self.world
         if W == 1:
-            out = self.local_fn(x, localize_ids(ids, self.e0, self.e1).to(torch.int32), w)
+            res = self.local_fn(x, localize_ids(ids, self.e0, self.e1).to(torch.int32), w)
             if self.shared_fn is not None:
-                out += self.shared_fn(x)
-            return out
+                res += self.shared_fn(x)
+            if out is not None:
+                out.copy_(res)
+                return out
+            return res
         if self.capacity is None:
             self.capacity = B
         cap = self.capacity
@@ -181,7 +186,7 @@ class ExpertParallelMoE:
             raise ValueError(f"expert parallelism: batch of {B} rows exceeds the capacity {cap} of this layer")
         exchange = self.exchange or ("p2p" if x.is_cuda else "nccl")
         if exchange == "p2p":
-            return self._forward_p2p(x, ids, w)
+            return self._forward_p2p(x, ids, w, out)
         k = ids.shape[1]
         ids = ids.to(torch.int32)
         if B < cap:                                     # padding rows: no picks anywhere
@@ -209,14 +214,17 @@ class ExpertParallelMoE:
         # ---- combine: partial rows back to their source rank, summed in rank order ----
         back = torch.empty((W, cap, H), dtype=torch.float32, device=x.device)
         dist.all_to_all_single(back, part.view(W, cap, H).contiguous(), group=self.group)
-        out = back[0, :B].clone()
+        res = back[0, :B].clone()
         for r in range(1, W):
-            out += back[r, :B]
+            res += back[r, :B]
         if self.shared_fn is not None:
-            out += self.shared_fn(x[:B])
-        return out
+            res += self.shared_fn(x[:B])
+        if out is not None:
+            out.copy_(res)
+            return out
+        return res
 
-    def _forward_p2p(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    def _forward_p2p(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, out=None) -> torch.Tensor:
         """dispatch / local experts / combine / reduce on this package's peer-memory kernels."""
         from . import _lib as L
         B, H = x.shape
@@ -237,7 +245,8 @@ class ExpertParallelMoE:
         L.check(lib.exl3_ep_combine(part.data_ptr(), k, self.E, H, W, self.rank, cap, ex.peers.data_ptr(), ex.ptr,
                                     st), "exl3_ep_combine")
         shared = self.shared_fn(xc) if self.shared_fn is not None else None
-        out = torch.empty((B, H), dtype=torch.float32, device=x.device)
+        if out is None or out.dtype != torch.float32 or not out.is_contiguous():
+            out = torch.empty((B, H), dtype=torch.float32, device=x.device)
         L.check(lib.exl3_ep_reduce(idc.data_ptr(), B, k, self.E, H, W, self.rank, cap, L.ptr(shared), ex.ptr,
                                    out.data_ptr(), st), "exl3_ep_reduce")
         return out

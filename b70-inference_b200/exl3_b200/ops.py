@@ -338,41 +338,86 @@ def route(logits: torch.Tensor, kind: int, k: int, bias=None, res=None, mul=None
 ROUTE_HIDDEN_MAX_ROWS = 64
 
 
+def router_logits(hidden: torch.Tensor, gate_t: torch.Tensor, logits_f16: torch.Tensor | None = None) -> torch.Tensor:
+    """logits fp32 [R, E] = fp16(hidden [R, H] @ gate_t [E, H]^T) on the tensor cores (C ABI exl3_router_logits),
+    any R; logits_f16 (optional, fp16 [R, E]) receives the same values in fp16."""
+    L.require_cuda(hidden, gate_t)
+    h = _f16(hidden.reshape(-1, hidden.shape[-1]))
+    if h.data_ptr() % 16 or h.stride(0) % 8:
+        h = h.clone()
+    R, H = h.shape
+    g = gate_t.half().contiguous()
+    E = g.shape[0]
+    out = torch.empty((R, E), dtype=torch.float32, device=h.device)
+    lo = logits_f16
+    if lo is not None and (lo.dtype != torch.float16 or not lo.is_contiguous() or lo.numel() != R * E):
+        raise L.Exl3Error("router_logits: logits_f16 must be a contiguous fp16 [R, E] tensor")
+    rc = L.lib().exl3_router_logits(h.data_ptr(), L.dtype_code(h.dtype), h.stride(0), R, H, g.data_ptr(), E,
+                                    out.data_ptr(), L.ptr(lo), L.stream_of(h))
+    L.check(rc, "exl3_router_logits")
+    return out
+
+
 def route_hidden(hidden: torch.Tensor, gate_t: torch.Tensor, kind: int, k: int, bias=None, res=None, mul=None,
                  scale: float = 1.0, renorm: bool = True, want: bool = False, ids_dtype=torch.int32,
-                 logits_out: torch.Tensor | None = None):
+                 logits_out: torch.Tensor | None = None, next_router: dict | None = None):
     """Top-k routing from hidden states [R, H] fp16/bf16 and the router weight transposed gate_t fp16 [E, H]:
     logits = fp16(hidden @ gate_t^T) then `route`. Up to ROUTE_HIDDEN_MAX_ROWS rows: one fused launch (C ABI
-    exl3_route_hidden); more rows: a library GEMM for the logits, then exl3_route. logits_out (optional, fp16 [R, E])
-    receives the logits. Returns (ids, w, want or None)."""
+    exl3_route_hidden); more rows: the tensor-core router GEMM (exl3_router_logits), then exl3_route. logits_out
+    (optional, fp16 [R, E]) receives the logits. Returns (ids, w, want or None).
+
+    next_router: the next layer's router for the layer-ahead prediction, dict(gate_t fp16 [E1, H], kind, k, and
+    optionally bias, mul, scale, renorm): its logits come from the same GEMV and its picks from the same launch (C ABI
+    exl3_route_hidden_pair); the return value is then (ids, w, want, ids_next, w_next)."""
     L.require_cuda(hidden, gate_t)
     h = _f16(hidden.reshape(-1, hidden.shape[-1]))
     R, H = h.shape
     E = gate_t.shape[0]
     g = gate_t.half().contiguous()
+    f32 = lambda t: t.float().contiguous() if t is not None else None     # noqa: E731
     if R > ROUTE_HIDDEN_MAX_ROWS:
-        logits = torch.matmul(h.float(), g.float().t()).half()
-        if logits_out is not None:
-            logits_out.copy_(logits)
-        return route(logits.float(), kind, k, bias, res, mul, scale, renorm, want, ids_dtype)
+        logits = router_logits(h, g, logits_out)
+        res_ = route(logits, kind, k, bias, res, mul, scale, renorm, want, ids_dtype)
+        if next_router is None:
+            return res_
+        nr = next_router
+        lg1 = router_logits(h, nr["gate_t"])
+        ids1, w1, _ = route(lg1, nr["kind"], nr["k"], nr.get("bias"), None, nr.get("mul"), nr.get("scale", 1.0),
+                            nr.get("renorm", True), False, ids_dtype)
+        return (*res_, ids1, w1)
     dev = h.device
     ids = torch.empty((R, k), dtype=ids_dtype, device=dev)
     w = torch.empty((R, k), dtype=torch.float32, device=dev)
     wt = torch.empty((R, k), dtype=ids_dtype, device=dev) if want else None
-    b = bias.float().contiguous() if bias is not None else None
-    r = res.float().contiguous() if res is not None else None
-    m = mul.float().contiguous() if mul is not None else None
+    b, r, m = f32(bias), f32(res), f32(mul)
     lo = logits_out
     if lo is not None and (lo.dtype != torch.float16 or not lo.is_contiguous() or lo.numel() != R * E):
         raise L.Exl3Error("route_hidden: logits_out must be a contiguous fp16 [R, E] tensor")
     lib = L.lib()
-    ws = L.zeroed_workspace(dev, lib.exl3_route_hidden_workspace_size(R, E), "route_hidden")
-    rc = lib.exl3_route_hidden(h.data_ptr(), L.dtype_code(h.dtype), h.stride(0), R, H, g.data_ptr(), E, int(kind),
-                               int(k), L.ptr(b), L.ptr(r), L.ptr(m), float(scale), int(bool(renorm)), ids.data_ptr(),
-                               int(ids_dtype == torch.int64), w.data_ptr(), L.ptr(wt), L.ptr(lo), ws.data_ptr(),
-                               ws.numel(), L.stream_of(h))
-    L.check(rc, "exl3_route_hidden")
-    return ids, w, wt
+    i64 = int(ids_dtype == torch.int64)
+    if next_router is None:
+        ws = L.zeroed_workspace(dev, lib.exl3_route_hidden_workspace_size(R, E), "route_hidden")
+        rc = lib.exl3_route_hidden(h.data_ptr(), L.dtype_code(h.dtype), h.stride(0), R, H, g.data_ptr(), E, int(kind),
+                                   int(k), L.ptr(b), L.ptr(r), L.ptr(m), float(scale), int(bool(renorm)),
+                                   ids.data_ptr(), i64, w.data_ptr(), L.ptr(wt), L.ptr(lo), ws.data_ptr(), ws.numel(),
+                                   L.stream_of(h))
+        L.check(rc, "exl3_route_hidden")
+        return ids, w, wt
+    nr = next_router
+    g1 = nr["gate_t"].half().contiguous()
+    E1, k1 = g1.shape[0], int(nr["k"])
+    ids1 = torch.empty((R, k1), dtype=ids_dtype, device=dev)
+    w1 = torch.empty((R, k1), dtype=torch.float32, device=dev)
+    b1, m1 = f32(nr.get("bias")), f32(nr.get("mul"))
+    ws = L.zeroed_workspace(dev, lib.exl3_route_hidden_workspace_size(R, E + E1), "route_hidden")
+    rc = lib.exl3_route_hidden_pair(h.data_ptr(), L.dtype_code(h.dtype), h.stride(0), R, H, g.data_ptr(), E,
+                                    int(kind), int(k), L.ptr(b), L.ptr(r), L.ptr(m), float(scale), int(bool(renorm)),
+                                    ids.data_ptr(), i64, w.data_ptr(), L.ptr(wt), L.ptr(lo), g1.data_ptr(), E1,
+                                    int(nr["kind"]), k1, L.ptr(b1), L.ptr(m1), float(nr.get("scale", 1.0)),
+                                    int(bool(nr.get("renorm", True))), ids1.data_ptr(), i64, w1.data_ptr(),
+                                    ws.data_ptr(), ws.numel(), L.stream_of(h))
+    L.check(rc, "exl3_route_hidden_pair")
+    return ids, w, wt, ids1, w1
 
 
 def routing_ds3_nogroup(hidden, gate, scores, bias, topk_indices, topk_weights, scaling_factor, gate_t, act_fn,

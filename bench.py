@@ -503,7 +503,7 @@ def run_decode(ctx, args, wl, cfg, steps, warmup, primary: bool):
             if world == 1:
                 moe.moe_forward(x[l], ids, w, tables[l], cfg["act_limit"], torch.float32, out=out[l], events=events)
             else:
-                out[l].copy_(epm[l].forward(x[l], ids, w))
+                epm[l].forward(x[l], ids, w, out=out[l])
 
     for _ in range(2):                                                  # eager: kernel attributes, communicators
         step()
@@ -662,7 +662,7 @@ def run_prefill(ctx, args, wl, cfg, steps, warmup, primary: bool):
         if world == 1:
             moe.moe_prefill(x, ids, w, table, cfg["act_limit"], out=out, workspace=ws)
         else:
-            out.copy_(epm.forward(x, ids, w))
+            epm.forward(x, ids, w, out=out)
 
     def timed(body):
         ctx.barrier()

@@ -188,6 +188,26 @@ EXL3_API int exl3_route_hidden(const void* hidden, int h_dtype, int ldh, int R, 
                                int renorm, void* ids, int ids64, float* w, void* want, void* logits_out,
                                void* workspace, size_t ws_bytes, void* stream);
 
+/* The fused router above with a second router on the same hidden states: gate_t1 fp16 [E1][H] (the next layer's
+ * router weight transposed) joins the same GEMV ([R][E + E1] logits in the workspace), and the next layer's picks
+ * (ids1, w1; kind1, k1, bias1, mul1, scale1, renorm1 as for exl3_route; no residency bias) come out of the same
+ * launch: the layer-ahead prediction the reference uses as a prefetch hint. workspace >=
+ * exl3_route_hidden_workspace_size(R, E + E1). Replaces route_fused with w1 (dsv41/xpu/csrc/dsv_moe_glue.sycl:
+ * 442-520) and the next-layer router call of glm/xpu/glm_xpu/moe_patch.py:74-84. */
+EXL3_API int exl3_route_hidden_pair(const void* hidden, int h_dtype, int ldh, int R, int H, const void* gate_t, int E,
+                                    int kind, int k, const float* bias, const float* res, const float* mul,
+                                    float scale, int renorm, void* ids, int ids64, float* w, void* want,
+                                    void* logits_out, const void* gate_t1, int E1, int kind1, int k1,
+                                    const float* bias1, const float* mul1, float scale1, int renorm1, void* ids1,
+                                    int ids1_64, float* w1, void* workspace, size_t ws_bytes, void* stream);
+
+/* Router logits for any number of rows on the tensor cores: logits fp32 [R][E] (and logits_f16, optional) =
+ * fp16(hidden [R][H] . gate_t [E][H]) with fp32 accumulation (bf16 hidden states are converted to fp16 on the way),
+ * the fused router's rounding; then exl3_route selects. H % 32 == 0; hidden and gate_t 16-byte aligned, ldh % 8 == 0.
+ * Replaces the routing GEMM of routing_ds3_nogroup at prefill sizes (glm/docs/ext-op-inventory.md:958-1004). */
+EXL3_API int exl3_router_logits(const void* hidden, int h_dtype, int ldh, int R, int H, const void* gate_t, int E,
+                                float* logits, void* logits_f16, void* stream);
+
 /* ---- MoE decode ----
  * Routed MoE layer for decode batches: out[M][H] (fp32 or fp16) = sum_j w[m][j] * expert_{ids[m][j]}(x[m])
  * (+ expert E, the shared expert, with weight 1 when shared != 0), summed in slot order.

@@ -63,10 +63,13 @@ def test_route_bitexact(kind, R, E, k, ties):
 
 @pytest.mark.parametrize("kind", [O.ROUTE_SIGMOID, O.ROUTE_SOFTMAX, O.ROUTE_SQRT_SOFTPLUS])
 @pytest.mark.parametrize("R,H,E,k,dt", [(1, 2048, 512, 10, torch.float16), (4, 6144, 160, 8, torch.bfloat16),
-                                        (37, 256, 1024, 32, torch.float16), (64, 512, 9, 3, torch.float16)])
+                                        (37, 256, 1024, 32, torch.float16), (64, 512, 9, 3, torch.float16),
+                                        (65, 512, 130, 4, torch.float16), (300, 7168, 256, 8, torch.bfloat16),
+                                        (1000, 2048, 512, 10, torch.float16)])
 def test_route_hidden_fused(kind, R, H, E, k, dt):
-    """The router GEMV fused into the routing launch: fp16 logits within one ulp of the fp32 product, then ids
-    bit-exact and weights as the oracle router gives for those logits; repeated calls reuse the zeroed ticket."""
+    """The router GEMV fused into the routing launch (up to 64 rows) or the tensor-core router GEMM (more rows): fp16
+    logits within one ulp of the fp32 product, then ids bit-exact and weights as the oracle router gives for those
+    logits; repeated calls reuse the zeroed ticket."""
     rng = np.random.default_rng(R + H + E + kind)
     hid = torch.from_numpy(rng.standard_normal((R, H)).astype(np.float32)).to(DEV, dt)
     gate_t = torch.from_numpy((rng.standard_normal((E, H)) / np.sqrt(H) * 3).astype(np.float16)).to(DEV)
@@ -90,6 +93,31 @@ def test_route_hidden_fused(kind, R, H, E, k, dt):
         assert np.array_equal(ids.cpu().numpy(), rid), "routed ids must be bit-exact"
         assert np.array_equal(want.cpu().numpy(), rwant)
         np.testing.assert_allclose(w.cpu().numpy(), rw, rtol=2e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("R", [1, 4, 64, 200])
+def test_route_hidden_pair_predicts_the_next_layer(R):
+    """This layer's and the next layer's routers in one launch (exl3_route_hidden_pair): both layers' picks equal
+    the separate routers' on the same hidden states, bit for bit."""
+    rng = np.random.default_rng(900 + R)
+    H, E0, E1 = 1024, 160, 256
+    hid = to_dev(rng.standard_normal((R, H)).astype(np.float16))
+    g0 = to_dev((rng.standard_normal((E0, H)) / np.sqrt(H) * 3).astype(np.float16))
+    g1 = to_dev((rng.standard_normal((E1, H)) / np.sqrt(H) * 3).astype(np.float16))
+    b0 = to_dev((rng.standard_normal(E0) * 0.1).astype(np.float32))
+    b1 = to_dev((rng.standard_normal(E1) * 0.1).astype(np.float32))
+    res = to_dev(np.where(rng.random(E0) < 0.25, 0.1, 0.0).astype(np.float32))
+    lo = torch.empty((R, E0), dtype=torch.float16, device=DEV)
+    ids, w, want, ids1, w1 = ops.route_hidden(hid, g0, O.ROUTE_SIGMOID, 8, bias=b0, res=res, scale=2.5, want=True,
+                                              logits_out=lo, next_router=dict(gate_t=g1, kind=O.ROUTE_SQRT_SOFTPLUS,
+                                                                              k=6, bias=b1, scale=1.5))
+    lo_ref = torch.empty((R, E0), dtype=torch.float16, device=DEV)
+    rid, rw, rwant = ops.route_hidden(hid, g0, O.ROUTE_SIGMOID, 8, bias=b0, res=res, scale=2.5, want=True,
+                                      logits_out=lo_ref)
+    rid1, rw1, _ = ops.route_hidden(hid, g1, O.ROUTE_SQRT_SOFTPLUS, 6, bias=b1, scale=1.5)
+    assert torch.equal(lo, lo_ref)
+    assert torch.equal(ids, rid) and torch.equal(w, rw) and torch.equal(want, rwant)
+    assert torch.equal(ids1, rid1) and torch.equal(w1, rw1)
 
 
 def test_route_prefill_rows_and_int64():
