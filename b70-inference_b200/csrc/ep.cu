@@ -126,9 +126,9 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_dispatch(const EpArgs a) {
             for (int v = threadIdx.x; v < vec; v += blockDim.x) rx[(size_t)i * vec + v] = src[v];
         }
     }
-    __threadfence_system();                                     // every thread's peer stores, before the signal
-    __syncthreads();
-    if (threadIdx.x != 0) return;
+    __syncthreads();                                            // the CTA's peer stores, then one thread fences
+    if (threadIdx.x != 0) return;                               // them at system scope and signals
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
     if (atomicAdd(&ctl->d_sent[p], 1u) == gridDim.x - 1) {     // the last CTA for peer p signals it
         ctl->d_sent[p] = 0;
         __threadfence_system();
@@ -164,9 +164,9 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpArgs a) {
         if (!any) continue;                                    // block-uniform
         for (int v = threadIdx.x; v < vec; v += blockDim.x) dst[(size_t)i * vec + v] = src[(size_t)i * vec + v];
     }
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x != 0) return;
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
     if (atomicAdd(&ctl->c_sent[r], 1u) == gridDim.x - 1) {
         ctl->c_sent[r] = 0;
         __threadfence_system();

@@ -147,7 +147,7 @@ def table_from_piece_store(store_dir: str, layer: int, device="cuda", name: str 
             n = (Kg + Ku + Kd) * unit
             f.seek(off * unit)
             raw = torch.frombuffer(bytearray(f.read(n)), dtype=torch.uint8).to(device)
-            v = torch.from_numpy(np.ascontiguousarray(vec[layer, e])).to(device)
+            v = torch.from_numpy(np.array(vec[layer, e])).to(device)
             experts.append(expert_from_pieces(raw, v, H, I, (Kg, Ku, Kd)))
     return ExpertTable(experts, shared, torch.device(device))
 
