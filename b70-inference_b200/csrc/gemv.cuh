@@ -87,7 +87,6 @@ struct ItemTable {
     const int* item_cnt;     // [max_items], 1..kMaxRows
     const int* pair_src;     // [positions] gate|up activation row of a pair position
     const float* pair_w;     // [positions] routing weight of a pair position
-    const int* pair_tok;     // [positions] token of a pair position (MoE only; the fused combine reads it)
 };
 
 struct GemvArgs {
@@ -111,15 +110,6 @@ struct GemvArgs {
     const float* xsum;
     __half* xf_out;         // gate|up only: the down input in xf order [positions][I]
     float* xsum_out;        // gate|up only: its block sums [positions][I / 128]
-    // down only, optional: the layer's combine fused into the epilogue. The warp that completes the last
-    // contribution to (token m, column block cb) sums ybuf over m's slots in slot order (+ m's shared-expert row) into
-    // comb_out[m][cb * 128 ..] (fp32 or fp16). comb_cnt [tokens][n / 128] zero before the launch, left zero.
-    void* comb_out;
-    int comb_dtype;
-    int* comb_cnt;
-    const int* comb_pair_of;   // [tokens][topk] position of each slot, -1 when dropped
-    const int* comb_n_valid;   // positions of the routed pairs; shared rows follow at n_valid + m
-    int comb_topk, comb_shared;
     // shape of the matrices this launch runs (gate|up: k = H, n = I; down: k = I, n = H)
     int k, n;
     float* partial;         // [2 gridDim.x][unit_floats] split-unit partial sums
@@ -372,6 +362,7 @@ struct EpiOperands {
     float sv[nmat_of(EPI)][4];
     float su_dn[4];                                           // gate|up: suh of the down projection
     float w[kMaxRows / kEpilogueWarps];                       // down: routing weights of rows ew, ew + kEpilogueWarps
+    float c2s0[nmat_of(EPI)];                                 // c2 * S of row ew (the fold's term), per matrix
 };
 
 template <int EPI>
@@ -404,50 +395,14 @@ __device__ __forceinline__ EpiOperands<EPI> epi_operands(const GemvArgs& a, cons
             op.w[i] = row < ui.Mi ? __ldcg(a.items.pair_w + ui.s0 + row) : 0.f;
         }
     }
+    // the fold's activation sum of the warp's first row, before the accumulators are waited for (the other rows of
+    // an item, rare in decode, load theirs in the epilogue)
+#pragma unroll
+    for (int m = 0; m < NMAT; ++m)
+        op.c2s0[m] = ew < ui.Mi ? kMul1C2 * xsum_total(a.xsum + ((size_t)ui.xrow[ew] * NMAT + m) * (a.k / 128),
+                                                       a.k / 128, lane)
+                                : 0.f;
     return op;
-}
-
-// The combine of a MoE decode layer inside the down epilogue (see GemvArgs::comb_out): after position pos's row of
-// column block cb is stored, count it for its token; the warp that completes the token's count sums the token's rows
-// in slot order, as the separate combine kernel does, so the result does not depend on which warp finishes last.
-__device__ __forceinline__ void fused_combine(const GemvArgs& a, int pos, int cb, int lane) {
-    const int m = __ldcg(a.items.pair_tok + pos);
-    const int NB = a.n / 128;
-    __threadfence();
-    __syncwarp();
-    int last = 0;
-    if (lane == 0) {
-        int need = a.comb_shared;
-        for (int j = 0; j < a.comb_topk; ++j) need += __ldcg(a.comb_pair_of + (size_t)m * a.comb_topk + j) >= 0;
-        const int old = atomicAdd(a.comb_cnt + (size_t)m * NB + cb, 1);
-        last = old == need - 1;
-        if (last) {
-            a.comb_cnt[(size_t)m * NB + cb] = 0;                  // left zero for the next launch
-            __threadfence();
-        }
-    }
-    last = __shfl_sync(0xFFFFFFFFu, last, 0);
-    if (!last) return;
-    const int col = cb * 128 + 4 * lane;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < a.comb_topk; ++j) {
-        const int p = __ldcg(a.comb_pair_of + (size_t)m * a.comb_topk + j);
-        if (p < 0) continue;
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.ybuf + (size_t)p * a.n + col));
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-    }
-    if (a.comb_shared) {
-        const int p = __ldcg(a.comb_n_valid) + m;
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.ybuf + (size_t)p * a.n + col));
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-    }
-    if (a.comb_dtype == EXL3_F32) {
-        *reinterpret_cast<float4*>(static_cast<float*>(a.comb_out) + (size_t)m * a.n + col) = acc;
-    } else {
-        __half* o = static_cast<__half*>(a.comb_out) + (size_t)m * a.n + col;
-        o[0] = __float2half_rn(acc.x); o[1] = __float2half_rn(acc.y);
-        o[2] = __float2half_rn(acc.z); o[3] = __float2half_rn(acc.w);
-    }
 }
 
 // Epilogue of one unit from its summed accumulators red[nmat][kMaxRows][128] (shared memory), one row per warp.
@@ -464,8 +419,9 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
             // the codebook affine on the product: c1 * sum h a + c2 * sum a (S: the row's activation sum)
-            const float c2s = kMul1C2 * xsum_total(a.xsum + ((size_t)ui.xrow[row] * NMAT + m) * (a.k / 128),
-                                                   a.k / 128, lane);
+            const float c2s = ri == 0 ? op.c2s0[m]
+                                      : kMul1C2 * xsum_total(a.xsum + ((size_t)ui.xrow[row] * NMAT + m) * (a.k / 128),
+                                                             a.k / 128, lane);
             const float4 t = *reinterpret_cast<const float4*>(red + ((size_t)m * kMaxRows + row) * 128 + 4 * lane);
             v[m][0] = fmaf(kMul1C1, t.x, c2s);
             v[m][1] = fmaf(kMul1C1, t.y, c2s);
@@ -531,7 +487,6 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
             }
             float* dst = a.ybuf + (size_t)(ui.s0 + row) * a.n + col;
             *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
-            if (a.comb_out) fused_combine(a, ui.s0 + row, ui.cb, lane);
         }
     }
 }

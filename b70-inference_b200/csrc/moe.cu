@@ -22,7 +22,7 @@ inline int item_rows(int M) { return M < 8 ? (M > 0 ? M : 1) : 8; }
 struct WsLayout {
     size_t item_expert, item_start, item_cnt, pair_tok, pair_expert, pair_of, pair_w, pair_src, tickets, seg_cnt,
         xf_gu, xf_dn, xsum_gu, xsum_dn, ybuf, partial, total;
-    int max_items, p_max, n_tickets, n_zero;       // n_zero: tickets + the fused combine's counters
+    int max_items, p_max, n_tickets;
 };
 
 constexpr int kAlignSegPairs = 8192;                            // pairs per CTA of the multi-CTA alignment
@@ -44,8 +44,7 @@ inline WsLayout ws_layout(int M, int topk, int E, int H, int I, int shared, int 
     L.pair_of = o; o += (size_t)npairs * 4;
     L.pair_w = o; o += (size_t)L.p_max * 4;
     L.pair_src = o; o += (size_t)L.p_max * 4;
-    L.n_zero = L.n_tickets + M * (H / 128);
-    L.tickets = o; o += (size_t)L.n_zero * 4;
+    L.tickets = o; o += (size_t)L.n_tickets * 4;
     L.seg_cnt = o; o += (size_t)((npairs + kAlignSegPairs - 1) / kAlignSegPairs) * E * 4;   // multi-CTA alignment
     o = align_up(o, 256);
     L.xf_gu = o; o += align_up((size_t)L.p_max * 2 * H * 2, 256);
@@ -777,8 +776,6 @@ struct PrepareArgs {
     int n_tickets;
     __half* xf;                  // [P][2][H]
     float* xsum;                 // [P][2][H / 128] block sums of the rotated rows
-    void* out;                   // with the combine fused into the down launch: the rows of tokens without any
-    int out_dtype;               // contribution (every pick dropped, no shared expert) are zeroed here
 };
 
 __global__ void __launch_bounds__(kAlignThreads) k_prepare(const PrepareArgs a) {
@@ -789,23 +786,6 @@ __global__ void __launch_bounds__(kAlignThreads) k_prepare(const PrepareArgs a) 
         for (int i = threadIdx.x; i < a.n_tickets; i += kAlignThreads) a.tickets[i] = 0;
         if (npairs <= kAlignSmallPairs) align_small(a.ids, a.w, npairs, a.topk, a.E, a.M, a.shared, a.chunk, a.o, sm);
         else align_cta(a.ids, a.w, npairs, a.topk, a.E, a.M, a.shared, a.chunk, a.o, sm);
-        if (a.out && !a.shared) {
-            const int per = a.H / 4;
-            for (int idx = threadIdx.x; idx < a.M * per; idx += kAlignThreads) {
-                const int m = idx / per, c = (idx % per) * 4;
-                bool any = false;
-                for (int j = 0; j < a.topk; ++j) {
-                    const int e = a.ids[(size_t)m * a.topk + j];
-                    any |= e >= 0 && e < a.E;
-                }
-                if (any) continue;
-                if (a.out_dtype == EXL3_F32)
-                    *reinterpret_cast<float4*>(static_cast<float*>(a.out) + (size_t)m * a.H + c) =
-                        make_float4(0.f, 0.f, 0.f, 0.f);
-                else
-                    *reinterpret_cast<uint2*>(static_cast<__half*>(a.out) + (size_t)m * a.H + c) = make_uint2(0, 0);
-            }
-        }
         __threadfence();
         __syncthreads();
         pdl_trigger();
@@ -961,7 +941,7 @@ static int ws_check(void* workspace, size_t ws_bytes, const WsLayout& L, const c
 
 static int run_prepare(const void* x, int x_dtype, int ldx, int M, const int32_t* ids, const float* w, int topk,
                        const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
-                       size_t ws_bytes, cudaStream_t st, void* out = nullptr, int out_dtype = EXL3_F32) {
+                       size_t ws_bytes, cudaStream_t st) {
     int rc = moe_check(M, topk, experts, E, H, I, 0, "exl3_moe_prepare");
     if (rc || M == 0) return rc;
     EXL3_REQUIRE(x && ids && w, EXL3_ERR_ARG, "exl3_moe_prepare: null pointer");
@@ -992,11 +972,9 @@ static int run_prepare(const void* x, int x_dtype, int ldx, int M, const int32_t
     a.experts = reinterpret_cast<const ExpertDesc*>(experts);
     a.o = align_out(ws, L);
     a.tickets = reinterpret_cast<int*>(ws + L.tickets);
-    a.n_tickets = L.n_zero;
+    a.n_tickets = L.n_tickets;
     a.xf = reinterpret_cast<__half*>(ws + L.xf_gu);
     a.xsum = reinterpret_cast<float*>(ws + L.xsum_gu);
-    a.out = out;
-    a.out_dtype = out_dtype;
     const long jobs = (long)L.p_max * 2 * (H / 128);
     long ctas = (jobs + kAlignWarps - 1) / kAlignWarps;
     if (ctas > 2 * num_sms()) ctas = 2 * num_sms();
@@ -1014,7 +992,6 @@ static GemvArgs moe_args(const exl3_expert* experts, float act_limit, uint8_t* w
     a.items.item_cnt = reinterpret_cast<const int*>(ws + L.item_cnt);
     a.items.pair_src = reinterpret_cast<const int*>(ws + L.pair_src);
     a.items.pair_w = reinterpret_cast<const float*>(ws + L.pair_w);
-    a.items.pair_tok = reinterpret_cast<const int*>(ws + L.pair_tok);
     a.ybuf = reinterpret_cast<float*>(ws + L.ybuf);
     a.act_limit = act_limit;
     a.partial = reinterpret_cast<float*>(ws + L.partial);
@@ -1043,7 +1020,7 @@ static int run_gateup(int M, int topk, const exl3_expert* experts, int E, int sh
 }
 
 static int run_down(int M, int topk, const exl3_expert* experts, int E, int shared, int H, int I, void* workspace,
-                    size_t ws_bytes, int n_ctas, cudaStream_t st, void* out = nullptr, int out_dtype = EXL3_F32) {
+                    size_t ws_bytes, int n_ctas, cudaStream_t st) {
     int rc = moe_check(M, topk, experts, E, H, I, n_ctas, "exl3_moe_down");
     if (rc || M == 0) return rc;
     const WsLayout L = ws_layout(M, topk, E, H, I, shared, item_rows(M));
@@ -1055,15 +1032,6 @@ static int run_down(int M, int topk, const exl3_expert* experts, int E, int shar
     a.xsum = reinterpret_cast<const float*>(ws + L.xsum_dn);
     a.k = I;
     a.n = H;
-    if (out) {                                                // the combine in the down epilogue
-        a.comb_out = out;
-        a.comb_dtype = out_dtype;
-        a.comb_cnt = reinterpret_cast<int*>(ws + L.tickets) + L.n_tickets;
-        a.comb_pair_of = reinterpret_cast<const int*>(ws + L.pair_of);
-        a.comb_n_valid = reinterpret_cast<const int*>(ws) + 1;
-        a.comb_topk = topk;
-        a.comb_shared = shared;
-    }
     const GemvPlan pl = plan_gemv(EPI_DOWN, (long long)L.max_items * (H / 128) * (I / 128), n_ctas);
     return launch_gemv<EPI_DOWN>(a, pl, st, "exl3_moe_down");
 }
@@ -1351,13 +1319,13 @@ int exl3_moe_decode(const void* x, int x_dtype, int ldx, int M, const int32_t* i
     EXL3_REQUIRE(out_dtype == EXL3_F16 || out_dtype == EXL3_F32, EXL3_ERR_UNSUPPORTED, "exl3_moe_decode: out dtype");
     if (M == 0) return EXL3_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    rc = run_prepare(x, x_dtype, ldx, M, ids, w, topk, experts, E, shared, H, I, workspace, ws_bytes, st, out,
-                     out_dtype);
+    rc = run_prepare(x, x_dtype, ldx, M, ids, w, topk, experts, E, shared, H, I, workspace, ws_bytes, st);
     if (rc) return rc;
     rc = run_gateup(M, topk, experts, E, shared, H, I, act_limit, workspace, ws_bytes, n_ctas, st);
     if (rc) return rc;
-    // the combine runs inside the down launch's epilogue (fused_combine)
-    return run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, n_ctas, st, out, out_dtype);
+    rc = run_down(M, topk, experts, E, shared, H, I, workspace, ws_bytes, n_ctas, st);
+    if (rc) return rc;
+    return run_combine(M, topk, E, shared, H, I, out, out_dtype, workspace, ws_bytes, st);
 }
 
 }  // extern "C"

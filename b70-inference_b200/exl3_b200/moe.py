@@ -212,7 +212,7 @@ def moe_align(topk_ids: torch.Tensor, topk_w: torch.Tensor, E: int, shared: bool
     max_items = (npairs + active * (chunk - 1)) // chunk + shared_items
     p_max = npairs + (M if shared else 0)
     nseg = (npairs + 8191) // 8192                                          # multi-CTA alignment segments
-    nbytes = 32 + 4 * (3 * max_items + 4 * p_max + npairs + max_items + M + nseg * E)   # tables, tickets, counts
+    nbytes = 32 + 4 * (3 * max_items + 4 * p_max + npairs + max_items + nseg * E)   # tables, tickets, counts
     ws = torch.zeros(nbytes + 4096, dtype=torch.uint8, device=ids.device)
     rc = L.lib().exl3_moe_align(ids.data_ptr(), w.data_ptr(), M, k, E, int(shared), chunk, ws.data_ptr(), ws.numel(),
                                 L.stream_of(ids))
