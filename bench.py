@@ -6,7 +6,7 @@ routed experts of intermediate 512, top-10 softmax router (renormalised), K = 3 
 per GPU. A step is one decode step of the batch through all 48 MoE layers: router -> prepare (alignment + rotated
 activation rows) -> gate|up GEMV -> down GEMV -> fixed-order combine per layer, captured once in a CUDA graph and
 replayed. With N GPUs the experts are sharded expert-parallel (512/N per GPU), tokens are data-parallel (4 per GPU)
-and an NCCL all-to-all pair per layer moves the routed rows; before timing, an extra layer held in full by every rank
+and the peer-memory exchange kernels (dispatch / combine / reduce over NVLink) move the routed rows; before timing, an extra layer held in full by every rank
 checks that the expert-parallel output equals the local one (exit 1 on a mismatch, before any line is printed).
 
 The same line carries the other BASELINE configurations under "extra" (default run only; --workload runs one alone):
@@ -421,7 +421,7 @@ def build_layer(cfg, E_local, e_base, gen, dev):
 
 def ep_check(ctx):
     """Expert-parallel correctness on the GPUs (N > 1): one small layer whose experts every rank holds in full.
-    Each rank runs its own tokens through ExpertParallelMoE (its expert shard, NCCL dispatch / combine) and through
+    Each rank runs its own tokens through ExpertParallelMoE (its expert shard, peer-memory dispatch / combine) and through
     moe_forward on the full table; the two must agree within the parity tolerance (2e-3 relative, 1e-2 max-abs
     scaled to the output rms), at a decode batch (decode kernels) and at a prefill batch (tcgen05 kernels locally).
     Returns the worst relative error over ranks; raises SystemExit(1) on every rank if any rank mismatches."""
@@ -607,12 +607,13 @@ def run_decode(ctx, args, wl, cfg, steps, warmup, primary: bool):
         "e2e": {"value": round(B * world / (ms_e2e * 1e-3), 2), "unit": "tok/s",
                 "h2d_bytes_per_step": int(xh.numel() * 2 + lh.numel() * 4),
                 "d2h_bytes_per_step": int(oh.numel() * 4)},
-        "gpu_launches": 5 * Ltot * steps if world == 1 else 4 * Ltot * steps,
+        "gpu_launches": (5 if world == 1 else 8 + (4 if cfg["shared_K"] else 0)) * Ltot * steps,
         "clocks": clk.summary(),
     }
     if world > 1:
-        line["gpu_launches_note"] = ("our kernels only (route, prepare or align + GEMVs + combine per layer); NCCL "
-                                     "all-to-alls and torch copy kernels of the exchange are not counted")
+        line["gpu_launches_note"] = ("per layer: route, exchange dispatch, the local experts (prepare, gate|up, "
+                                     "down, combine), exchange combine and reduce, and the shared expert's four "
+                                     "when the workload has one; torch fill kernels are not counted")
     del graph, graph_ev
     return line
 
@@ -622,8 +623,8 @@ def run_decode(ctx, args, wl, cfg, steps, warmup, primary: bool):
 def run_prefill(ctx, args, wl, cfg, steps, warmup, primary: bool):
     """One MoE prefill layer per step (route + exl3_moe_prefill) timed with CUDA events. N > 1: expert parallelism
     (weak scaling): every rank routes its own `batch` tokens, holds E/N of the routed experts (plus the shared
-    expert) and exchanges token rows with the others through ExpertParallelMoE (NCCL all-to-all dispatch and
-    combine, the tcgen05 prefill kernels locally); value = all ranks' tokens / the slowest rank's step.
+    expert) and exchanges token rows with the others through ExpertParallelMoE (the peer-memory dispatch /
+    combine / reduce kernels, the tcgen05 prefill kernels locally); value = all ranks' tokens / the slowest rank's step.
     roofline: tensor-bound; achieved = one rank's algorithmic flops (2 tokens topk 3 H I + shared 2 tokens 3 H I)
     / the step time (router, alignment, rotations, combine and the exchange included)."""
     import numpy as np
@@ -699,7 +700,7 @@ def run_prefill(ctx, args, wl, cfg, steps, warmup, primary: bool):
     _, tflops, peak_kind = peaks()
     ach = flops / (ms * 1e-3) / 1e12
     per_call = lambda rows: 8 if rows * topk > 8192 else 7
-    launches = (per_call(T) if world == 1 else 1 + per_call(T * world) + per_call(T)) * steps
+    launches = (per_call(T) if world == 1 else 1 + 3 + per_call(T * world) + per_call(T)) * steps
     line = {
         "metric": "MoE-layer prefill tok/s (tcgen05 grouped GEMM, tensor-pipe fraction)",
         "value": round(world * T / (ms * 1e-3), 1), "unit": "tok/s", "n_gpus": world, "steps": steps,
@@ -820,7 +821,7 @@ RUNNERS = {"decode": run_decode, "prefill": run_prefill, "dense": run_dense}
 
 # DRAM bytes (read + write) per gate|up launch from the committed ncu capture
 # (profiles/k_gemv_moe_qwen_next_full.md), per workload; None where no capture was made.
-TRAFFIC_PER_LAUNCH: dict = {"qwen_next_decode": 31216384 + 39680}
+TRAFFIC_PER_LAUNCH: dict = {"qwen_next_decode": 31226624 + 86272}
 
 
 def main():
