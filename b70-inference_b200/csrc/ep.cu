@@ -205,6 +205,74 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_reduce(const EpArgs a, const 
     }
 }
 
+// The combine and the reduce in one launch: CTA (c, r) returns its rows received from rank r as k_ep_combine does;
+// then every CTA waits (thread 0, bounded) for every peer's combine signal of this call and sums its share of this
+// rank's output rows as k_ep_reduce does. The epoch advances only after every CTA has finished its wait (a second
+// ticket), so no CTA of this launch can read an advanced epoch. All CTAs of the grid are resident together (at most
+// 2 per SM, no shared memory), and no CTA waits on another CTA of its own grid, only on the peers' signals.
+__global__ void __launch_bounds__(kEpThreads) k_ep_combine_reduce(const EpArgs a, const float* shared, float* out) {
+    pdl_wait();
+    pdl_trigger();
+    __shared__ int ok;
+    EpCtl* ctl = reinterpret_cast<EpCtl*>(a.local);
+    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&ctl->combine_epoch) + 1;
+    const int r = blockIdx.y;
+    const int rpc = (a.cap + gridDim.x - 1) / gridDim.x;
+    const int i0 = blockIdx.x * rpc, i1 = min(a.cap, i0 + rpc);
+    uint8_t* peer = reinterpret_cast<uint8_t*>(a.peers[r]);
+    const int32_t* myids = reinterpret_cast<const int32_t*>(a.local + a.L.recv_ids) + (size_t)r * a.cap * a.k;
+    float4* dst = reinterpret_cast<float4*>(peer + a.L.back) + ((size_t)a.rank * a.cap) * (a.H / 4);
+    const float4* src = reinterpret_cast<const float4*>(a.part) + ((size_t)r * a.cap) * (a.H / 4);
+    const int vec = a.H / 4;
+    for (int i = i0; i < i1; ++i) {
+        bool any = false;
+        for (int j = 0; j < a.k; ++j) any |= myids[(size_t)i * a.k + j] >= 0;
+        if (!any) continue;                                    // block-uniform
+        for (int v = threadIdx.x; v < vec; v += blockDim.x) dst[(size_t)i * vec + v] = src[(size_t)i * vec + v];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        if (atomicAdd(&ctl->c_sent[r], 1u) == gridDim.x - 1) {
+            ctl->c_sent[r] = 0;
+            __threadfence_system();
+            EpCtl* pc = reinterpret_cast<EpCtl*>(peer);
+            st_release_sys(&pc->combine_flag[a.rank], epoch);
+        }
+        ok = ep_wait_flags(ctl->combine_flag, a.W, epoch);     // acquire loads: the peers' rows are visible after
+        if (!ok) report(a.status, EXL3_ERR_TIMEOUT);
+    }
+    __syncthreads();
+    if (ok) {
+        const int per = a.E / a.W;
+        const long total = (long)a.B * vec;
+        const long nthr = (long)gridDim.x * gridDim.y * blockDim.x;
+        const float4* back = reinterpret_cast<const float4*>(a.local + a.L.back);
+        for (long t = ((long)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += nthr) {
+            const int i = (int)(t / vec), v = (int)(t % vec);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int p = 0; p < a.W; ++p) {
+                if (!row_picks_rank(a.ids, i, a.k, p, per)) continue;
+                const float4 b = back[((size_t)p * a.cap + i) * vec + v];
+                acc.x += b.x; acc.y += b.y; acc.z += b.z; acc.w += b.w;
+            }
+            if (shared) {
+                const float4 s = reinterpret_cast<const float4*>(shared)[(size_t)i * vec + v];
+                acc.x += s.x; acc.y += s.y; acc.z += s.z; acc.w += s.w;
+            }
+            reinterpret_cast<float4*>(out)[(size_t)i * vec + v] = acc;
+        }
+    }
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(&ctl->c_total, 1u) == gridDim.x * gridDim.y - 1) {
+            ctl->c_total = 0;
+            ctl->combine_epoch = epoch;
+            __threadfence();
+        }
+    }
+}
+
 static int ep_common(EpArgs& a, const uint64_t* peers, void* local, int W, int rank, int cap, int H, int k, int E,
                      int B, const char* what) {
     EXL3_REQUIRE(peers && local && W >= 1 && W <= kEpMaxRanks && rank >= 0 && rank < W, EXL3_ERR_ARG,
@@ -321,6 +389,26 @@ int exl3_ep_combine(const float* part, int topk, int E, int H, int W, int rank, 
     cudaError_t e = launch_pdl(k_ep_combine, dim3(ep_chunks(cap, W), W), dim3(kEpThreads), 0,
                                static_cast<cudaStream_t>(stream), a);
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_ep_combine: launch failed: %s", cudaGetErrorString(e));
+    return EXL3_OK;
+}
+
+int exl3_ep_combine_reduce(const float* part, const int32_t* ids, int B, int topk, int E, int H, int W, int rank,
+                           int cap, const float* shared, const uint64_t* peers, void* local, float* out,
+                           void* stream) {
+    EpArgs a = {};
+    int rc = ep_common(a, peers, local, W, rank, cap, H, topk, E, B, "exl3_ep_combine_reduce");
+    if (rc) return rc;
+    EXL3_REQUIRE(part && (reinterpret_cast<uintptr_t>(part) & 15) == 0 && H % 4 == 0, EXL3_ERR_ARG,
+                 "exl3_ep_combine_reduce: part must be 16-byte aligned");
+    EXL3_REQUIRE(out && (reinterpret_cast<uintptr_t>(out) & 15) == 0 && (B == 0 || ids) &&
+                     (reinterpret_cast<uintptr_t>(shared) & 15) == 0,
+                 EXL3_ERR_ARG, "exl3_ep_combine_reduce: out / shared must be 16-byte aligned, ids non-null");
+    a.part = part;
+    a.ids = ids;
+    cudaError_t e = launch_pdl(k_ep_combine_reduce, dim3(ep_chunks(cap, W), W), dim3(kEpThreads), 0,
+                               static_cast<cudaStream_t>(stream), a, shared, out);
+    EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_ep_combine_reduce: launch failed: %s",
+                 cudaGetErrorString(e));
     return EXL3_OK;
 }
 

@@ -52,7 +52,9 @@ namespace exl3 {
 enum { EPI_LINEAR = 0, EPI_GATEUP = 1, EPI_DOWN = 2 };
 
 constexpr int kTilesPerMat = 8;     // 128 output columns per unit and matrix (one Hadamard block)
-constexpr int kMaxRows = 8;         // MMA N dimension: input rows per unit
+constexpr int kMaxRows = 8;         // MMA N dimension: input rows per row group of a unit
+constexpr int kMaxRowGroups = 2;    // the linear GEMV's units take up to 2 row groups (16 rows, two MMAs per decoded
+                                    // fragment); the MoE units take one
 constexpr int kStageBytes = 8192;   // ring stage (one bulk copy)
 constexpr int kStages = 10;         // ring stages per CTA (80 KB in flight; the rest of the 256 KB stays L1 for the
                                     // activation rows)
@@ -65,8 +67,8 @@ static_assert(kMaxRows % kEpilogueWarps == 0, "epilogue rows per warp");
 
 __host__ __device__ constexpr int nmat_of(int epi) { return epi == EPI_GATEUP ? 2 : 1; }
 __host__ __device__ constexpr int tiles_per_warp(int epi) { return nmat_of(epi) * kTilesPerMat / kConsumers; }
-// floats of one unit's accumulators (also one partial slot): [nmat][kMaxRows][128]
-__host__ __device__ constexpr int unit_floats(int epi) { return nmat_of(epi) * kMaxRows * 128; }
+// floats of one unit's accumulators (also one partial slot): [nmat][kMaxRows * rg][128]
+__host__ __device__ constexpr int unit_floats(int epi, int rg = 1) { return nmat_of(epi) * kMaxRows * rg * 128; }
 
 // Expert descriptor (device table, one entry per expert; the shared expert is an ordinary entry).
 // tr[0] = packed gate|up [I/128][H/16][8 gate tiles | 8 up tiles], tr[1] unused, tr[2] = packed down.
@@ -125,10 +127,10 @@ constexpr int kDescBytes = 128;     // >= sizeof(UnitInfo<any>)
 struct Smem {
     int red_off, bar_off, flag_off, ring_off, desc_off, total;
 };
-__host__ __device__ __forceinline__ Smem smem_layout(int epi) {
+__host__ __device__ __forceinline__ Smem smem_layout(int epi, int rg = 1) {
     Smem s;
     s.red_off = 0;
-    s.bar_off = 2 * kSub * unit_floats(epi) * 4;
+    s.bar_off = 2 * kSub * unit_floats(epi, rg) * 4;
     s.flag_off = s.bar_off + (2 * kStages + 4) * 8;
     s.ring_off = (s.flag_off + 16 + 127) & ~127;
     s.desc_off = s.ring_off + kStages * kStageBytes;
@@ -197,23 +199,29 @@ __device__ __forceinline__ void rotated_block(const TIn* x, const __half* suh, i
 // (ring sequence numbers it with it % kSub == sub, visited directly), continuing the CTA's ring sequence at `it` and
 // leaving it at the segment's end. The ring couples the sub-groups: one that falls behind holds the producer back, and
 // the others then wait and leave it the issue slots. The B fragments of a stage's first kBatch tile-rows are loaded
-// before the stage's full barrier is waited on, and each further row's fragment kBatch rows ahead.
-// d[t] = D[16 n x 8 rows] of tile t: d[0], d[1] = (n = g, rows 2q, 2q+1), d[2], d[3] = (n = g + 8, rows 2q, 2q+1).
-template <int K, int TPW>
-__device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, int row_stride, int mat_off, int tile0,
-                                        int n_rows, int rps, int sub, uint64_t* full, uint64_t* empty,
-                                        const __half* xf_row, bool has_row, int lane, int& it, bool& timed_out) {
-    constexpr int kBatch = TPW >= 4 ? 2 : 4;             // B fragments in flight (registers: the 4-tile warps hold
-                                                          // twice the accumulators)
+// before the stage's full barrier is waited on, and each further row's fragment kBatch rows ahead. With RG row groups
+// (the linear's 9..16-row calls) every decoded fragment feeds RG MMAs, one per group of 8 input rows.
+// d[rg * TPW + t] = D[16 n x 8 rows] of tile t and row group rg: d[.][0], d[.][1] = (n = g, rows 2q, 2q+1),
+// d[.][2], d[.][3] = (n = g + 8, rows 2q, 2q+1), rows counted inside the group.
+template <int K, int TPW, int RG>
+__device__ __forceinline__ void consume(float d[RG * TPW][4], const uint8_t* ring, int row_stride, int mat_off,
+                                        int tile0, int n_rows, int rps, int sub, uint64_t* full, uint64_t* empty,
+                                        const __half* const xf_row[RG], const bool has_row[RG], int lane, int& it,
+                                        bool& timed_out) {
+    constexpr int kBatch = RG > 1 ? 1 : (TPW >= 4 ? 2 : 4);   // B fragments in flight per group (registers: the
+                                                              // 4-tile warps and the 2-group calls hold twice the
+                                                              // accumulators)
     const LaneWords lw = lane_words<K>(lane);
     const int q = lane & 3;
-    // B fragment of tile-row r for this lane: 8 bytes at xf_row + r * 16 + q * 4
-    const uint2* bp = reinterpret_cast<const uint2*>(xf_row + q * 4);
+    // B fragment of tile-row r for this lane and group: 8 bytes at xf_row[rg] + r * 16 + q * 4
+    const uint2* bp[RG];
+#pragma unroll
+    for (int rg = 0; rg < RG; ++rg) bp[rg] = reinterpret_cast<const uint2*>(xf_row[rg] + q * 4);
     // a stage of a segment whose matrices share K holds RPS whole tile-rows of a compile-time stride: that case
     // runs fully unrolled with every row's B fragment loaded before the stage's barrier
     constexpr int RS = (TPW / 2) * kTilesPerMat * 32 * K;
     constexpr int RPS = kStageBytes / RS;
-    constexpr int UNR = RPS <= (TPW >= 4 ? 5 : 10) ? RPS : 0;
+    constexpr int UNR = RG == 1 && RPS <= (TPW >= 4 ? 5 : 10) ? RPS : 0;
     const int nst = (n_rows + rps - 1) / rps, it_begin = it;
     for (int j = (sub - it % kSub + kSub) % kSub; j < nst; j += kSub) {
         it = it_begin + j;
@@ -222,9 +230,12 @@ __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, in
         const int rows = min(rps, n_rows - r0);
         if constexpr (UNR > 0) {
             if (row_stride == RS && rows == RPS) {
-                uint2 bf[UNR > 0 ? UNR : 1];
+                uint2 bf[UNR > 0 ? UNR : 1][RG];
 #pragma unroll
-                for (int r = 0; r < UNR; ++r) bf[r] = has_row ? __ldg(bp + (size_t)(r0 + r) * 4) : make_uint2(0, 0);
+                for (int r = 0; r < UNR; ++r)
+#pragma unroll
+                    for (int rg = 0; rg < RG; ++rg)
+                        bf[r][rg] = has_row[rg] ? __ldg(bp[rg] + (size_t)(r0 + r) * 4) : make_uint2(0, 0);
                 if (!timed_out && !mbar_wait(&full[s], (it / kStages) & 1)) timed_out = true;
                 if (!timed_out) {
                     const uint8_t* base = ring + (size_t)s * kStageBytes + mat_off + tile0 * 32 * K;
@@ -234,7 +245,8 @@ __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, in
                         for (int t = 0; t < TPW; ++t) {
                             uint32_t a[4];
                             decode_frag_raw<K>(reinterpret_cast<const uint32_t*>(base + r * RS + t * 32 * K), lw, a);
-                            mma_16816(d[t], a, bf[r].x, bf[r].y);
+#pragma unroll
+                            for (int rg = 0; rg < RG; ++rg) mma_16816(d[rg * TPW + t], a, bf[r][rg].x, bf[r][rg].y);
                         }
                     }
                 }
@@ -243,10 +255,12 @@ __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, in
                 continue;
             }
         }
-        uint2 bq[kBatch];
+        uint2 bq[kBatch][RG];
 #pragma unroll
         for (int b = 0; b < kBatch; ++b)
-            bq[b] = (has_row && b < rows) ? __ldg(bp + (size_t)(r0 + b) * 4) : make_uint2(0, 0);
+#pragma unroll
+            for (int rg = 0; rg < RG; ++rg)
+                bq[b][rg] = (has_row[rg] && b < rows) ? __ldg(bp[rg] + (size_t)(r0 + b) * 4) : make_uint2(0, 0);
         if (!timed_out && !mbar_wait(&full[s], (it / kStages) & 1)) timed_out = true;
         if (!timed_out) {
             const uint8_t* base = ring + (size_t)s * kStageBytes + mat_off + tile0 * 32 * K;
@@ -254,14 +268,19 @@ __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, in
 #pragma unroll
                 for (int b = 0; b < kBatch; ++b) {
                     if (rb + b < rows) {
-                        const uint2 bv = bq[b];
+                        uint2 bv[RG];
                         const int nx = rb + kBatch + b;            // the row this slot holds next
-                        if (has_row && nx < rows) bq[b] = __ldg(bp + (size_t)(r0 + nx) * 4);
+#pragma unroll
+                        for (int rg = 0; rg < RG; ++rg) {
+                            bv[rg] = bq[b][rg];
+                            if (has_row[rg] && nx < rows) bq[b][rg] = __ldg(bp[rg] + (size_t)(r0 + nx) * 4);
+                        }
 #pragma unroll
                         for (int t = 0; t < TPW; ++t) {
                             uint32_t a[4];
                             decode_frag_raw<K>(reinterpret_cast<const uint32_t*>(base + t * 32 * K), lw, a);
-                            mma_16816(d[t], a, bv.x, bv.y);
+#pragma unroll
+                            for (int rg = 0; rg < RG; ++rg) mma_16816(d[rg * TPW + t], a, bv[rg].x, bv[rg].y);
                         }
                         base += row_stride;
                     }
@@ -274,13 +293,14 @@ __device__ __forceinline__ void consume(float d[TPW][4], const uint8_t* ring, in
     it = it_begin + nst;
 }
 
-template <int TPW>
-__device__ __forceinline__ void consume_k(int K, float d[TPW][4], const uint8_t* ring, int row_stride, int mat_off,
-                                          int tile0, int n_rows, int rps, int sub, uint64_t* full, uint64_t* empty,
-                                          const __half* xf_row, bool has_row, int lane, int& it, bool& to) {
+template <int TPW, int RG>
+__device__ __forceinline__ void consume_k(int K, float d[RG * TPW][4], const uint8_t* ring, int row_stride,
+                                          int mat_off, int tile0, int n_rows, int rps, int sub, uint64_t* full,
+                                          uint64_t* empty, const __half* const xf_row[RG], const bool has_row[RG],
+                                          int lane, int& it, bool& to) {
 #define EXL3_CONSUME(KK)                                                                                          \
-    consume<KK, TPW>(d, ring, row_stride, mat_off, tile0, n_rows, rps, sub, full, empty, xf_row, has_row, lane,    \
-                     it, to)
+    consume<KK, TPW, RG>(d, ring, row_stride, mat_off, tile0, n_rows, rps, sub, full, empty, xf_row, has_row,     \
+                         lane, it, to)
     switch (K) {
         case 1: EXL3_CONSUME(1); break;
         case 2: EXL3_CONSUME(2); break;
@@ -353,6 +373,13 @@ __device__ __forceinline__ UnitInfo<EPI> unit_info(const GemvArgs& a, int u, int
     return ui;
 }
 
+// Activation row of the unit's input row `row` (the linear's rows are the call's rows; up to 16 of them).
+template <int EPI>
+__device__ __forceinline__ int xrow_of(const UnitInfo<EPI>& ui, int row) {
+    if constexpr (EPI == EPI_LINEAR) return row;
+    else return ui.xrow[row];
+}
+
 // The epilogue operands of a unit for lane `lane` (columns cb * 128 + 4 lane ..+3) of epilogue warp ew: output
 // scales of each matrix, the down projection's input signs (gate|up), the routing weights of the warp's rows (down).
 // Loaded before the epilogue warps wait for the unit's accumulators, so that the dependent loads (expert descriptor,
@@ -399,20 +426,21 @@ __device__ __forceinline__ EpiOperands<EPI> epi_operands(const GemvArgs& a, cons
     // an item, rare in decode, load theirs in the epilogue)
 #pragma unroll
     for (int m = 0; m < NMAT; ++m)
-        op.c2s0[m] = ew < ui.Mi ? kMul1C2 * xsum_total(a.xsum + ((size_t)ui.xrow[ew] * NMAT + m) * (a.k / 128),
+        op.c2s0[m] = ew < ui.Mi ? kMul1C2 * xsum_total(a.xsum + ((size_t)xrow_of(ui, ew) * NMAT + m) * (a.k / 128),
                                                        a.k / 128, lane)
                                 : 0.f;
     return op;
 }
 
-// Epilogue of one unit from its summed accumulators red[nmat][kMaxRows][128] (shared memory), one row per warp.
-template <int EPI>
+// Epilogue of one unit from its summed accumulators red[nmat][kMaxRows * RG][128] (shared memory), one row per warp.
+template <int EPI, int RG>
 __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<EPI>& ui, const float* red, int ew,
                                               int lane, const EpiOperands<EPI>& op) {
     constexpr int NMAT = nmat_of(EPI);
+    constexpr int R = kMaxRows * RG;
     const int col = ui.cb * 128 + 4 * lane;
-#pragma unroll
-    for (int ri = 0; ri < kMaxRows / kEpilogueWarps; ++ri) {
+#pragma unroll(RG == 1 ? R / kEpilogueWarps : 1)
+    for (int ri = 0; ri < R / kEpilogueWarps; ++ri) {
         const int row = ew + ri * kEpilogueWarps;
         if (row >= ui.Mi) break;
         float v[NMAT][4];
@@ -420,9 +448,9 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
         for (int m = 0; m < NMAT; ++m) {
             // the codebook affine on the product: c1 * sum h a + c2 * sum a (S: the row's activation sum)
             const float c2s = ri == 0 ? op.c2s0[m]
-                                      : kMul1C2 * xsum_total(a.xsum + ((size_t)ui.xrow[row] * NMAT + m) * (a.k / 128),
+                                      : kMul1C2 * xsum_total(a.xsum + ((size_t)xrow_of(ui, row) * NMAT + m) * (a.k / 128),
                                                              a.k / 128, lane);
-            const float4 t = *reinterpret_cast<const float4*>(red + ((size_t)m * kMaxRows + row) * 128 + 4 * lane);
+            const float4 t = *reinterpret_cast<const float4*>(red + ((size_t)m * R + row) * 128 + 4 * lane);
             v[m][0] = fmaf(kMul1C1, t.x, c2s);
             v[m][1] = fmaf(kMul1C1, t.y, c2s);
             v[m][2] = fmaf(kMul1C1, t.z, c2s);
@@ -502,11 +530,13 @@ __device__ __forceinline__ long long next_owner(long long c, long long T, long l
 
 // Grid: persistent, at most one CTA per SM, each a contiguous range of the launch's k-blocks; block: 1 producer warp,
 // kConsumerWarps consumer warps, kEpilogueWarps epilogue warps.
-template <int EPI>
+template <int EPI, int RG>
 __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
+    static_assert(RG >= 1 && RG <= kMaxRowGroups && (RG == 1 || EPI == EPI_LINEAR), "row groups: linear only");
     constexpr int NMAT = nmat_of(EPI);
     constexpr int TPW = tiles_per_warp(EPI);
-    constexpr int UF = unit_floats(EPI);
+    constexpr int R = kMaxRows * RG;                            // input rows of a unit
+    constexpr int UF = unit_floats(EPI, RG);
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_trigger();
@@ -518,7 +548,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
     const long long T = (long long)U * KB;
     const long long r0 = range_start(ci, T, G), r1 = range_start(ci + 1, T, G);
 
-    const Smem L = smem_layout(EPI);
+    const Smem L = smem_layout(EPI, RG);
     float* red = reinterpret_cast<float*>(smem + L.red_off);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
     uint64_t* empty = full + kStages;
@@ -587,32 +617,40 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
             const int lo = i == 0 ? (int)(r0 - u * KB) : 0;
             const int hi = (int)min((long long)KB, r1 - u * KB);
             const UnitInfo<EPI> ui = i < kMaxSeg ? descs[i] : unit_info<EPI>(args, (int)u, NB, KB);
-            const bool has_row = g < ui.Mi;
-            const __half* xf_row =
-                args.xf + (size_t)ui.xrow[g] * NMAT * args.k + (size_t)m * args.k + (size_t)lo * 128;
+            bool has_row[RG];
+            const __half* xf_row[RG];
+#pragma unroll
+            for (int rg = 0; rg < RG; ++rg) {
+                const int row = g + kMaxRows * rg;
+                has_row[rg] = row < ui.Mi;
+                const int xr = RG == 1 ? ui.xrow[g] : (has_row[rg] ? row : 0);
+                xf_row[rg] = args.xf + (size_t)xr * NMAT * args.k + (size_t)m * args.k + (size_t)lo * 128;
+            }
             int mat_off = 0;
 #pragma unroll
             for (int mm = 0; mm < NMAT; ++mm)
                 if (mm < m) mat_off += kTilesPerMat * 32 * ui.K[mm];
-            float d[TPW][4];
+            float d[RG * TPW][4];
 #pragma unroll
-            for (int t = 0; t < TPW; ++t)
+            for (int t = 0; t < RG * TPW; ++t)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) d[t][e] = 0.f;
-            consume_k<TPW>(ui.K[m], d, ring, ui.row_stride, mat_off, tile0, (hi - lo) * 8,
-                           kStageBytes / ui.row_stride, sub, full, empty, xf_row, has_row, lane, it, to);
+            consume_k<TPW, RG>(ui.K[m], d, ring, ui.row_stride, mat_off, tile0, (hi - lo) * 8,
+                               kStageBytes / ui.row_stride, sub, full, empty, xf_row, has_row, lane, it, to);
             // hand the accumulators over: red[i & 1][sub], once the epilogue released segment i - 2's
             const int buf = i & 1;
             if (i >= 2 && !to && !mbar_wait(&acc_empty[buf], ((i >> 1) - 1) & 1)) to = true;
             float* rs = red + ((size_t)buf * kSub + sub) * UF;
 #pragma unroll
-            for (int t = 0; t < TPW; ++t)
+            for (int rg = 0; rg < RG; ++rg)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int row = 2 * q + (e & 1);
-                    const int col = (tile0 + t) * 16 + g + ((e >> 1) << 3);
-                    rs[((size_t)m * kMaxRows + row) * 128 + col] = d[t][e];
-                }
+                for (int t = 0; t < TPW; ++t)
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int row = kMaxRows * rg + 2 * q + (e & 1);
+                        const int col = (tile0 + t) * 16 + g + ((e >> 1) << 3);
+                        rs[((size_t)m * R + row) * 128 + col] = d[rg * TPW + t][e];
+                    }
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_full[buf]);
         }
@@ -638,7 +676,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
         float4* slot = reinterpret_cast<float4*>(args.partial + (size_t)(i == 0 ? 2 * ci : 2 * ci + 1) * UF);
         // sub-group sums in sub-group order: into rb[0] (whole unit) or this CTA's partial slot
         for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
-            if ((e / 32) % kMaxRows >= ui.Mi) continue;       // rows beyond the unit's
+            if ((e / 32) % R >= ui.Mi) continue;              // rows beyond the unit's
             float4 acc = reinterpret_cast<const float4*>(rb)[e];
 #pragma unroll
             for (int j = 1; j < kSub; ++j) {
@@ -677,7 +715,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
                     if (range_start(c + 1, T, G) >= a1) break;
                 }
                 for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
-                    if ((e / 32) % kMaxRows >= ui.Mi) continue;
+                    if ((e / 32) % R >= ui.Mi) continue;
                     float4 p[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
@@ -702,7 +740,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
         }
         if (finish) {
             epilogue_sync();
-            unit_epilogue<EPI>(args, ui, rb, ew, lane, op);
+            unit_epilogue<EPI, RG>(args, ui, rb, ew, lane, op);
         }
         epilogue_sync();                                      // the flag and red[buf] are read: release them
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
@@ -769,26 +807,26 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 
 // Split-unit partial slots of a GEMV launch on the current device (workspace sizing): two per CTA.
 inline int max_ctas() { return num_sms(); }
-inline size_t partial_bytes(int epi) { return (size_t)2 * max_ctas() * unit_floats(epi) * 4; }
+inline size_t partial_bytes(int epi, int rg = 1) { return (size_t)2 * max_ctas() * unit_floats(epi, rg) * 4; }
 
 // Work decomposition: one CTA per SM, or fewer when the launch has fewer k-blocks; `ctas` > 0 overrides the count
 // (tests, tuning).
 struct GemvPlan {
     int ctas, smem;
 };
-inline GemvPlan plan_gemv(int epi, long long work_upper, int ctas) {
+inline GemvPlan plan_gemv(int epi, long long work_upper, int ctas, int rg = 1) {
     GemvPlan pl;
     const int sms = max_ctas();
     if (ctas <= 0) ctas = work_upper < sms ? (int)(work_upper < 1 ? 1 : work_upper) : sms;
     pl.ctas = ctas > sms ? sms : ctas;
-    pl.smem = smem_layout(epi).total;
+    pl.smem = smem_layout(epi, rg).total;
     return pl;
 }
 
-template <int EPI>
+template <int EPI, int RG = 1>
 int launch_gemv(GemvArgs a, const GemvPlan& pl, cudaStream_t st, const char* what) {
     EXL3_REQUIRE(pl.smem <= 227 * 1024, EXL3_ERR_UNSUPPORTED, "%s: shared memory plan too large", what);
-    auto kern = k_gemv<EPI>;
+    auto kern = k_gemv<EPI, RG>;
     static int configured[64] = {0};
     int dev = 0;
     cudaGetDevice(&dev);

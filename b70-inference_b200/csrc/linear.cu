@@ -154,7 +154,7 @@ static GemvWs gemv_ws(int M, int k, int n) {
     w.xsum = align_up((size_t)M * k * 2, 256);
     w.tickets = align_up(w.xsum + (size_t)M * (k / 128) * 4, 256);
     w.partial = align_up(w.tickets + (size_t)(n / 128) * 4, 256);
-    w.total = w.partial + partial_bytes(EPI_LINEAR);
+    w.total = w.partial + partial_bytes(EPI_LINEAR, M > kMaxRows ? 2 : 1);
     return w;
 }
 
@@ -227,7 +227,7 @@ int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* packed, co
               int n_ctas, void* stream) {
     EXL3_REQUIRE(cb == 2, EXL3_ERR_UNSUPPORTED, "exl3_gemv: only the mul1 codebook (cb=2) is supported");
     EXL3_REQUIRE(K >= 1 && K <= 8, EXL3_ERR_UNSUPPORTED, "exl3_gemv: K=%d not in 1..8", K);
-    EXL3_REQUIRE(M >= 0 && M <= kMaxRows, EXL3_ERR_ARG, "exl3_gemv: M=%d rows (1..8 per call)", M);
+    EXL3_REQUIRE(M >= 0 && M <= kMaxRows * kMaxRowGroups, EXL3_ERR_ARG, "exl3_gemv: M=%d rows (1..16 per call)", M);
     EXL3_REQUIRE(k > 0 && n > 0 && k % 128 == 0 && n % 128 == 0, EXL3_ERR_ARG,
                  "exl3_gemv: k=%d, n=%d must be multiples of 128", k, n);
     EXL3_REQUIRE(x && packed && svh && y, EXL3_ERR_ARG, "exl3_gemv: null pointer");
@@ -278,6 +278,10 @@ int exl3_gemv(const void* x, int x_dtype, int ldx, int M, const void* packed, co
     a.partial = reinterpret_cast<float*>(ws + W.partial);
     a.counters = tickets;
     a.status = device_status_ptr();
+    if (M > kMaxRows) {                                       // 9..16 rows: two MMAs per decoded fragment
+        const GemvPlan pl = plan_gemv(EPI_LINEAR, (long long)(n / 128) * (k / 128), n_ctas, 2);
+        return launch_gemv<EPI_LINEAR, 2>(a, pl, st, "exl3_gemv");
+    }
     const GemvPlan pl = plan_gemv(EPI_LINEAR, (long long)(n / 128) * (k / 128), n_ctas);
     return launch_gemv<EPI_LINEAR>(a, pl, st, "exl3_gemv");
 }

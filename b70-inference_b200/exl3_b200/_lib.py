@@ -73,6 +73,7 @@ _PROTOS = [
     ("exl3_ep_dispatch", i32, [vp, i32, i32, i32, vp, vp, i32, i32, i32, i32, i32, i32, vp, vp, vp]),
     ("exl3_ep_combine", i32, [vp, i32, i32, i32, i32, i32, i32, vp, vp, vp]),
     ("exl3_ep_reduce", i32, [vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp]),
+    ("exl3_ep_combine_reduce", i32, [vp, vp, i32, i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]),
 ]
 
 _lib = None

@@ -14,7 +14,8 @@ data-parallel, and each layer exchanges the routed rows in three steps:
 
 Two exchanges implement dispatch / combine:
   "p2p" (GPUs, the default there): this package's kernels write straight into the peers' exchange buffers over
-        NVLink (exl3_ep_dispatch / exl3_ep_combine / exl3_ep_reduce; buffers shared once through CUDA IPC handles):
+        NVLink (exl3_ep_dispatch, then exl3_ep_combine_reduce, or exl3_ep_combine / exl3_ep_reduce as two launches;
+        buffers shared once through CUDA IPC handles):
         a row's activations go only to the ranks it picked, a partial row comes back only from the ranks it picked,
         no host synchronisation, no collective launch, graph-capturable (the calls count themselves on the device);
   "nccl": two NCCL (or gloo) all_to_all_single calls per layer on fixed-size chunks (every row to every rank), and
@@ -141,6 +142,7 @@ class ExpertParallelMoE:
         self.group = group
         self.capacity = capacity
         self.exchange = exchange
+        self.fused_reduce = True          # p2p: combine and reduce in one launch (exl3_ep_combine_reduce)
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.E, self.H, self.topk = E, H, topk
@@ -242,11 +244,17 @@ class ExpertParallelMoE:
         xr, rid, rw = ex.recv_views(xc.dtype)
         part = self.local_fn(xr, rid, rw)
         part = part.contiguous()
-        L.check(lib.exl3_ep_combine(part.data_ptr(), k, self.E, H, W, self.rank, cap, ex.peers.data_ptr(), ex.ptr,
-                                    st), "exl3_ep_combine")
-        shared = self.shared_fn(xc) if self.shared_fn is not None else None
         if out is None or out.dtype != torch.float32 or not out.is_contiguous():
             out = torch.empty((B, H), dtype=torch.float32, device=x.device)
+        if self.fused_reduce:
+            shared = self.shared_fn(xc).contiguous() if self.shared_fn is not None else None
+            L.check(lib.exl3_ep_combine_reduce(part.data_ptr(), idc.data_ptr(), B, k, self.E, H, W, self.rank, cap,
+                                               L.ptr(shared), ex.peers.data_ptr(), ex.ptr, out.data_ptr(), st),
+                    "exl3_ep_combine_reduce")
+            return out
+        L.check(lib.exl3_ep_combine(part.data_ptr(), k, self.E, H, W, self.rank, cap, ex.peers.data_ptr(), ex.ptr,
+                                    st), "exl3_ep_combine")
+        shared = self.shared_fn(xc).contiguous() if self.shared_fn is not None else None
         L.check(lib.exl3_ep_reduce(idc.data_ptr(), B, k, self.E, H, W, self.rank, cap, L.ptr(shared), ex.ptr,
                                    out.data_ptr(), st), "exl3_ep_reduce")
         return out

@@ -13,7 +13,8 @@ import torch
 
 from . import _lib as L
 
-SMALL_M_MAX = int(os.environ.get("EXL3_SMALL_M_MAX", "32"))        # rows up to this: fused decode GEMV (8-row calls)
+SMALL_M_MAX = int(os.environ.get("EXL3_SMALL_M_MAX", "32"))        # rows up to this: fused decode GEMV (16-row calls)
+GEMV_MAX_ROWS = 16                                                  # rows per exl3_gemv call
 
 
 def _f16(t: torch.Tensor) -> torch.Tensor:
@@ -48,7 +49,7 @@ def pack_gateup(gate: torch.Tensor, up: torch.Tensor, Kg: int, Ku: int) -> torch
 
 def exl3_gemv(x: torch.Tensor, packed: torch.Tensor, suh: torch.Tensor, svh: torch.Tensor, K: int,
               y: torch.Tensor, n_ctas: int = 0, workspace: torch.Tensor | None = None) -> None:
-    """y[M, n] = Had(Had(x * suh) @ W_hat) * svh for M <= 8 rows; packed = pack(trellis, K); y fp16/bf16/fp32
+    """y[M, n] = Had(Had(x * suh) @ W_hat) * svh for M <= 16 rows; packed = pack(trellis, K); y fp16/bf16/fp32
     preallocated (C ABI exl3_gemv). n_ctas: CTAs of the persistent launch (0 = one per SM)."""
     L.require_cuda(x, packed, y)
     M, k = x.shape
@@ -137,7 +138,8 @@ class BC_LinearEXL3:
     glm/docs/ext-op-inventory.md:471-496). Other modules read trellis/suh/svh/K/mcg/mul1 by name.
 
     run(x, y): x fp16/bf16 [..., k] -> y (fp16/bf16/fp32, preallocated) [..., n].
-      rows <= SMALL_M_MAX: the fused decode GEMV, 8 rows per launch (weights streamed once per launch);
+      rows <= SMALL_M_MAX: the fused decode GEMV, up to 16 rows per launch (weights streamed and decoded once per
+      launch, each decoded fragment feeding one MMA per 8 rows);
       larger: the tcgen05 linear (exl3_gemm_tc: trellis decoded into tensor memory, 2-SM MMAs, weights decoded once
       per 320 rows), in place of the reference's dequantise + library GEMM prefill path
       (glm/xpu/csrc/exl3_ops.sycl:651-757)."""
@@ -177,8 +179,8 @@ class BC_LinearEXL3:
             return
         if M <= SMALL_M_MAX:
             pk = self.packed()
-            for m0 in range(0, M, 8):
-                exl3_gemv(x2[m0:m0 + 8], pk, self.suh, self.svh, self.Ki, y2[m0:m0 + 8])
+            for m0 in range(0, M, GEMV_MAX_ROWS):
+                exl3_gemv(x2[m0:m0 + GEMV_MAX_ROWS], pk, self.suh, self.svh, self.Ki, y2[m0:m0 + GEMV_MAX_ROWS])
         else:
             suh = self.suh if self.suh is None or self.suh.data_ptr() % 8 == 0 else self.suh.clone()
             svh = self.svh if self.svh.data_ptr() % 8 == 0 else self.svh.clone()

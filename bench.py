@@ -575,6 +575,8 @@ def run_decode(ctx, args, wl, cfg, steps, warmup, primary: bool):
         roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
                 "traffic": TRAFFIC_PER_LAUNCH.get(wl), "kernel": "k_gemv<EPI_GATEUP> (gate|up GEMV)",
                 "peak_kind": peak_kind, "launch_ms": round(gu_ms, 5), "bytes_per_launch": gu_bytes // Ltot}
+        if wl in DECODE_ALU:
+            roof["decode_alu"] = DECODE_ALU[wl]
     weight_gbs = ctx.sum_over_ranks(float(w_bytes)) / (ms * 1e-3) / 1e9
 
     # e2e: the same step with host buffers (pinned), copies inside the timed region
@@ -822,6 +824,13 @@ RUNNERS = {"decode": run_decode, "prefill": run_prefill, "dense": run_dense}
 # DRAM bytes (read + write) per gate|up launch from the committed ncu capture
 # (profiles/k_gemv_moe_qwen_next_full.md), per workload; None where no capture was made.
 TRAFFIC_PER_LAUNCH: dict = {"qwen_next_decode": 31226624 + 86272}
+# The decode's own roofline for the same launch, from the same capture: the kernel is bound by the integer decode of
+# the trellis, not by HBM (warp instructions per 16x16 tile, issue and pipe utilisation, and the ceiling that the
+# IMUL + IDP4A pair per weight sets on the half-rate pipe at this K).
+DECODE_ALU: dict = {"qwen_next_decode": {
+    "warp_instructions_per_tile": 54.2, "issue_active": 0.596, "alu_pipe": 0.497,
+    "fma_pipe": 0.212, "smsp_active_of_elapsed": round(48650.6 / 65582.2, 3), "K": 3,
+    "hbm_frac_ceiling_of_mul1_pipe": 0.53}}
 
 
 def main():

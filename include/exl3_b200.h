@@ -96,8 +96,8 @@ EXL3_API int exl3_pack_gateup(const void* gate, const void* up, int H, int I, in
                               void* stream);
 
 /* ---- EXL3 linear, decode sizes ----
- * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for M <= 8 rows (larger M: call per 8-row chunk, or use the
- * reconstruct + GEMM path); x fp16 or bf16 (x_dtype), y fp16/bf16/fp32 (y_dtype) with row strides ldx, ldy.
+ * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for M <= 16 rows (9..16 rows: every decoded weight fragment feeds two
+ * MMAs, so the weights are decoded once per call; larger M: call per 16-row chunk, or use exl3_gemm_tc); x fp16 or bf16 (x_dtype), y fp16/bf16/fp32 (y_dtype) with row strides ldx, ldy.
  * packed = the weights in the packed layout (exl3_pack). k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2.
  * workspace >= exl3_gemv_workspace_size(M, k, n) bytes (rotated input rows, split-unit reduction state; calls that
  * share a workspace must be ordered on one stream). n_ctas = CTAs of the persistent launch (0 = one per SM).
@@ -274,7 +274,9 @@ EXL3_API int exl3_moe_align(const int32_t* ids, const float* w, int M, int topk,
  *   (the caller runs its local experts on the W * cap received rows: recv_x / recv_ids / recv_w at the offsets
  *    exl3_ep_recv_offsets gives, producing part fp32 [W][cap][H])
  *   exl3_ep_combine   every received row that had a pick here goes back to its rank; waits for every peer's rows;
- *   exl3_ep_reduce    out[i] = sum over the ranks row i picked, in rank order, of their partial rows (+ shared[i]).
+ *   exl3_ep_reduce    out[i] = sum over the ranks row i picked, in rank order, of their partial rows (+ shared[i]);
+ *   exl3_ep_combine_reduce  the two steps above in one launch (every CTA waits for the peers' rows, then sums its
+ *                     share of out): one kernel boundary less per layer, the same result bit for bit.
  * The calls count themselves on the device, so a captured sequence replays. exl3_ep_buffer_create allocates device
  * memory; no other entry point here does. */
 EXL3_API size_t exl3_ep_buffer_bytes(int W, int cap, int H, int topk);
@@ -288,6 +290,9 @@ EXL3_API int exl3_ep_dispatch(const void* x, int x_dtype, int ldx, int B, const 
                               void* stream);
 EXL3_API int exl3_ep_combine(const float* part, int topk, int E, int H, int W, int rank, int cap,
                              const uint64_t* peers, void* local, void* stream);
+EXL3_API int exl3_ep_combine_reduce(const float* part, const int32_t* ids, int B, int topk, int E, int H, int W,
+                                    int rank, int cap, const float* shared, const uint64_t* peers, void* local,
+                                    float* out, void* stream);
 EXL3_API int exl3_ep_reduce(const int32_t* ids, int B, int topk, int E, int H, int W, int rank, int cap,
                             const float* shared, void* local, float* out, void* stream);
 

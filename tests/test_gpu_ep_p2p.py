@@ -1,8 +1,8 @@
-"""Expert parallelism on two GPUs with the peer-memory exchange (exl3_ep_dispatch / combine / reduce): each rank's
-output equals moe_forward / moe_prefill on the full expert table for the same tokens; uneven batches under one
-capacity; the exchange captured in a CUDA graph and replayed; and a rank that skips a dispatch makes its peer's wait
-run out with EXL3_ERR_TIMEOUT instead of hanging (no GPU fault involved: the absent rank stays alive, its buffer
-mapped, until the waiting rank has finished). Child processes, one per GPU, NCCL for the plumbing with NVLS off.
+"""Expert parallelism on two GPUs with the peer-memory exchange (exl3_ep_dispatch / combine / reduce, and the fused
+combine + reduce, bit for bit): each rank's output equals moe_forward / moe_prefill on the full expert table for the
+same tokens; uneven batches under one capacity; the exchange captured in a CUDA graph and replayed; and a rank that
+skips a dispatch makes its peer's wait run out with EXL3_ERR_TIMEOUT instead of hanging (no GPU fault involved: the
+absent rank stays alive, its buffer mapped, until the waiting rank has finished). Child processes, one per GPU, NCCL for the plumbing with NVLS off.
 Skipped with fewer than two GPUs."""
 import os
 import socket
@@ -77,6 +77,10 @@ def _worker(rank, world, port, mode, q):
             ids, w, _ = ops.route(torch.randn((B, E), device=dev, generator=tg), L.ROUTE_SOFTMAX, topk)
             epm = ep.ExpertParallelMoE(E, H, topk, None, local_tab, 10.0, capacity=cap, exchange="p2p")
             got = epm.forward(x, ids, w)
+            epm.fused_reduce = False                                  # combine and reduce as two launches
+            got2 = epm.forward(x, ids, w)
+            epm.fused_reduce = True
+            res[f"fused_equal_B{B}"] = bool(torch.equal(got, got2))
             fn = moe.moe_prefill if B * topk >= ep.PREFILL_MIN_PAIRS else moe.moe_forward
             ref = fn(x, ids, w, full_tab, 10.0)
             torch.cuda.synchronize()
@@ -157,6 +161,9 @@ def test_p2p_expert_parallel_matches_full_table():
         assert v["status"] == 0
         for key, t in v.items():
             if key == "status":
+                continue
+            if key.startswith("fused_equal"):
+                assert t, (r, key)                                    # one launch or two: the same bits
                 continue
             rel, mx, rms = t
             assert rel <= 2e-3 and mx <= 1e-2 * max(1.0, rms), (r, key, rel, mx, rms)

@@ -106,7 +106,7 @@ def test_had_r_128_bitexact():
 
 
 @pytest.mark.parametrize("K", range(1, 9))
-@pytest.mark.parametrize("M", [1, 3, 8])
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16])
 def test_gemv_matches_oracle(K, M):
     rng = np.random.default_rng(1000 * K + M)
     k, n = 512, 384
@@ -119,12 +119,13 @@ def test_gemv_matches_oracle(K, M):
         assert_close(y.float().cpu().numpy(), ref.astype(np.float32), what=f"gemv K={K} M={M} {y_dt}")
 
 
+@pytest.mark.parametrize("M", [4, 13])
 @pytest.mark.parametrize("groups", [1, 2, 3, 7, 64, 0])
-def test_gemv_cta_counts_are_consistent(groups):
+def test_gemv_cta_counts_are_consistent(groups, M):
     """Any CTA count (1 = every unit whole in one CTA; many = units split over CTAs and reduced through the tickets)
-    gives the oracle's result, bit-identically from call to call."""
+    gives the oracle's result, bit-identically from call to call; also with two row groups (13 rows)."""
     rng = np.random.default_rng(77)
-    k, n, K, M = 1024, 256, 3, 4
+    k, n, K = 1024, 256, 3
     tr, suh, svh = rand_linear(rng, k, n, K)
     x = rng.standard_normal((M, k)).astype(np.float16)
     y = torch.full((M, n), float("nan"), dtype=torch.float32, device=DEV)
@@ -158,7 +159,7 @@ def test_linear_golden(K):
     assert rel < 5e-3          # glm/xpu/tests/units.py:104
 
 
-@pytest.mark.parametrize("M", [1, 5, 20, 100])
+@pytest.mark.parametrize("M", [1, 5, 12, 20, 32, 100])
 def test_bc_linear_paths(M):
     rng = np.random.default_rng(M)
     k, n, K = 256, 640, 4
