@@ -13,9 +13,9 @@
 // a 10-stage shared-memory ring to 20 consumer warps: five sub-groups of four warps take the stages in turn, the four
 // warps of a sub-group covering all tiles of each tile-row; the shared ring keeps the sub-groups within a few
 // stages of each other. At the end of each segment the consumers park their accumulators in one of two shared-memory
-// slots and go on decoding; four epilogue warps sum them, reduce split units and run the epilogue. A CTA that covers a whole unit
-// finishes it on the spot; units shared by several CTAs are reduced through global memory: each contributor stores
-// its fp32 partial, and the contributor whose atomic ticket completes the count sums all partials in CTA order (a
+// slots and go on decoding; two epilogue warps sum them, reduce split units and run the epilogue. A CTA that covers a
+// whole unit finishes it on the spot; units shared by several CTAs are reduced through global memory: each
+// contributor stores its fp32 partial, and the contributor whose atomic ticket completes the count sums all partials in CTA order (a
 // fixed order: results do not depend on timing) and runs the epilogue. No CTA ever waits for another, and every SM
 // has work until the last k-block, whatever the number of units.
 //
@@ -27,11 +27,12 @@
 // state times 0x83DCD12D, byte sum + 0x6400 by dp4a = the fp16 bits of h = 1024 + bytesum (exact), packed two per
 // register straight into the MMA A fragment (the EXL3 position order is that fragment's layout: lane 4g+q owns
 // positions 8l..8l+7, so no shuffles). One m16n8k16 MMA per 16x16 tile accumulates D = sum_k h_k a_k in fp32; batch
-// rows ride in the MMA's 8 columns, so rows 1..8 cost the same decode. The codebook's affine w = h c1 + c2 (fp16
-// constants 0x1EEE / 0xC931) is applied once per output in the epilogue, D' = c1 D + c2 S with S = sum_k a_k from the
-// per-128-block activation sums the rotation kernels write: the product is the one of the unrounded affine
-// (|w' - w| <= half an fp16 ulp of the reference's fp16 weight), one fp16 FMA per weight pair less than applying it to
-// every weight. exl3_dequant keeps the rounded fp16 weights, bit for bit.
+// rows ride in the MMA's 8 columns, so rows 1..8 cost the same decode (the linear's 9..16-row calls issue a second
+// MMA per decoded fragment for rows 9..16). The codebook's affine w = h c1 + c2 (fp16 constants 0x1EEE / 0xC931) is
+// applied once per output in the epilogue, D' = c1 D + c2 S with S = sum_k a_k from the per-128-block activation sums
+// the rotation kernels write: the product is the one of the unrounded affine (|w' - w| <= half an fp16 ulp of the
+// reference's fp16 weight), one fp16 FMA per weight pair less than applying it to every weight. exl3_dequant keeps
+// the rounded fp16 weights, bit for bit.
 //
 // Epilogues: the output Hadamard x svh (linear), the gated-MLP activation + the down projection's input rotation
 // (MoE gate|up), or Hadamard x svh x routing weight (MoE down).
@@ -447,9 +448,8 @@ __device__ __forceinline__ void unit_epilogue(const GemvArgs& a, const UnitInfo<
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) {
             // the codebook affine on the product: c1 * sum h a + c2 * sum a (S: the row's activation sum)
-            const float c2s = ri == 0 ? op.c2s0[m]
-                                      : kMul1C2 * xsum_total(a.xsum + ((size_t)xrow_of(ui, row) * NMAT + m) * (a.k / 128),
-                                                             a.k / 128, lane);
+            const float* xs = a.xsum + ((size_t)xrow_of(ui, row) * NMAT + m) * (a.k / 128);
+            const float c2s = ri == 0 ? op.c2s0[m] : kMul1C2 * xsum_total(xs, a.k / 128, lane);
             const float4 t = *reinterpret_cast<const float4*>(red + ((size_t)m * R + row) * 128 + 4 * lane);
             v[m][0] = fmaf(kMul1C1, t.x, c2s);
             v[m][1] = fmaf(kMul1C1, t.y, c2s);

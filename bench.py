@@ -46,7 +46,7 @@ for _p in (ROOT, os.path.join(ROOT, "b70-inference_b200")):
 WORKLOADS = {
     # BASELINE config 4
     "qwen_next_decode": dict(kind="decode", H=2048, E=512, I=512, topk=10, Ks=(3,), layers=48, router="softmax",
-                             batch=4, act_limit=0.0, shared_K=0, res_frac=0.0, scale=1.0),
+                             batch=4, act_limit=0.0, shared_K=0, res_frac=0.0, scale=1.0, batch_sweep=(1, 2)),
     # BASELINE config 3 (one GLM-like layer shape, 8 layers per step so that a step's weights exceed L2)
     "glm_decode": dict(kind="decode", H=6144, E=160, I=1536, topk=8, Ks=(2, 3), layers=8, router="sigmoid", batch=1,
                        act_limit=10.0, shared_K=4, res_frac=0.25, scale=2.5),
@@ -617,7 +617,48 @@ def run_decode(ctx, args, wl, cfg, steps, warmup, primary: bool):
                                      "down, combine), exchange combine and reduce, and the shared expert's four "
                                      "when the workload has one; torch fill kernels are not counted")
     del graph, graph_ev
+    if world == 1 and cfg.get("batch_sweep"):
+        line["batch_sweep"] = decode_batch_sweep(cfg, steps, warmup, x, logits, out, tables, kind, bias, res, line)
     return line
+
+
+def decode_batch_sweep(cfg, steps, warmup, x, logits, out, tables, kind, bias, res, line):
+    """The config's other decode batches (1 GPU): the first b tokens of the same step through the same layers,
+    captured and timed the same way (CUDA events over `steps` replays after `warmup`)."""
+    import torch
+    from exl3_b200 import moe, ops
+    Ltot, topk = cfg["layers"], cfg["topk"]
+    sweep = {str(cfg["batch"]): {"tok_s": line["value"], "ms_per_step": line["ms_per_step"]}}
+    for b in cfg["batch_sweep"]:
+        def step():
+            for l in range(Ltot):
+                ids, w, _ = ops.route(logits[l, :b], kind, topk, bias=None if bias is None else bias[l],
+                                      res=None if res is None else res[l], scale=cfg["scale"], renorm=True)
+                moe.moe_forward(x[l, :b], ids, w, tables[l], cfg["act_limit"], torch.float32, out=out[l, :b])
+        step()
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            step()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step()
+        for _ in range(warmup):
+            g.replay()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        t0.record()
+        for _ in range(steps):
+            g.replay()
+        t1.record()
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / steps
+        sweep[str(b)] = {"tok_s": round(b / (ms * 1e-3), 2), "ms_per_step": round(ms, 5)}
+        del g
+    return sweep
 
 
 # ------------------------------------------------------------------------------------------------ prefill

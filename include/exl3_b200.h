@@ -97,7 +97,8 @@ EXL3_API int exl3_pack_gateup(const void* gate, const void* up, int H, int I, in
 
 /* ---- EXL3 linear, decode sizes ----
  * y[M][n] = Had(Had(x * suh) @ W_hat) * svh for M <= 16 rows (9..16 rows: every decoded weight fragment feeds two
- * MMAs, so the weights are decoded once per call; larger M: call per 16-row chunk, or use exl3_gemm_tc); x fp16 or bf16 (x_dtype), y fp16/bf16/fp32 (y_dtype) with row strides ldx, ldy.
+ * MMAs, so the weights are decoded once per call; larger M: call per 16-row chunk, or use exl3_gemm_tc); x fp16 or
+ * bf16 (x_dtype), y fp16/bf16/fp32 (y_dtype) with row strides ldx, ldy.
  * packed = the weights in the packed layout (exl3_pack). k % 128 == 0, n % 128 == 0, 1 <= K <= 8, cb == 2.
  * workspace >= exl3_gemv_workspace_size(M, k, n) bytes (rotated input rows, split-unit reduction state; calls that
  * share a workspace must be ordered on one stream). n_ctas = CTAs of the persistent launch (0 = one per SM).
@@ -126,10 +127,10 @@ EXL3_API int exl3_gemm_tc(const void* x, int x_dtype, int ldx, int M, const void
 
 /* No-allocation variant of exl3_gemv: same arguments minus the workspace and n_ctas; its scratch is a fixed
  * file-scope device array (1,845,248 bytes per device that loads the library: the rotated input rows and their
- * block sums, the split tickets and the partial slots, sized from the limits below), for callers that cannot allocate device memory.
- * Limits: M <= 8, k <= 32768, n <= 65536 (larger shapes return EXL3_ERR_UNSUPPORTED). Calls on one device that may
- * overlap race on the shared scratch: order them on one stream. Make the first call on each device outside stream
- * capture (it looks up the scratch's address). No reference counterpart. */
+ * block sums, the split tickets and the partial slots, sized from the limits below), for callers that cannot
+ * allocate device memory. Limits: M <= 8, k <= 32768, n <= 65536 (larger shapes return EXL3_ERR_UNSUPPORTED).
+ * Calls on one device that may overlap race on the shared scratch: order them on one stream. Make the first call on
+ * each device outside stream capture (it looks up the scratch's address). No reference counterpart. */
 EXL3_API int exl3_gemv_noalloc(const void* x, int x_dtype, int ldx, int M, const void* packed, const void* suh,
                                const void* svh, int k, int n, int K, int cb, void* y, int y_dtype, int ldy,
                                void* stream);
