@@ -14,10 +14,12 @@
 // warps of a sub-group covering all tiles of each tile-row; the shared ring keeps the sub-groups within a few
 // stages of each other. At the end of each segment the consumers park their accumulators in one of two shared-memory
 // slots and go on decoding; two epilogue warps sum them, reduce split units and run the epilogue. A CTA that covers a
-// whole unit finishes it on the spot; units shared by several CTAs are reduced through global memory: each
-// contributor stores its fp32 partial, and the contributor whose atomic ticket completes the count sums all partials in CTA order (a
-// fixed order: results do not depend on timing) and runs the epilogue. No CTA ever waits for another, and every SM
-// has work until the last k-block, whatever the number of units.
+// whole unit finishes it on the spot; units shared by several CTAs are reduced through global memory: the other
+// contributors store their fp32 partials and count themselves, and the unit's first contributor, for which the unit
+// is the last segment of its range, sums all partials in CTA order (a fixed order: results do not depend on timing)
+// and runs the epilogue. Its bounded wait for the count almost never waits: the others have the unit as the first
+// segment of their ranges. Units split over more than 4 CTAs go through an atomic ticket instead (the contributor
+// that completes the count finishes). Every SM has work until the last k-block, whatever the number of units.
 //
 // Activations arrive pre-rotated in "xf" order (prep kernels, or the gate|up epilogue for the down projection):
 // a = fp16(H(fp16(x*suh))/sqrt(128)) (exllamav3's roundings), stored per (row, 16-input tile-row) as 4 quads x 4 fp16
@@ -145,6 +147,13 @@ __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.lau
 
 __device__ __forceinline__ void prefetch_l1(const void* p) {
     asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+// Acquire load at GPU scope (a ticket written by other CTAs with a fence before their atomic).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 // Named barrier over the epilogue warps (id 1; 0 is __syncthreads, used once before the roles split).
@@ -659,6 +668,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
     }
 
     // ---------------- epilogue warps: sum the sub-groups, reduce split units, finish units ----------------
+    // A unit split over n_c <= 4 CTAs is finished by its first contributor (the owner of its first k-block, for which
+    // the unit is the last segment of its range): the others store their partials and count themselves (a fence and
+    // an atomic add whose result nobody waits for), usually long before, since the unit is the first segment of their
+    // ranges; the finisher loads their partials into red[buf ^ 1] (no later segment of this CTA uses it) while its
+    // own consumers are still decoding, or, if they are not all in yet, waits for the count (bounded) once its own
+    // part is done. That wait is on CTAs that never wait themselves for this unit, all resident (one CTA per SM).
+    // Units split over more than 4 CTAs use a ticket instead: every contributor stores its partial and the one whose
+    // atomic completes the count finishes. Either way the partials are summed in CTA order, so the result does not
+    // depend on timing or on the path.
     const int ew = warp - 1 - kConsumerWarps;
     const int et = ew * 32 + lane;
     pdl_wait();                                               // tickets and outputs belong to this launch from here
@@ -670,11 +688,39 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
         const UnitInfo<EPI> ui = i < kMaxSeg ? descs[i] : unit_info<EPI>(args, (int)u, NB, KB);
         const EpiOperands<EPI> op = epi_operands<EPI>(args, ui, ew, lane);
         const int buf = i & 1;
+        const bool whole = lo == 0 && hi == KB;
+        const long long a0 = u * KB, a1 = a0 + KB;            // the unit's k-blocks [a0, a1)
+        int n_c = 1;                                          // contributors (up to 4 counted, more = ticket path)
+        bool more = false;
+        if (!whole) {
+            n_c = 0;
+            for (long long c = owner_of(a0, T, G);; c = next_owner(c, T, G)) {
+                ++n_c;
+                if (range_start(c + 1, T, G) >= a1) break;
+                if (n_c == 4) { more = true; break; }
+            }
+        }
+        const bool head = !whole && !more && owner_of(a0, T, G) == ci;   // this CTA finishes the unit
+        float* pf = red + (size_t)(buf ^ 1) * kSub * UF;
+        bool ready = false;
+        if (head) {
+            if (et == 0) flag[1] = ld_acquire_gpu(args.counters + u) == n_c - 1;
+            epilogue_sync();
+            ready = flag[1] != 0;
+            if (ready) {                                      // the others' partials, while the consumers finish
+                long long c = next_owner(ci, T, G);
+                for (int j = 1; j < n_c; ++j, c = next_owner(c, T, G)) {
+                    const float4* src = reinterpret_cast<const float4*>(args.partial + (size_t)(2 * c) * UF);
+                    for (int e = et; e < UF / 4; e += kEpilogueWarps * 32)
+                        if ((e / 32) % R < ui.Mi) reinterpret_cast<float4*>(pf + (size_t)j * UF)[e] = __ldcg(src + e);
+                }
+            }
+        }
         if (!to && !mbar_wait(&acc_full[buf], (i >> 1) & 1)) to = true;
         float* rb = red + (size_t)buf * kSub * UF;
-        const bool whole = lo == 0 && hi == KB;
         float4* slot = reinterpret_cast<float4*>(args.partial + (size_t)(i == 0 ? 2 * ci : 2 * ci + 1) * UF);
-        // sub-group sums in sub-group order: into rb[0] (whole unit) or this CTA's partial slot
+        // sub-group sums in sub-group order: into rb[0] (whole unit, or the finisher's own part), with the others'
+        // partials in CTA order when they are already loaded, or into this CTA's partial slot
         for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
             if ((e / 32) % R >= ui.Mi) continue;              // rows beyond the unit's
             float4 acc = reinterpret_cast<const float4*>(rb)[e];
@@ -683,15 +729,63 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
                 const float4 v = reinterpret_cast<const float4*>(rb + (size_t)j * UF)[e];
                 acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
             }
-            if (whole) reinterpret_cast<float4*>(rb)[e] = acc;
-            else slot[e] = acc;
+            if (ready) {
+                float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (j == 0) p = acc;
+                    else if (j < n_c) p = reinterpret_cast<const float4*>(pf + (size_t)j * UF)[e];
+                    t.x += p.x; t.y += p.y; t.z += p.z; t.w += p.w;
+                }
+                reinterpret_cast<float4*>(rb)[e] = t;
+            } else if (whole || head) {
+                reinterpret_cast<float4*>(rb)[e] = acc;
+            } else {
+                slot[e] = acc;
+            }
         }
-        bool finish = whole;
-        if (!whole) {
+        bool finish = whole || head;
+        if (head && !ready) {
+            // the others are not all in yet: wait for the count (bounded), then add their partials in CTA order
+            if (et == 0) {
+                const uint64_t t0 = globaltimer_ns();
+                while (ld_acquire_gpu(args.counters + u) != n_c - 1) {
+                    if (globaltimer_ns() - t0 > kWaitLimitNs) { to = true; break; }
+                    __nanosleep(64);
+                }
+            }
+            epilogue_sync();
+            for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
+                if ((e / 32) % R >= ui.Mi) continue;
+                float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+                long long c = ci;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
+                    if (j == 0) p = reinterpret_cast<const float4*>(rb)[e];
+                    else if (j < n_c) {
+                        c = next_owner(c, T, G);
+                        p = __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)(2 * c) * UF) + e);
+                    }
+                    t.x += p.x; t.y += p.y; t.z += p.z; t.w += p.w;
+                }
+                reinterpret_cast<float4*>(rb)[e] = t;
+            }
+        }
+        if (head && et == 0) args.counters[u] = 0;           // every other contributor has counted: left zero
+        if (!whole && !more && !head) {
+            // publish this CTA's partial: the slot stores of both warps, then one fence and the count
+            epilogue_sync();
+            if (et == 0) {
+                __threadfence();
+                atomicAdd(args.counters + u, 1);
+            }
+        }
+        if (more) {
             // ticket: the last contributor of unit u sums every partial in CTA order
             __threadfence();
             epilogue_sync();
-            const long long a0 = u * KB, a1 = a0 + KB;        // the unit's k-blocks [a0, a1)
             if (et == 0) {
                 int nseg = 1;
                 for (long long c = owner_of(a0, T, G); range_start(c + 1, T, G) < a1; c = next_owner(c, T, G)) ++nseg;
@@ -709,9 +803,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
                 // contributors in order: the owner of a0, then the owner after each range, up to the unit's end; a
                 // contributor that started before a0 keeps this unit's partial in its second slot
                 int slots[4];                                 // partial slots of the first contributors, in order
-                int n_c = 0;
-                for (long long c = owner_of(a0, T, G); n_c < 4; c = next_owner(c, T, G)) {
-                    slots[n_c++] = (int)(range_start(c, T, G) < a0 ? 2 * c + 1 : 2 * c);
+                int nc = 0;
+                for (long long c = owner_of(a0, T, G); nc < 4; c = next_owner(c, T, G)) {
+                    slots[nc++] = (int)(range_start(c, T, G) < a0 ? 2 * c + 1 : 2 * c);
                     if (range_start(c + 1, T, G) >= a1) break;
                 }
                 for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
@@ -719,12 +813,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
                     float4 p[4];
 #pragma unroll
                     for (int j = 0; j < 4; ++j)
-                        p[j] = j < n_c ? __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)slots[j] * UF) + e)
-                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+                        p[j] = j < nc ? __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)slots[j] * UF) + e)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) { acc.x += p[j].x; acc.y += p[j].y; acc.z += p[j].z; acc.w += p[j].w; }
-                    if (n_c == 4) {                           // units split over more than 4 CTAs: the rest in order
+                    if (nc == 4) {                            // units split over more than 4 CTAs: the rest in order
                         long long c = owner_of(a0, T, G);
                         for (int j = 0; j < 4; ++j) c = next_owner(c, T, G);
                         for (;; c = next_owner(c, T, G)) {
@@ -742,7 +836,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
             epilogue_sync();
             unit_epilogue<EPI, RG>(args, ui, rb, ew, lane, op);
         }
-        epilogue_sync();                                      // the flag and red[buf] are read: release them
+        epilogue_sync();                                      // the flags and red[buf] are read: release them
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
     if (to) report(args.status, EXL3_ERR_TIMEOUT);
