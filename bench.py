@@ -578,6 +578,12 @@ def run_decode(ctx, args, wl, cfg, steps, warmup, primary: bool):
         if wl in DECODE_ALU:
             roof["decode_alu"] = DECODE_ALU[wl]
     weight_gbs = ctx.sum_over_ranks(float(w_bytes)) / (ms * 1e-3) / 1e9
+    if roof is None:
+        # N > 1: the per-GPU compressed weight bytes of a step over the step time (the exchange included)
+        ach = weight_gbs / world
+        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm, "unit": "GB/s", "frac": round(ach / hbm, 4),
+                "traffic": None, "kernel": "whole step per GPU (expert weights read / step time)",
+                "peak_kind": peak_kind}
 
     # e2e: the same step with host buffers (pinned), copies inside the timed region
     xh = x.cpu().pin_memory()
