@@ -5,23 +5,27 @@
 // Every rank holds one exchange buffer (exl3_ep_buffer_create: cudaMalloc'd, exported with a CUDA IPC handle) and maps
 // its peers' buffers (exl3_ep_buffer_open). Layout of a buffer (W ranks, cap rows per rank and call, H hidden, k
 // picks per row), identical on every rank:
-//   control (2 KB): dispatch_flag[64], combine_flag[64] (written by the peers: the epoch of their last signal),
-//                   dispatch_epoch, combine_epoch (this rank's call counters), per-peer CTA tickets, CTA totals
+//   control (8 KB): dispatch and combine flags [W][chunks] (slot [r][c] written by rank r's CTA for chunk c: the
+//                   epoch of its last signal) and this rank's per-CTA call counters
 //   recv_x   fp16 [W][cap][H]    row i of source rank r at [r][i]: written by rank r
 //   recv_ids int32 [W][cap][k]   rank r's picks for row i rebased to this rank's experts (-1: another rank's)
 //   recv_w   fp32 [W][cap][k]
 //   back     fp32 [W][cap][H]    this rank's row i as computed by rank p's experts, at [p][i]: written by rank p
-// dispatch: rank r writes each of its rows, with the picks rebased to peer p's expert range, into recv[r] of every
-//   peer p (a row's activations only when it has a pick there; rows past the batch carry no picks), then signals
-//   p's dispatch_flag[r] with a system-scope release store; the launch ends when every peer's signal for this call
-//   has arrived (a bounded wait: 100 ms, then EXL3_ERR_TIMEOUT in the status word).
+// Rows are cut into `chunks` contiguous chunks (the same on every rank); CTA (c, p) of a launch handles chunk c for
+// peer p. No CTA waits for another CTA of its own launch and no atomics are involved:
+// dispatch: CTA (c, p) of rank r writes chunk c of r's rows, with the picks rebased to p's expert range (a row's
+//   activations only when it has a pick there; rows past the batch carry no picks), into recv[r] of peer p, fences
+//   at system scope and stores the call's epoch into p's dispatch flag [r][c]; then it waits for its own flag [p][c]
+//   (peer p's chunk c for this rank). The launch ends when every chunk of every peer has arrived (bounded waits:
+//   100 ms, then EXL3_ERR_TIMEOUT in the status word).
 // local experts: the grouped MoE kernels run on recv as one batch of W * cap rows.
-// combine: rank p writes, for every source rank r, the partial rows of r's rows that had a pick on p into r's
-//   back[p], signals combine_flag[p], and waits for every peer's signal likewise.
-// reduce: out[i] = sum over p in rank order of back[p][i] for the ranks p that row i picked (+ the shared expert's
+// combine: CTA (c, r) of rank p writes the partial rows of chunk c received from r that had a pick on p into r's
+//   back[p], fences, signals r's combine flag [p][c], and waits for the flags [q][c] of every rank q: this rank's
+//   chunk-c rows are then complete; with the reduce fused, the W CTAs of chunk c then sum its rows:
+// reduce: out[i] = sum over q in rank order of back[q][i] for the ranks q that row i picked (+ the shared expert's
 //   row): a fixed order, so the result is bit-reproducible for a given world size.
-// Calls are counted on the device (epochs), so the sequence is graph-capturable; every rank must make the same calls
-// in the same order. The buffers are single-buffered: a rank's next dispatch can only start after its combine, which
+// Every CTA counts its own calls (epochs), so the sequence is graph-capturable; every rank must make the same calls in
+// the same order. The buffers are single-buffered: a rank's next dispatch can only start after its combine, which
 // needs every peer's combine of the previous call, which follows that peer's use of its receive region.
 #include "gemv.cuh"
 
@@ -29,23 +33,23 @@ namespace exl3 {
 
 constexpr int kEpMaxRanks = 64;
 constexpr int kEpThreads = 256;
+constexpr int kEpMaxSlots = 512;    // W * chunks
 
 struct EpCtl {
-    uint32_t dispatch_flag[kEpMaxRanks];
-    uint32_t combine_flag[kEpMaxRanks];
-    uint32_t dispatch_epoch, combine_epoch, pad0[14];
-    uint32_t d_sent[kEpMaxRanks];     // CTAs of this launch done with peer p (dispatch)
-    uint32_t c_sent[kEpMaxRanks];
-    uint32_t d_total, c_total, pad1[14];
+    uint32_t dflag[kEpMaxSlots];      // [source rank][chunk]: written by the peers
+    uint32_t cflag[kEpMaxSlots];
+    uint32_t d_epoch[kEpMaxSlots];    // [peer][chunk]: this rank's CTA calls
+    uint32_t c_epoch[kEpMaxSlots];
 };
-static_assert(sizeof(EpCtl) <= 2048, "control block");
+constexpr size_t kEpCtlBytes = 8192;
+static_assert(sizeof(EpCtl) <= kEpCtlBytes, "control block");
 
 struct EpLayout {
     size_t recv_x, recv_ids, recv_w, back, total;
 };
 inline EpLayout ep_layout(int W, int cap, int H, int k) {
     EpLayout L;
-    size_t o = 2048;
+    size_t o = kEpCtlBytes;
     L.recv_x = o; o += align_up((size_t)W * cap * H * 2, 256);
     L.recv_ids = o; o += align_up((size_t)W * cap * k * 4, 256);
     L.recv_w = o; o += align_up((size_t)W * cap * k * 4, 256);
@@ -63,13 +67,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     return v;
 }
 
-// Wait (one thread) until flags[0..W) all equal `epoch`; bounded by kWaitLimitNs of global time.
-__device__ bool ep_wait_flags(const uint32_t* flags, int W, uint32_t epoch) {
+// Wait (one thread) until flags[0], flags[stride], ..., flags[(n - 1) stride] all equal `epoch`; bounded by
+// kWaitLimitNs of global time.
+__device__ bool ep_wait_flags(const uint32_t* flags, int n, int stride, uint32_t epoch) {
     const uint64_t t0 = globaltimer_ns();
-    for (int p = 0; p < W; ++p) {
-        while (ld_acquire_sys(flags + p) != epoch) {
+    for (int p = 0; p < n; ++p) {
+        while (ld_acquire_sys(flags + (size_t)p * stride) != epoch) {
             if (globaltimer_ns() - t0 > kWaitLimitNs) return false;
-            __nanosleep(64);
+            __nanosleep(32);
         }
     }
     return true;
@@ -97,15 +102,14 @@ __device__ __forceinline__ bool row_picks_rank(const int32_t* ids, int i, int k,
     return false;
 }
 
-// grid (chunks, W): CTA (c, p) sends rows [c * rpc, ...) of this rank to peer p.
+// grid (chunks, W): CTA (c, p) sends rows [c * rpc, ...) of this rank to peer p and waits for peer p's chunk c.
 __global__ void __launch_bounds__(kEpThreads) k_ep_dispatch(const EpArgs a) {
     pdl_wait();                                                 // ids and rows come from earlier kernels
     pdl_trigger();
     EpCtl* ctl = reinterpret_cast<EpCtl*>(a.local);
-    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&ctl->dispatch_epoch) + 1;
-    const int p = blockIdx.y, per = a.E / a.W;
-    const int rpc = (a.cap + gridDim.x - 1) / gridDim.x;
-    const int i0 = blockIdx.x * rpc, i1 = min(a.cap, i0 + rpc);
+    const int c = blockIdx.x, p = blockIdx.y, nch = gridDim.x, per = a.E / a.W;
+    const int rpc = (a.cap + nch - 1) / nch;
+    const int i0 = c * rpc, i1 = min(a.cap, i0 + rpc);
     uint8_t* peer = reinterpret_cast<uint8_t*>(a.peers[p]);
     const size_t slot = (size_t)a.rank * a.cap;                // rows of this rank in the peer's recv arrays
     int32_t* rid = reinterpret_cast<int32_t*>(peer + a.L.recv_ids) + slot * a.k;
@@ -128,31 +132,25 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_dispatch(const EpArgs a) {
     }
     __syncthreads();                                            // the CTA's peer stores, then one thread fences
     if (threadIdx.x != 0) return;                               // them at system scope and signals
+    const int my = p * nch + c;                                 // this CTA's counter; also its incoming flag slot
+    const uint32_t epoch = ctl->d_epoch[my] + 1;
     asm volatile("fence.acq_rel.sys;" ::: "memory");
-    if (atomicAdd(&ctl->d_sent[p], 1u) == gridDim.x - 1) {     // the last CTA for peer p signals it
-        ctl->d_sent[p] = 0;
-        __threadfence_system();
-        EpCtl* pc = reinterpret_cast<EpCtl*>(peer);
-        st_release_sys(&pc->dispatch_flag[a.rank], epoch);
-    }
-    __threadfence();
-    if (atomicAdd(&ctl->d_total, 1u) == gridDim.x * gridDim.y - 1) {   // the last CTA waits for every peer
-        ctl->d_total = 0;
-        if (!ep_wait_flags(ctl->dispatch_flag, a.W, epoch)) report(a.status, EXL3_ERR_TIMEOUT);
-        ctl->dispatch_epoch = epoch;
-        __threadfence();
-    }
+    st_release_sys(&reinterpret_cast<EpCtl*>(peer)->dflag[a.rank * nch + c], epoch);
+    if (!ep_wait_flags(&ctl->dflag[my], 1, 0, epoch)) report(a.status, EXL3_ERR_TIMEOUT);
+    ctl->d_epoch[my] = epoch;
 }
 
-// grid (chunks, W): CTA (c, r) returns the rows [c * rpc, ...) received from rank r that had a pick here.
-__global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpArgs a) {
+// grid (chunks, W): CTA (c, r) returns the rows of chunk c received from rank r that had a pick here, signals r, and
+// waits for every rank's chunk c of this rank's rows; with `out`, the W CTAs of chunk c then sum its rows (a
+// fixed rank order) into out (+ shared), as k_ep_reduce does.
+__global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpArgs a, const float* shared, float* out) {
     pdl_wait();
     pdl_trigger();
+    __shared__ int ok;
     EpCtl* ctl = reinterpret_cast<EpCtl*>(a.local);
-    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&ctl->combine_epoch) + 1;
-    const int r = blockIdx.y;
-    const int rpc = (a.cap + gridDim.x - 1) / gridDim.x;
-    const int i0 = blockIdx.x * rpc, i1 = min(a.cap, i0 + rpc);
+    const int c = blockIdx.x, r = blockIdx.y, nch = gridDim.x;
+    const int rpc = (a.cap + nch - 1) / nch;
+    const int i0 = c * rpc, i1 = min(a.cap, i0 + rpc);
     uint8_t* peer = reinterpret_cast<uint8_t*>(a.peers[r]);
     const int32_t* myids = reinterpret_cast<const int32_t*>(a.local + a.L.recv_ids) + (size_t)r * a.cap * a.k;
     float4* dst = reinterpret_cast<float4*>(peer + a.L.back) + ((size_t)a.rank * a.cap) * (a.H / 4);
@@ -165,20 +163,37 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_combine(const EpArgs a) {
         for (int v = threadIdx.x; v < vec; v += blockDim.x) dst[(size_t)i * vec + v] = src[(size_t)i * vec + v];
     }
     __syncthreads();
-    if (threadIdx.x != 0) return;
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    if (atomicAdd(&ctl->c_sent[r], 1u) == gridDim.x - 1) {
-        ctl->c_sent[r] = 0;
-        __threadfence_system();
-        EpCtl* pc = reinterpret_cast<EpCtl*>(peer);
-        st_release_sys(&pc->combine_flag[a.rank], epoch);
+    if (threadIdx.x == 0) {
+        const int my = r * nch + c;
+        const uint32_t epoch = ctl->c_epoch[my] + 1;
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        st_release_sys(&reinterpret_cast<EpCtl*>(peer)->cflag[a.rank * nch + c], epoch);
+        // every rank's partial rows of this rank's chunk c: flags [q][c], q = 0..W-1
+        ok = ep_wait_flags(&ctl->cflag[c], a.W, nch, epoch);   // acquire loads: their rows are visible after
+        if (!ok) report(a.status, EXL3_ERR_TIMEOUT);
+        ctl->c_epoch[my] = epoch;
     }
-    __threadfence();
-    if (atomicAdd(&ctl->c_total, 1u) == gridDim.x * gridDim.y - 1) {
-        ctl->c_total = 0;
-        if (!ep_wait_flags(ctl->combine_flag, a.W, epoch)) report(a.status, EXL3_ERR_TIMEOUT);
-        ctl->combine_epoch = epoch;
-        __threadfence();
+    if (out == nullptr) return;
+    __syncthreads();
+    if (!ok) return;
+    // this rank's rows of chunk c (below B), shared by the W CTAs of the chunk
+    const int per = a.E / a.W;
+    const int b1 = min(a.B, i1);
+    const long total = (long)max(0, b1 - i0) * vec;
+    const float4* back = reinterpret_cast<const float4*>(a.local + a.L.back);
+    for (long t = (long)r * blockDim.x + threadIdx.x; t < total; t += (long)a.W * blockDim.x) {
+        const int i = i0 + (int)(t / vec), v = (int)(t % vec);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int q = 0; q < a.W; ++q) {
+            if (!row_picks_rank(a.ids, i, a.k, q, per)) continue;
+            const float4 b = back[((size_t)q * a.cap + i) * vec + v];
+            acc.x += b.x; acc.y += b.y; acc.z += b.z; acc.w += b.w;
+        }
+        if (shared) {
+            const float4 sh = reinterpret_cast<const float4*>(shared)[(size_t)i * vec + v];
+            acc.x += sh.x; acc.y += sh.y; acc.z += sh.z; acc.w += sh.w;
+        }
+        reinterpret_cast<float4*>(out)[(size_t)i * vec + v] = acc;
     }
 }
 
@@ -205,74 +220,6 @@ __global__ void __launch_bounds__(kEpThreads) k_ep_reduce(const EpArgs a, const 
     }
 }
 
-// The combine and the reduce in one launch: CTA (c, r) returns its rows received from rank r as k_ep_combine does;
-// then every CTA waits (thread 0, bounded) for every peer's combine signal of this call and sums its share of this
-// rank's output rows as k_ep_reduce does. The epoch advances only after every CTA has finished its wait (a second
-// ticket), so no CTA of this launch can read an advanced epoch. All CTAs of the grid are resident together (at most
-// 2 per SM, no shared memory), and no CTA waits on another CTA of its own grid, only on the peers' signals.
-__global__ void __launch_bounds__(kEpThreads) k_ep_combine_reduce(const EpArgs a, const float* shared, float* out) {
-    pdl_wait();
-    pdl_trigger();
-    __shared__ int ok;
-    EpCtl* ctl = reinterpret_cast<EpCtl*>(a.local);
-    const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(&ctl->combine_epoch) + 1;
-    const int r = blockIdx.y;
-    const int rpc = (a.cap + gridDim.x - 1) / gridDim.x;
-    const int i0 = blockIdx.x * rpc, i1 = min(a.cap, i0 + rpc);
-    uint8_t* peer = reinterpret_cast<uint8_t*>(a.peers[r]);
-    const int32_t* myids = reinterpret_cast<const int32_t*>(a.local + a.L.recv_ids) + (size_t)r * a.cap * a.k;
-    float4* dst = reinterpret_cast<float4*>(peer + a.L.back) + ((size_t)a.rank * a.cap) * (a.H / 4);
-    const float4* src = reinterpret_cast<const float4*>(a.part) + ((size_t)r * a.cap) * (a.H / 4);
-    const int vec = a.H / 4;
-    for (int i = i0; i < i1; ++i) {
-        bool any = false;
-        for (int j = 0; j < a.k; ++j) any |= myids[(size_t)i * a.k + j] >= 0;
-        if (!any) continue;                                    // block-uniform
-        for (int v = threadIdx.x; v < vec; v += blockDim.x) dst[(size_t)i * vec + v] = src[(size_t)i * vec + v];
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        if (atomicAdd(&ctl->c_sent[r], 1u) == gridDim.x - 1) {
-            ctl->c_sent[r] = 0;
-            __threadfence_system();
-            EpCtl* pc = reinterpret_cast<EpCtl*>(peer);
-            st_release_sys(&pc->combine_flag[a.rank], epoch);
-        }
-        ok = ep_wait_flags(ctl->combine_flag, a.W, epoch);     // acquire loads: the peers' rows are visible after
-        if (!ok) report(a.status, EXL3_ERR_TIMEOUT);
-    }
-    __syncthreads();
-    if (ok) {
-        const int per = a.E / a.W;
-        const long total = (long)a.B * vec;
-        const long nthr = (long)gridDim.x * gridDim.y * blockDim.x;
-        const float4* back = reinterpret_cast<const float4*>(a.local + a.L.back);
-        for (long t = ((long)blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + threadIdx.x; t < total; t += nthr) {
-            const int i = (int)(t / vec), v = (int)(t % vec);
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int p = 0; p < a.W; ++p) {
-                if (!row_picks_rank(a.ids, i, a.k, p, per)) continue;
-                const float4 b = back[((size_t)p * a.cap + i) * vec + v];
-                acc.x += b.x; acc.y += b.y; acc.z += b.z; acc.w += b.w;
-            }
-            if (shared) {
-                const float4 s = reinterpret_cast<const float4*>(shared)[(size_t)i * vec + v];
-                acc.x += s.x; acc.y += s.y; acc.z += s.z; acc.w += s.w;
-            }
-            reinterpret_cast<float4*>(out)[(size_t)i * vec + v] = acc;
-        }
-    }
-    if (threadIdx.x == 0) {
-        __threadfence();
-        if (atomicAdd(&ctl->c_total, 1u) == gridDim.x * gridDim.y - 1) {
-            ctl->c_total = 0;
-            ctl->combine_epoch = epoch;
-            __threadfence();
-        }
-    }
-}
-
 static int ep_common(EpArgs& a, const uint64_t* peers, void* local, int W, int rank, int cap, int H, int k, int E,
                      int B, const char* what) {
     EXL3_REQUIRE(peers && local && W >= 1 && W <= kEpMaxRanks && rank >= 0 && rank < W, EXL3_ERR_ARG,
@@ -293,9 +240,12 @@ static int ep_common(EpArgs& a, const uint64_t* peers, void* local, int W, int r
     return EXL3_OK;
 }
 
+// Chunks per peer: about two CTAs per SM over all peers, at most one per row, and W * chunks flag slots at most.
+// Depends only on (cap, W) and the GPU model, so every rank of a launch cuts its rows the same way.
 static int ep_chunks(int cap, int W) {
     int c = (2 * num_sms() + W - 1) / W;
     if (c > cap) c = cap;
+    if (c > kEpMaxSlots / W) c = kEpMaxSlots / W;
     return c < 1 ? 1 : c;
 }
 
@@ -321,7 +271,7 @@ int exl3_ep_recv_offsets(int W, int cap, int H, int topk, size_t* recv_x, size_t
 }
 
 int exl3_ep_buffer_create(size_t bytes, void** ptr, void* ipc_handle) {
-    EXL3_REQUIRE(ptr && ipc_handle && bytes >= 2048, EXL3_ERR_ARG, "exl3_ep_buffer_create: bad arguments");
+    EXL3_REQUIRE(ptr && ipc_handle && bytes >= kEpCtlBytes, EXL3_ERR_ARG, "exl3_ep_buffer_create: bad arguments");
     void* p = nullptr;
     cudaError_t e = cudaMalloc(&p, bytes);
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_ep_buffer_create: cudaMalloc(%zu): %s", bytes,
@@ -387,7 +337,8 @@ int exl3_ep_combine(const float* part, int topk, int E, int H, int W, int rank, 
                  "exl3_ep_combine: part must be 16-byte aligned");
     a.part = part;
     cudaError_t e = launch_pdl(k_ep_combine, dim3(ep_chunks(cap, W), W), dim3(kEpThreads), 0,
-                               static_cast<cudaStream_t>(stream), a);
+                               static_cast<cudaStream_t>(stream), a, static_cast<const float*>(nullptr),
+                               static_cast<float*>(nullptr));
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_ep_combine: launch failed: %s", cudaGetErrorString(e));
     return EXL3_OK;
 }
@@ -405,7 +356,7 @@ int exl3_ep_combine_reduce(const float* part, const int32_t* ids, int B, int top
                  EXL3_ERR_ARG, "exl3_ep_combine_reduce: out / shared must be 16-byte aligned, ids non-null");
     a.part = part;
     a.ids = ids;
-    cudaError_t e = launch_pdl(k_ep_combine_reduce, dim3(ep_chunks(cap, W), W), dim3(kEpThreads), 0,
+    cudaError_t e = launch_pdl(k_ep_combine, dim3(ep_chunks(cap, W), W), dim3(kEpThreads), 0,
                                static_cast<cudaStream_t>(stream), a, shared, out);
     EXL3_REQUIRE(e == cudaSuccess, EXL3_ERR_CUDA, "exl3_ep_combine_reduce: launch failed: %s",
                  cudaGetErrorString(e));
