@@ -870,13 +870,13 @@ RUNNERS = {"decode": run_decode, "prefill": run_prefill, "dense": run_dense}
 
 # DRAM bytes (read + write) per gate|up launch from the committed ncu capture
 # (profiles/k_gemv_moe_qwen_next_full.md), per workload; None where no capture was made.
-TRAFFIC_PER_LAUNCH: dict = {"qwen_next_decode": 31226624 + 86272}
+TRAFFIC_PER_LAUNCH: dict = {"qwen_next_decode": 31225856 + 102144}
 # The decode's own roofline for the same launch, from the same capture: the kernel is bound by the integer decode of
 # the trellis, not by HBM (warp instructions per 16x16 tile, issue and pipe utilisation, and the ceiling that the
 # IMUL + IDP4A pair per weight sets on the half-rate pipe at this K).
 DECODE_ALU: dict = {"qwen_next_decode": {
-    "warp_instructions_per_tile": 54.2, "issue_active": 0.596, "alu_pipe": 0.497,
-    "fma_pipe": 0.212, "smsp_active_of_elapsed": round(48650.6 / 65582.2, 3), "K": 3,
+    "warp_instructions_per_tile": 54.3, "issue_active": 0.626, "alu_pipe": 0.529,
+    "fma_pipe": 0.234, "smsp_active_of_elapsed": round(46355.5 / 63015.8, 3), "K": 3,
     "hbm_frac_ceiling_of_mul1_pipe": 0.53}}
 
 
