@@ -44,6 +44,9 @@ int num_sms();
 // Device address of the library's sticky status word on the current device (see exl3_device_status).
 int* device_status_ptr();
 
+// The decode GEMVs' finisher wait for a split unit's other partials (exl3_set_finisher_wait), in ns.
+uint64_t finisher_wait_ns();
+
 // ------------------------------------------------------------------------------------------------ device helpers
 
 constexpr uint32_t kMul1 = 0x83DCD12Du;

@@ -15,11 +15,13 @@
 // stages of each other. At the end of each segment the consumers park their accumulators in one of two shared-memory
 // slots and go on decoding; two epilogue warps sum them, reduce split units and run the epilogue. A CTA that covers a
 // whole unit finishes it on the spot; units shared by several CTAs are reduced through global memory: the other
-// contributors store their fp32 partials and count themselves, and the unit's first contributor, for which the unit
-// is the last segment of its range, sums all partials in CTA order (a fixed order: results do not depend on timing)
-// and runs the epilogue. Its bounded wait for the count almost never waits: the others have the unit as the first
-// segment of their ranges. Units split over more than 4 CTAs go through an atomic ticket instead (the contributor
-// that completes the count finishes). Every SM has work until the last k-block, whatever the number of units.
+// contributors store their fp32 partials and take an atomic ticket, and the unit's first contributor, for which the
+// unit is the last segment of its range, waits briefly for their count (they have the unit as the first segment of
+// their ranges, so it is usually complete) and sums all partials in CTA order (a fixed order: results do not depend
+// on timing). If the count does not complete within 20 us (exl3_set_finisher_wait) it publishes its own partial
+// and takes a ticket too, and the contributor that completes the count finishes: no CTA waits long for one that may
+// not be resident, so concurrent kernels cannot stall a launch. Units split over more than 4 CTAs always use the
+// ticket. Every SM has work until the last k-block, whatever the number of units.
 //
 // Activations arrive pre-rotated in "xf" order (prep kernels, or the gate|up epilogue for the down projection):
 // a = fp16(H(fp16(x*suh))/sqrt(128)) (exllamav3's roundings), stored per (row, 16-input tile-row) as 4 quads x 4 fp16
@@ -120,6 +122,7 @@ struct GemvArgs {
     float* partial;         // [2 gridDim.x][unit_floats] split-unit partial sums
     int* counters;          // [units] tickets, zero before the launch, left zero after it
     int* status;
+    uint64_t head_wait_ns;  // a split unit's finisher waits this long for the other partials (set at launch)
 };
 
 // Dynamic shared memory: red [2][kSub][unit_floats] fp32 (per sub-group accumulators of two segments in flight),
@@ -669,18 +672,55 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
 
     // ---------------- epilogue warps: sum the sub-groups, reduce split units, finish units ----------------
     // A unit split over n_c <= 4 CTAs is finished by its first contributor (the owner of its first k-block, for which
-    // the unit is the last segment of its range): the others store their partials and count themselves (a fence and
-    // an atomic add whose result nobody waits for), usually long before, since the unit is the first segment of their
-    // ranges; the finisher loads their partials into red[buf ^ 1] (no later segment of this CTA uses it) while its
-    // own consumers are still decoding, or, if they are not all in yet, waits for the count (bounded) once its own
-    // part is done. That wait is on CTAs that never wait themselves for this unit, all resident (one CTA per SM).
-    // Units split over more than 4 CTAs use a ticket instead: every contributor stores its partial and the one whose
-    // atomic completes the count finishes. Either way the partials are summed in CTA order, so the result does not
-    // depend on timing or on the path.
+    // the unit is the last segment of its range): the others store their partials and take a ticket (a fence and an
+    // atomic add whose result they read only at the end of the launch), usually long before, since the unit is the
+    // first segment of their ranges; the finisher loads their partials into red[buf ^ 1] (no later segment of this
+    // CTA uses it) while its own consumers are still decoding, or, if they are not all in yet, waits up to
+    // head_wait_ns (exl3_set_finisher_wait, 20 us by default) once its own part is done, and after that publishes
+    // its partial and takes a ticket as well; the contributor whose ticket completes the count then finishes (which
+    // the others' tickets cannot do while the first contributor holds back its own). Units split over more than 4
+    // CTAs always use the ticket. Every path sums the partials in CTA order, so the result does not depend on timing
+    // or on the path.
     const int ew = warp - 1 - kConsumerWarps;
     const int et = ew * 32 + lane;
     pdl_wait();                                               // tickets and outputs belong to this launch from here
     bool to = false;
+    // the partials of the unit's contributors summed in CTA order into rb (rows below Mi)
+    auto sum_slots = [&](long long a0, long long a1, int Mi, float* rb) {
+        int slots[4];                                         // partial slots of the first contributors, in order
+        int nc = 0;
+        for (long long c = owner_of(a0, T, G); nc < 4; c = next_owner(c, T, G)) {
+            slots[nc++] = (int)(range_start(c, T, G) < a0 ? 2 * c + 1 : 2 * c);   // started before a0: 2nd slot
+            if (range_start(c + 1, T, G) >= a1) break;
+        }
+        for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
+            if ((e / 32) % R >= Mi) continue;
+            float4 p[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                p[j] = j < nc ? __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)slots[j] * UF) + e)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) { acc.x += p[j].x; acc.y += p[j].y; acc.z += p[j].z; acc.w += p[j].w; }
+            if (nc == 4) {                                    // units split over more than 4 CTAs: the rest in order
+                long long c = owner_of(a0, T, G);
+                for (int j = 0; j < 4; ++j) c = next_owner(c, T, G);
+                for (;; c = next_owner(c, T, G)) {
+                    if (range_start(c, T, G) >= a1) break;
+                    const long long sl = range_start(c, T, G) < a0 ? 2 * c + 1 : 2 * c;
+                    const float4 q = __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)sl * UF) + e);
+                    acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
+                }
+            }
+            reinterpret_cast<float4*>(rb)[e] = acc;
+        }
+    };
+    // a published partial whose ticket is read at the end (at most one per CTA: its first segment); def_old is the
+    // ticket of thread et == 0, def_u and def_nc are set in every epilogue thread
+    bool has_def = false;
+    int def_old = -1, def_nc = 0;
+    long long def_u = 0;
     for (int i = 0; i < n_seg; ++i) {
         const long long u = u0 + i;
         const int lo = i == 0 ? (int)(r0 - u * KB) : 0;
@@ -746,44 +786,61 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
             }
         }
         bool finish = whole || head;
+        bool ticket = more || (!whole && !head && has_def);   // publish the partial, take a ticket and read it
+        const bool publish = !whole && !more && !head && !has_def;   // publish, take a ticket, read it at the end
         if (head && !ready) {
-            // the others are not all in yet: wait for the count (bounded), then add their partials in CTA order
+            // the others are not all in yet: wait a short while for the count, then add their partials in CTA
+            // order; if it does not complete (another kernel holds the SMs a contributor needs), publish this
+            // partial too and take a ticket like the others: the last of them finishes the unit
+            epilogue_sync();                                  // every thread has read flag[1] (ready) and rb
             if (et == 0) {
                 const uint64_t t0 = globaltimer_ns();
+                bool in = true;
                 while (ld_acquire_gpu(args.counters + u) != n_c - 1) {
-                    if (globaltimer_ns() - t0 > kWaitLimitNs) { to = true; break; }
+                    if (globaltimer_ns() - t0 > args.head_wait_ns) { in = false; break; }
                     __nanosleep(64);
                 }
+                flag[1] = in;
             }
             epilogue_sync();
-            for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
-                if ((e / 32) % R >= ui.Mi) continue;
-                float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-                long long c = ci;
+            if (flag[1]) {
+                for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
+                    if ((e / 32) % R >= ui.Mi) continue;
+                    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+                    long long c = ci;
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (j == 0) p = reinterpret_cast<const float4*>(rb)[e];
-                    else if (j < n_c) {
-                        c = next_owner(c, T, G);
-                        p = __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)(2 * c) * UF) + e);
+                    for (int j = 0; j < 4; ++j) {
+                        float4 p = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if (j == 0) p = reinterpret_cast<const float4*>(rb)[e];
+                        else if (j < n_c) {
+                            c = next_owner(c, T, G);
+                            p = __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)(2 * c) * UF) + e);
+                        }
+                        t.x += p.x; t.y += p.y; t.z += p.z; t.w += p.w;
                     }
-                    t.x += p.x; t.y += p.y; t.z += p.z; t.w += p.w;
+                    reinterpret_cast<float4*>(rb)[e] = t;
                 }
-                reinterpret_cast<float4*>(rb)[e] = t;
+            } else {
+                for (int e = et; e < UF / 4; e += kEpilogueWarps * 32)
+                    if ((e / 32) % R < ui.Mi) slot[e] = reinterpret_cast<const float4*>(rb)[e];
+                finish = false;
+                ticket = true;
             }
         }
-        if (head && et == 0) args.counters[u] = 0;           // every other contributor has counted: left zero
-        if (!whole && !more && !head) {
-            // publish this CTA's partial: the slot stores of both warps, then one fence and the count
-            epilogue_sync();
+        if (finish && head && et == 0) args.counters[u] = 0;  // every other contributor has counted: left zero
+        if (publish) {
+            epilogue_sync();                                  // both warps' slot stores, then one fence and the add
             if (et == 0) {
                 __threadfence();
-                atomicAdd(args.counters + u, 1);
+                def_old = atomicAdd(args.counters + u, 1);    // read by this thread only, at the end
             }
+            def_u = u;                                        // every epilogue thread: the unit and its count
+            def_nc = n_c;
+            has_def = true;
         }
-        if (more) {
-            // ticket: the last contributor of unit u sums every partial in CTA order
+        if (ticket) {
+            // the partial is in this CTA's slot: one fence, then the ticket; the contributor that completes the
+            // count sums every partial in CTA order
             __threadfence();
             epilogue_sync();
             if (et == 0) {
@@ -799,38 +856,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
             }
             epilogue_sync();
             finish = *flag != 0;
-            if (finish) {
-                // contributors in order: the owner of a0, then the owner after each range, up to the unit's end; a
-                // contributor that started before a0 keeps this unit's partial in its second slot
-                int slots[4];                                 // partial slots of the first contributors, in order
-                int nc = 0;
-                for (long long c = owner_of(a0, T, G); nc < 4; c = next_owner(c, T, G)) {
-                    slots[nc++] = (int)(range_start(c, T, G) < a0 ? 2 * c + 1 : 2 * c);
-                    if (range_start(c + 1, T, G) >= a1) break;
-                }
-                for (int e = et; e < UF / 4; e += kEpilogueWarps * 32) {
-                    if ((e / 32) % R >= ui.Mi) continue;
-                    float4 p[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j)
-                        p[j] = j < nc ? __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)slots[j] * UF) + e)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) { acc.x += p[j].x; acc.y += p[j].y; acc.z += p[j].z; acc.w += p[j].w; }
-                    if (nc == 4) {                            // units split over more than 4 CTAs: the rest in order
-                        long long c = owner_of(a0, T, G);
-                        for (int j = 0; j < 4; ++j) c = next_owner(c, T, G);
-                        for (;; c = next_owner(c, T, G)) {
-                            if (range_start(c, T, G) >= a1) break;
-                            const long long sl = range_start(c, T, G) < a0 ? 2 * c + 1 : 2 * c;
-                            const float4 q = __ldcg(reinterpret_cast<const float4*>(args.partial + (size_t)sl * UF) + e);
-                            acc.x += q.x; acc.y += q.y; acc.z += q.z; acc.w += q.w;
-                        }
-                    }
-                    reinterpret_cast<float4*>(rb)[e] = acc;
-                }
-            }
+            if (finish) sum_slots(a0, a1, ui.Mi, rb);
         }
         if (finish) {
             epilogue_sync();
@@ -838,6 +864,27 @@ __global__ void __launch_bounds__(kGemvThreads, 1) k_gemv(const GemvArgs args) {
         }
         epilogue_sync();                                      // the flags and red[buf] are read: release them
         if (lane == 0) mbar_arrive(&acc_empty[buf]);
+    }
+    if (has_def) {
+        // the first segment's ticket: its add completed the count only if the unit's first contributor gave up
+        // waiting and counted itself; then this CTA finishes that unit (red[] is free: every segment is done)
+        if (et == 0) {
+            const int last = def_old == def_nc - 1;
+            if (last) {
+                args.counters[def_u] = 0;                     // left zero for the next launch
+                __threadfence();
+            }
+            flag[0] = last;
+        }
+        epilogue_sync();
+        if (flag[0]) {
+            const int i0 = (int)(def_u - u0);
+            const UnitInfo<EPI> ui = i0 < kMaxSeg ? descs[i0] : unit_info<EPI>(args, (int)def_u, NB, KB);
+            const EpiOperands<EPI> op = epi_operands<EPI>(args, ui, ew, lane);
+            sum_slots(def_u * KB, def_u * KB + KB, ui.Mi, red);
+            epilogue_sync();
+            unit_epilogue<EPI, RG>(args, ui, red, ew, lane, op);
+        }
     }
     if (to) report(args.status, EXL3_ERR_TIMEOUT);
 }
@@ -931,6 +978,7 @@ int launch_gemv(GemvArgs a, const GemvPlan& pl, cudaStream_t st, const char* wha
         }
         configured[dev] = 1;
     }
+    a.head_wait_ns = finisher_wait_ns();
     cudaError_t e = launch_pdl(kern, dim3(pl.ctas), dim3(kGemvThreads), pl.smem, st, a);
     if (e != cudaSuccess) {
         set_error("%s: launch failed: %s", what, cudaGetErrorString(e));

@@ -3,6 +3,8 @@
 
 #include <mutex>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace exl3 {
@@ -55,9 +57,19 @@ static __global__ void k_wait_probe(uint64_t limit_ns, int* status) {
     if (!mbar_wait(&bar, 0, limit_ns)) report(status, EXL3_ERR_TIMEOUT);
 }
 
+static std::atomic<uint64_t> g_finisher_wait_ns{20000};
+uint64_t finisher_wait_ns() { return g_finisher_wait_ns.load(std::memory_order_relaxed); }
+
 }  // namespace exl3
 
 extern "C" {
+
+int exl3_set_finisher_wait(uint64_t wait_ns) {
+    EXL3_REQUIRE(wait_ns <= exl3::kWaitLimitNs, EXL3_ERR_ARG, "exl3_set_finisher_wait: %llu ns above %llu",
+                 (unsigned long long)wait_ns, (unsigned long long)exl3::kWaitLimitNs);
+    exl3::g_finisher_wait_ns.store(wait_ns, std::memory_order_relaxed);
+    return EXL3_OK;
+}
 
 int exl3_wait_probe(uint64_t limit_ns, void* stream) {
     EXL3_REQUIRE(limit_ns > 0 && limit_ns <= exl3::kWaitLimitNs, EXL3_ERR_ARG,

@@ -33,6 +33,7 @@ _PROTOS = [
     ("exl3_last_error", C.c_char_p, []),
     ("exl3_device_status", i32, [i32]),
     ("exl3_wait_probe", i32, [C.c_uint64, vp]),
+    ("exl3_set_finisher_wait", i32, [C.c_uint64]),
     ("exl3_dequant", i32, [vp, i32, i32, i32, i32, i32, i32, vp, i32, vp]),
     ("exl3_had_r_128", i32, [vp, vp, i32, i32, i32, vp, vp, f32, vp]),
     ("exl3_pack", i32, [vp, i32, i32, i32, vp, vp]),

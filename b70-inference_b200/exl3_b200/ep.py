@@ -27,6 +27,7 @@ batches may differ between ranks; every rank makes the same calls in the same or
 from __future__ import annotations
 
 import ctypes as C
+import os
 from typing import Callable
 
 import torch
@@ -143,6 +144,8 @@ class ExpertParallelMoE:
         self.capacity = capacity
         self.exchange = exchange
         self.fused_reduce = True          # p2p: combine and reduce in one launch (exl3_ep_combine_reduce)
+        # p2p: the shared expert on a side stream, overlapping the exchange (EXL3_EP_SHARED_SIDE_STREAM=0: in line)
+        self.shared_side_stream = os.environ.get("EXL3_EP_SHARED_SIDE_STREAM", "1") != "0"
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.E, self.H, self.topk = E, H, topk
@@ -158,11 +161,20 @@ class ExpertParallelMoE:
         if shared_fn is None and table is not None and table.shared is not None:
             from .moe import moe_forward, moe_prefill
 
-            def shared_fn(x):
+            def shared_fn(x, workspace_key=None):
                 none = torch.full((x.shape[0], 1), -1, dtype=torch.int32, device=x.device)
                 zero = torch.zeros((x.shape[0], 1), dtype=torch.float32, device=x.device)
-                fn = moe_prefill if x.shape[0] >= PREFILL_MIN_PAIRS // 8 else moe_forward
-                return fn(x, none, zero, self.table, self.act_limit, torch.float32)
+                prefill = x.shape[0] >= PREFILL_MIN_PAIRS // 8
+                fn = moe_prefill if prefill else moe_forward
+                ws = None
+                if workspace_key is not None:                # a call that overlaps the routed experts' own
+                    from . import _lib as L
+                    lib = L.lib()
+                    size = (lib.exl3_moe_prefill_workspace_size if prefill else lib.exl3_moe_workspace_size)(
+                        x.shape[0], 1, self.table.E, self.H, self.table.I, 1)
+                    ws = L.workspace(x.device, size, workspace_key)
+                return fn(x, none, zero, self.table, self.act_limit, torch.float32, workspace=ws)
+            shared_fn.own_workspace = True
         self.local_fn = local_fn
         self.shared_fn = shared_fn
 
@@ -226,6 +238,16 @@ class ExpertParallelMoE:
             return out
         return res
 
+    _SIDE: dict = {}
+
+    @classmethod
+    def _side_stream(cls, device) -> torch.cuda.Stream:
+        """One side stream per device for the shared expert (reused across layers and calls)."""
+        key = str(device)
+        if key not in cls._SIDE:
+            cls._SIDE[key] = torch.cuda.Stream(device=device)
+        return cls._SIDE[key]
+
     def _forward_p2p(self, x: torch.Tensor, ids: torch.Tensor, w: torch.Tensor, out=None) -> torch.Tensor:
         """dispatch / local experts / combine / reduce on this package's peer-memory kernels."""
         from . import _lib as L
@@ -238,6 +260,17 @@ class ExpertParallelMoE:
         xc = xc.contiguous()
         idc = ids.to(torch.int32).contiguous()
         wc = w.to(torch.float32).contiguous()
+        # the shared expert of this rank's own rows needs nothing from the peers: on a side stream (its own
+        # workspace), it overlaps the exchange's waits and the routed experts
+        shared = None
+        side = None
+        if (self.shared_fn is not None and self.fused_reduce and self.shared_side_stream
+                and getattr(self.shared_fn, "own_workspace", False)):
+            cur = torch.cuda.current_stream(x.device)
+            side = self._side_stream(x.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                shared = self.shared_fn(xc, workspace_key="moe_ep_shared").contiguous()
         L.check(lib.exl3_ep_dispatch(xc.data_ptr(), L.dtype_code(xc.dtype), xc.stride(0), B, idc.data_ptr(),
                                      wc.data_ptr(), k, self.E, H, W, self.rank, cap, ex.peers.data_ptr(), ex.ptr, st),
                 "exl3_ep_dispatch")
@@ -247,7 +280,10 @@ class ExpertParallelMoE:
         if out is None or out.dtype != torch.float32 or not out.is_contiguous():
             out = torch.empty((B, H), dtype=torch.float32, device=x.device)
         if self.fused_reduce:
-            shared = self.shared_fn(xc).contiguous() if self.shared_fn is not None else None
+            if side is not None:
+                torch.cuda.current_stream(x.device).wait_stream(side)
+            elif self.shared_fn is not None:
+                shared = self.shared_fn(xc).contiguous()
             L.check(lib.exl3_ep_combine_reduce(part.data_ptr(), idc.data_ptr(), B, k, self.E, H, W, self.rank, cap,
                                                L.ptr(shared), ex.peers.data_ptr(), ex.ptr, out.data_ptr(), st),
                     "exl3_ep_combine_reduce")

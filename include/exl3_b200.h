@@ -69,6 +69,11 @@ EXL3_API int exl3_device_status(int reset);
  * usable. Every kernel's waits (TMA stages, accumulator hand-offs, tensor-memory stages) use the same wait with the
  * 100 ms limit. No reference counterpart: the reference's SYCL kernels do not wait on one another. */
 EXL3_API int exl3_wait_probe(uint64_t limit_ns, void* stream);
+/* How long the decode GEMVs' finisher of a unit split over CTAs waits for the other contributors' partials before it
+ * hands the unit to whichever contributor completes the count (0 <= wait_ns <= 100 ms; default 20 us). Results are
+ * the same bits for any value (the partials are summed in CTA order on every path); 0 exercises the hand-off path
+ * (tests). Applies to launches made after the call, on every device. No reference counterpart. */
+EXL3_API int exl3_set_finisher_wait(uint64_t wait_ns);
 
 /* ---- dequantisation ----
  * W_hat[:, n0 : n0 + n_slice] -> w (fp16 [k][n_slice], row stride ldw elements), Hadamard domain, no scales.

@@ -138,6 +138,30 @@ def test_gemv_cta_counts_are_consistent(groups, M):
     assert torch.equal(y, y2), "fixed-order split-unit reduction must be deterministic"
 
 
+@pytest.mark.parametrize("groups", [3, 7, 64, 0])
+def test_gemv_finisher_hand_off_gives_the_same_bits(groups):
+    """Split units finished by the ticket hand-off (finisher wait 0: the first contributor never waits for the
+    others) give bit for bit the result of the default path, for the linear and the MoE decode GEMVs."""
+    rng = np.random.default_rng(78)
+    k, n, K, M = 1024, 384, 3, 5
+    tr, suh, svh = rand_linear(rng, k, n, K)
+    x = to_dev(rng.standard_normal((M, k)).astype(np.float16))
+    pk = ops.pack(to_dev(tr), K)
+    outs = []
+    for wait in (20000, 0):
+        assert L.lib().exl3_set_finisher_wait(wait) == 0
+        try:
+            y = torch.full((M, n), float("nan"), dtype=torch.float32, device=DEV)
+            ops.exl3_gemv(x, pk, to_dev(suh), to_dev(svh), K, y, n_ctas=groups)
+            torch.cuda.synchronize()
+            outs.append(y)
+        finally:
+            L.lib().exl3_set_finisher_wait(20000)
+    assert torch.equal(outs[0], outs[1])
+    assert_close(outs[1].cpu().numpy(), O.exl3_linear(x.cpu().numpy(), tr, suh, svh, K, np.float32), what="hand-off")
+    assert L.lib().exl3_device_status(0) == 0
+
+
 def test_gemv_bf16_input_and_output():
     rng = np.random.default_rng(9)
     k, n, K, M = 256, 256, 4, 2

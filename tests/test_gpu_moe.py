@@ -291,6 +291,15 @@ def test_moe_decode_matches_oracle(M, shared):
     for groups in (1, 3, 11):
         og = moe.moe_forward(to_dev(x), to_dev(ids), to_dev(w), table, Lc, n_ctas=groups, workspace=poisoned(need))
         assert_close(og.cpu().numpy(), ref, what=f"moe M={M} ctas={groups}")
+        # split units handed to the ticket (finisher wait 0): the same bits
+        assert L.lib().exl3_set_finisher_wait(0) == 0
+        try:
+            oh = moe.moe_forward(to_dev(x), to_dev(ids), to_dev(w), table, Lc, n_ctas=groups,
+                                 workspace=poisoned(need))
+            torch.cuda.synchronize()
+        finally:
+            L.lib().exl3_set_finisher_wait(20000)
+        assert torch.equal(og, oh), f"moe M={M} ctas={groups}: hand-off path differs"
 
 
 def test_moe_decode_no_clamp_and_bf16_input():

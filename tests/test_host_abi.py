@@ -46,6 +46,10 @@ def test_argument_validation_returns_status_codes():
     assert gemv(k=100) == L.EXL3_ERR_ARG
     # too many rows per call (16 at most)
     assert gemv(M=17) == L.EXL3_ERR_ARG
+    # the split-unit finisher wait: 0 .. 100 ms (host-side setting, no device involved)
+    assert lib.exl3_set_finisher_wait(100_000_001) == L.EXL3_ERR_ARG
+    assert lib.exl3_set_finisher_wait(0) == L.EXL3_OK
+    assert lib.exl3_set_finisher_wait(20000) == L.EXL3_OK
     # misaligned packed weights
     assert gemv(packed=18) == L.EXL3_ERR_ARG
     # workspace missing or too small
