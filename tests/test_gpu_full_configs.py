@@ -8,8 +8,8 @@
 
 Routed ids are compared bit for bit with the oracle's router. Layer outputs are compared with tests/torch_ref.py:
 the oracle's rounding points in torch on the bit-exact dequantised weights (every token), which is itself pinned to
-the numpy oracle on the same shapes (test_torch_ref_matches_oracle). Measured errors are appended to
-gpurun_out/parity_errors.jsonl when that folder exists."""
+the numpy oracle on the same shapes (test_torch_ref_matches_oracle). Measured errors are appended, one JSON object
+per line, to the file named by $EXL3_PARITY_LOG when it is set."""
 import json
 import os
 
@@ -25,7 +25,7 @@ from tests.tolerance import assert_close
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
-OUT = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "gpurun_out")
+PARITY_LOG = os.environ.get("EXL3_PARITY_LOG")
 
 
 @pytest.fixture(autouse=True)
@@ -43,8 +43,8 @@ def record(what, out, ref):
     rel = float((o - r).norm() / max(float(r.norm()), 1e-30))
     mx = float((o - r).abs().max())
     rms = float(r.pow(2).mean().sqrt())
-    if os.path.isdir(OUT):
-        with open(os.path.join(OUT, "parity_errors.jsonl"), "a") as f:
+    if PARITY_LOG:
+        with open(PARITY_LOG, "a") as f:
             f.write(json.dumps({"what": what, "rel_l2": rel, "max_abs": mx, "ref_rms": rms}) + "\n")
     return rel, mx, rms
 
