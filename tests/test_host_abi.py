@@ -25,6 +25,27 @@ def test_library_exports_every_declared_symbol():
     assert sorted(L.exported_symbols()) == decl
 
 
+def declared_arities():
+    """Parameter count of every EXL3_API declaration in the header (void parameter lists count 0)."""
+    src = open(os.path.join(ROOT, "include", "exl3_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    out = {}
+    for m in re.finditer(r"EXL3_API\s+[\w\s\*]*?\b(exl3_\w+)\s*\(([^)]*)\)\s*;", src):
+        params = " ".join(m.group(2).split())
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_prototypes_match_the_header():
+    """Every ctypes prototype of the Python mirror has the header's number of parameters."""
+    ar = declared_arities()
+    assert set(ar) == set(declared_symbols())
+    assert {n for n, _, _ in L._PROTOS} == set(ar), "every declared entry point has a prototype"
+    for name, _, args in L._PROTOS:
+        assert name in ar, name
+        assert len(args) == ar[name], (name, len(args), ar[name])
+
+
 def test_version_and_error_text():
     assert L.lib().exl3_version() >= 100
     assert isinstance(L.lib().exl3_last_error(), bytes)
